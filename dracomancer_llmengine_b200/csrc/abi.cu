@@ -1,0 +1,1098 @@
+// C ABI of the B200 MoE FFN library: the reference engine's MoE entry points (same names,
+// signatures and argument meaning) plus draco_b200_* extensions, over the kernels of
+// route.cu / gemv.cu / q8k.cu.
+//
+// Host side: one context per CUDA device (stream, weight registry, workspace arena), a
+// process-wide mutex (the reference's callers are single-threaded too), thread-local error
+// text.  Weights arrive as the caller's addresses; host ranges are copied to device memory
+// once, on first use, and found again by address on later calls.
+#include "../../include/draco_moe_b200.h"
+#include "kernels.cuh"
+
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+using namespace draco;
+
+extern "C" {
+double m6_prof_t[24];
+long m6_prof_n[24];
+}
+
+namespace {
+
+thread_local std::string g_err;
+std::mutex g_mu;
+int g_act_mode = 0;
+int g_moe_chunk = 64;
+long g_launches = 0;          // kernels this library launched (all devices)
+
+// Optional per-phase device timing: CUDA events recorded around each phase on the launching
+// stream, resolved when read.
+enum Phase { kRoute = 0, kDispatch, kGateUp, kDown, kShared, kCombine, kPhases };
+bool g_prof = false;
+struct PendingEv {
+    int phase;
+    cudaEvent_t a, b;
+};
+std::vector<PendingEv> g_pending;
+std::vector<cudaEvent_t> g_ev_pool;
+double g_phase_ms[kPhases];
+long g_phase_n[kPhases];
+
+cudaEvent_t ev_get() {
+    if (!g_ev_pool.empty()) {
+        cudaEvent_t e = g_ev_pool.back();
+        g_ev_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+struct PhaseScope {
+    int phase;
+    cudaStream_t s;
+    cudaEvent_t a = nullptr;
+    PhaseScope(int p, cudaStream_t st) : phase(p), s(st) {
+        if (g_prof) {
+            a = ev_get();
+            cudaEventRecord(a, s);
+        }
+    }
+    ~PhaseScope() {
+        if (g_prof && a) {
+            cudaEvent_t b = ev_get();
+            cudaEventRecord(b, s);
+            g_pending.push_back(PendingEv{phase, a, b});
+        }
+    }
+};
+
+void resolve_prof() {
+    for (auto& p : g_pending) {
+        cudaEventSynchronize(p.b);
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, p.a, p.b) == cudaSuccess) {
+            g_phase_ms[p.phase] += ms;
+            g_phase_n[p.phase]++;
+        }
+        g_ev_pool.push_back(p.a);
+        g_ev_pool.push_back(p.b);
+    }
+    g_pending.clear();
+}
+
+void set_err(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+}
+
+bool env_flag(const char* name) {
+    const char* v = getenv(name);
+    return v && v[0] && strcmp(v, "0") != 0;
+}
+
+// Report an error of a `void` entry point: stderr, NaN output, optional abort.
+void fail_void(const char* fn, float* out, size_t n) {
+    fprintf(stderr, "[draco_moe_b200] %s: %s\n", fn, g_err.c_str());
+    if (env_flag("DRACO_B200_STRICT")) abort();
+    if (out)
+        for (size_t i = 0; i < n; i++) out[i] = NAN;
+}
+
+#define CK(call)                                                                         \
+    do {                                                                                 \
+        cudaError_t e_ = (call);                                                         \
+        if (e_ != cudaSuccess) {                                                         \
+            set_err("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+            return -3;                                                                   \
+        }                                                                                \
+    } while (0)
+
+double now_s() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct Region {
+    uintptr_t host;
+    size_t bytes;
+    void* dev;
+};
+
+struct Table {
+    std::vector<uint64_t> ptrs;
+    std::vector<int> codes;
+    int n = 0;
+    const uint8_t** d_w = nullptr;   // device array of 3n device addresses
+    int cg = 0, cu = 0, cd = 0;
+};
+
+struct Ctx {
+    int dev = -1;
+    cudaStream_t stream = nullptr;
+    std::map<uintptr_t, Region> regions;
+    size_t reg_bytes = 0;
+    std::map<std::tuple<uintptr_t, int, int, int, int>, Table> tables;
+    char* ws = nullptr;
+    size_t ws_cap = 0;
+    int* d_consts = nullptr;     // [0] = 0, [1] = 1, [2..3] = {0, T} (dense single-expert lists)
+    int* h_consts = nullptr;     // pinned mirror of d_consts[2..3]
+};
+
+Ctx* g_ctx[64];
+
+bool is_device_ptr(const void* p) {
+    if (!p) return false;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+Ctx* get_ctx() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        set_err("no CUDA device available");
+        return nullptr;
+    }
+    if (dev < 0 || dev >= 64) {
+        set_err("device index %d out of range", dev);
+        return nullptr;
+    }
+    if (!g_ctx[dev]) {
+        Ctx* c = new Ctx();
+        c->dev = dev;
+        if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaMalloc(&c->d_consts, 4 * sizeof(int)) != cudaSuccess ||
+            cudaMallocHost(&c->h_consts, 4 * sizeof(int)) != cudaSuccess) {
+            set_err("CUDA context set-up failed: %s", cudaGetErrorString(cudaGetLastError()));
+            delete c;
+            return nullptr;
+        }
+        const int init[4] = {0, 1, 0, 0};
+        cudaMemcpy(c->d_consts, init, sizeof init, cudaMemcpyHostToDevice);
+        g_ctx[dev] = c;
+    }
+    return g_ctx[dev];
+}
+
+// device address of host range [host, host+bytes): existing copy, or a new one
+const uint8_t* dev_range(Ctx* c, const void* host, size_t bytes) {
+    if (!host || bytes == 0) {
+        set_err("null or empty weight range");
+        return nullptr;
+    }
+    const uintptr_t h = (uintptr_t)host;
+    auto it = c->regions.upper_bound(h);
+    while (it != c->regions.begin()) {
+        --it;
+        const Region& r = it->second;
+        if (r.host <= h && h + bytes <= r.host + r.bytes) return (const uint8_t*)r.dev + (h - r.host);
+        if (r.host + (size_t(1) << 40) < h) break;   // regions are never that large
+    }
+    if (is_device_ptr(host)) return (const uint8_t*)host;
+    void* d = nullptr;
+    if (cudaMalloc(&d, bytes) != cudaSuccess) {
+        set_err("cudaMalloc of %zu weight bytes failed: %s", bytes, cudaGetErrorString(cudaGetLastError()));
+        return nullptr;
+    }
+    if (cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        set_err("weight upload failed: %s", cudaGetErrorString(cudaGetLastError()));
+        cudaFree(d);
+        return nullptr;
+    }
+    c->regions[h] = Region{h, bytes, d};
+    c->reg_bytes += bytes;
+    return (const uint8_t*)d;
+}
+
+// activations/outputs: device pointers are used in place, host ones staged
+bool dev_kind(const void* p) { return is_device_ptr(p); }
+
+// Resolve a [3n] (gate, up, down) pointer table to device addresses; cached per table
+// address and validated against its current contents on every call.
+Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inter, int n_in, int n_out) {
+    auto key = std::make_tuple((uintptr_t)ptrs, n, inter, n_in, n_out);
+    auto it = c->tables.find(key);
+    if (it != c->tables.end()) {
+        Table& t = it->second;
+        if (memcmp(t.ptrs.data(), ptrs, sizeof(uint64_t) * 3 * n) == 0 &&
+            memcmp(t.codes.data(), codes, sizeof(int) * 3 * n) == 0)
+            return &t;
+        cudaFree((void*)t.d_w);
+        c->tables.erase(it);
+    }
+    Table t;
+    t.n = n;
+    t.ptrs.assign(ptrs, ptrs + 3 * n);
+    t.codes.assign(codes, codes + 3 * n);
+    t.cg = codes[0];
+    t.cu = codes[1];
+    t.cd = codes[2];
+    for (int e = 0; e < n; e++)
+        if (codes[3 * e] != t.cg || codes[3 * e + 1] != t.cu || codes[3 * e + 2] != t.cd) {
+            set_err("expert %d has formats (%d,%d,%d) != expert 0 (%d,%d,%d); mixed formats unsupported", e,
+                    codes[3 * e], codes[3 * e + 1], codes[3 * e + 2], t.cg, t.cu, t.cd);
+            return nullptr;
+        }
+    for (int k = 0; k < 3; k++)
+        if (!code_supported(codes[k])) {
+            set_err("unsupported weight format code %d", codes[k]);
+            return nullptr;
+        }
+    if (n_in % block_values(t.cg) || n_in % block_values(t.cu) || inter % block_values(t.cd)) {
+        set_err("row lengths (n_in %d, inter %d) not a multiple of the block size", n_in, inter);
+        return nullptr;
+    }
+    if ((t.cg != DRACO_CODE_Q8_0 && n_in % 256) || (t.cd != DRACO_CODE_Q8_0 && inter % 256)) {
+        set_err("K-quant rows need multiples of 256 values");
+        return nullptr;
+    }
+    const size_t mat[3] = {(size_t)inter * row_bytes(t.cg, n_in), (size_t)inter * row_bytes(t.cu, n_in),
+                           (size_t)n_out * row_bytes(t.cd, inter)};
+    std::vector<uint64_t> dptr(3 * n);
+    for (int k = 0; k < 3; k++) {
+        // stacked experts base + e*per (the GGUF layout) are copied as one range
+        bool stacked = n > 1;
+        const uint64_t base = ptrs[k];
+        const uint64_t per = n > 1 ? ptrs[3 + k] - base : 0;
+        if (n > 1 && (ptrs[3 + k] <= base || per < mat[k])) stacked = false;
+        for (int e = 2; stacked && e < n; e++)
+            if (ptrs[3 * e + k] != base + per * (uint64_t)e) stacked = false;
+        if (stacked) {
+            const uint8_t* d = dev_range(c, (const void*)(uintptr_t)base, per * (n - 1) + mat[k]);
+            if (!d) return nullptr;
+            for (int e = 0; e < n; e++) dptr[3 * e + k] = (uint64_t)(uintptr_t)(d + per * e);
+        } else {
+            for (int e = 0; e < n; e++) {
+                const uint8_t* d = dev_range(c, (const void*)(uintptr_t)ptrs[3 * e + k], mat[k]);
+                if (!d) return nullptr;
+                dptr[3 * e + k] = (uint64_t)(uintptr_t)d;
+            }
+        }
+    }
+    for (int e = 0; e < 3 * n; e++)
+        if (dptr[e] % 2 || ((e % 3 != 2 ? t.cg : t.cd) == DRACO_CODE_Q4_K && dptr[e] % 16)) {
+            set_err("weight address 0x%llx misaligned for its format", (unsigned long long)dptr[e]);
+            return nullptr;
+        }
+    if (cudaMalloc((void**)&t.d_w, sizeof(uint64_t) * 3 * n) != cudaSuccess ||
+        cudaMemcpy((void*)t.d_w, dptr.data(), sizeof(uint64_t) * 3 * n, cudaMemcpyHostToDevice) != cudaSuccess) {
+        set_err("pointer table upload failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return nullptr;
+    }
+    auto res = c->tables.emplace(key, std::move(t));
+    return &res.first->second;
+}
+
+// workspace arena: carve aligned sub-buffers, growing the arena when needed
+struct Carver {
+    size_t off = 0;
+    template <typename T>
+    size_t take(size_t count) {
+        const size_t o = off;
+        off = align_up(off + sizeof(T) * (count ? count : 1), 256);
+        return o;
+    }
+};
+
+int ensure_ws(Ctx* c, size_t bytes) {
+    if (bytes <= c->ws_cap) return 0;
+    CK(cudaStreamSynchronize(c->stream));
+    if (c->ws) cudaFree(c->ws);
+    c->ws = nullptr;
+    c->ws_cap = 0;
+    const size_t cap = align_up(bytes + bytes / 2, 1 << 20);
+    CK(cudaMalloc((void**)&c->ws, cap));
+    c->ws_cap = cap;
+    return 0;
+}
+
+struct LayerArgs {
+    Table* tab = nullptr;
+    Table* sh = nullptr;         // shared expert (n = 1) or null
+    int sh_ff = 0;
+    int E = 0, K = 0, inter = 0, n_in = 0, n_out = 0;
+    RouterParams rp{};
+    const float* d_gi = nullptr; // router weights (device), null when routing is given
+};
+
+struct LayerBufs {
+    RouteBufs rb{};
+    float *x, *out, *act, *y, *act_sh, *y_sh;
+    int8_t* xq;
+    float* xd;
+    int16_t* xbs;
+};
+
+int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
+    const size_t n = (size_t)T * a.K;
+    Carver cv;
+    const size_t o_x = cv.take<float>((size_t)T * a.n_in), o_out = cv.take<float>((size_t)T * a.n_out);
+    const size_t o_lg = cv.take<float>((size_t)T * a.E), o_ord = cv.take<int>(n), o_w = cv.take<float>(n);
+    const size_t o_cnt = cv.take<int>(a.E), o_off = cv.take<int>(a.E + 1), o_il = cv.take<int>(n);
+    const size_t o_pos = cv.take<int>(n), o_act = cv.take<int>(a.E), o_na = cv.take<int>(1), o_err = cv.take<int>(1);
+    const size_t o_a = cv.take<float>(n * a.inter), o_y = cv.take<float>(n * a.n_out);
+    const size_t o_ash = cv.take<float>(a.sh ? (size_t)T * a.sh_ff : 0);
+    const size_t o_ysh = cv.take<float>(a.sh ? (size_t)T * a.n_out : 0);
+    const bool q8 = g_act_mode == 1;
+    const size_t o_xq = cv.take<int8_t>(q8 ? (size_t)T * a.n_in : 0);
+    const size_t o_xd = cv.take<float>(q8 ? (size_t)T * (a.n_in / 256) : 0);
+    const size_t o_xbs = cv.take<int16_t>(q8 ? (size_t)T * (a.n_in / 256) * 16 : 0);
+    if (int rc = ensure_ws(c, cv.off)) return rc;
+    char* w = c->ws;
+    b.x = (float*)(w + o_x);
+    b.out = (float*)(w + o_out);
+    b.rb.logits = (float*)(w + o_lg);
+    b.rb.order = (int*)(w + o_ord);
+    b.rb.wtop = (float*)(w + o_w);
+    b.rb.counts = (int*)(w + o_cnt);
+    b.rb.off = (int*)(w + o_off);
+    b.rb.ilist = (int*)(w + o_il);
+    b.rb.pos_of = (int*)(w + o_pos);
+    b.rb.active = (int*)(w + o_act);
+    b.rb.n_active = (int*)(w + o_na);
+    b.rb.err = (int*)(w + o_err);
+    b.act = (float*)(w + o_a);
+    b.y = (float*)(w + o_y);
+    b.act_sh = (float*)(w + o_ash);
+    b.y_sh = (float*)(w + o_ysh);
+    b.xq = (int8_t*)(w + o_xq);
+    b.xd = (float*)(w + o_xd);
+    b.xbs = (int16_t*)(w + o_xbs);
+    return 0;
+}
+
+// dense one-expert FFN over T token rows: act = silu(G x) * (U x), y = D act
+int dense_ffn(Ctx* c, Table* t, int T, const float* x, int ff, int n_in, int n_out, float* act, float* y,
+              cudaStream_t s) {
+    c->h_consts[2] = 0;
+    c->h_consts[3] = T;
+    CK(cudaMemcpyAsync(c->d_consts + 2, c->h_consts + 2, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
+    ExpertTable et{t->d_w};
+    {
+        PhaseScope ps(kShared, s);
+        launch_gateup_codes(et, t->cg, t->cu, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, nullptr, 1, x, ff,
+                            n_in, act, s);
+        launch_down_code(et, t->cd, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, act, ff, n_out, y, s);
+    }
+    g_launches += 2;
+    CK(cudaGetLastError());
+    // the pinned mirror is rewritten by the next call: finish this copy first
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+// Routed experts (+ shared) on device buffers.  Routing is computed when a.d_gi is set,
+// otherwise b.rb.order / b.rb.wtop already hold it.
+int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
+    RouteBufs& rb = b.rb;
+    CK(cudaMemsetAsync(rb.err, 0, sizeof(int), s));
+    if (a.d_gi) {
+        PhaseScope ps(kRoute, s);
+        launch_router_logits(b.x, a.d_gi, T, a.E, a.n_in, rb.logits, s);
+        launch_router_select(a.rp, T, rb, s);
+        g_launches += 2;
+    }
+    {
+        PhaseScope ps(kDispatch, s);
+        launch_dispatch(T, a.K, a.E, rb, s);
+        g_launches += 3;
+    }
+    ExpertTable et{a.tab->d_w};
+    const int na_max = std::min(a.E, T * a.K);
+    {
+        PhaseScope ps(kGateUp, s);
+        if (g_act_mode == 1 && a.tab->cg == a.tab->cu &&
+            (a.tab->cg == DRACO_CODE_Q4_K || a.tab->cg == DRACO_CODE_Q6_K) && a.n_in % 256 == 0) {
+            launch_q8k_quantize(b.x, T, a.n_in, b.xd, b.xq, b.xbs, s);
+            launch_gateup_q8k(et, a.tab->cg, rb.active, rb.n_active, na_max, rb.off, rb.ilist, a.K, b.xq, b.xd,
+                              b.xbs, a.inter, a.n_in, b.act, s);
+            g_launches += 2;
+        } else {
+            launch_gateup_codes(et, a.tab->cg, a.tab->cu, rb.active, rb.n_active, na_max, rb.off, rb.ilist, a.K,
+                                b.x, a.inter, a.n_in, b.act, s);
+            g_launches += 1;
+        }
+    }
+    {
+        PhaseScope ps(kDown, s);
+        launch_down_code(et, a.tab->cd, rb.active, rb.n_active, na_max, rb.off, b.act, a.inter, a.n_out, b.y, s);
+        g_launches += 1;
+    }
+    CK(cudaGetLastError());
+    if (a.sh) {
+        if (int rc = dense_ffn(c, a.sh, T, b.x, a.sh_ff, a.n_in, a.n_out, b.act_sh, b.y_sh, s)) return rc;
+    }
+    {
+        PhaseScope ps(kCombine, s);
+        launch_combine(b.y, rb.order, rb.wtop, rb.pos_of, T, a.K, a.E, a.n_out, a.sh ? b.y_sh : nullptr, b.out, s);
+        g_launches += 1;
+    }
+    CK(cudaGetLastError());
+    return 0;
+}
+
+int check_route_err(Ctx* c, LayerBufs& b, cudaStream_t s) {
+    int h_err = 0;
+    CK(cudaMemcpyAsync(&h_err, b.rb.err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    if (h_err) {
+        set_err("routing found fewer eligible experts than n_used (group limit or non-finite scores), code %d",
+                h_err);
+        return -2;
+    }
+    return 0;
+}
+
+int validate_shape(int n_exp, int n_used, int inter, int n_in, int n_out, int n_group, int n_group_used) {
+    if (n_exp <= 0 || n_exp > 512 || n_used <= 0 || n_used > 64 || n_used > n_exp || inter <= 0 || n_in <= 0 ||
+        n_out <= 0) {
+        set_err("unsupported shape n_exp=%d n_used=%d inter=%d n_in=%d n_out=%d (need 1<=n_used<=64, "
+                "n_used<=n_exp<=512)", n_exp, n_used, inter, n_in, n_out);
+        return -1;
+    }
+    if (n_group > 1 && (n_group > 64 || n_exp % n_group || n_group_used < 1 || n_group_used > n_group ||
+                        n_group_used * (n_exp / n_group) < n_used)) {
+        set_err("unsupported grouping n_group=%d n_group_used=%d for n_exp=%d n_used=%d", n_group, n_group_used,
+                n_exp, n_used);
+        return -1;
+    }
+    return 0;
+}
+
+// Synchronous single-call layer on host or device x/out (the reference entry points).
+int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, const float* gate_inp,
+               const float* probs_b, int scoring, int n_exp, int n_used, int n_group, int n_group_used, int norm_w,
+               float w_scale, int inter, int n_in, int n_out, const uint64_t* sh3, const int* shc3, int sh_ff,
+               float* out, int* order_out, float* wtop_out, cudaStream_t user_stream) {
+    if (int rc = validate_shape(n_exp, n_used, inter, n_in, n_out, scoring ? n_group : 1, n_group_used)) return rc;
+    if (T <= 0) return 0;
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    const double t0 = now_s();
+    LayerArgs a;
+    a.E = n_exp;
+    a.K = n_used;
+    a.inter = inter;
+    a.n_in = n_in;
+    a.n_out = n_out;
+    a.tab = get_table(c, ptrs, codes, n_exp, inter, n_in, n_out);
+    if (!a.tab) return -1;
+    if (sh3 && sh_ff > 0) {
+        a.sh = get_table(c, sh3, shc3, 1, sh_ff, n_in, n_out);
+        if (!a.sh) return -1;
+        a.sh_ff = sh_ff;
+    }
+    a.d_gi = (const float*)dev_range(c, gate_inp, sizeof(float) * (size_t)n_exp * n_in);
+    if (!a.d_gi) return -1;
+    a.rp.scoring = scoring;
+    a.rp.n_exp = n_exp;
+    a.rp.n_used = n_used;
+    a.rp.n_in = n_in;
+    a.rp.n_group = scoring ? n_group : 1;
+    a.rp.n_group_used = n_group_used;
+    a.rp.norm_w = norm_w;
+    a.rp.w_scale = w_scale;
+    a.rp.probs_b = nullptr;
+    if (scoring && probs_b) {
+        a.rp.probs_b = (const float*)dev_range(c, probs_b, sizeof(float) * n_exp);
+        if (!a.rp.probs_b) return -1;
+    }
+    LayerBufs b;
+    if (int rc = carve_layer(c, a, T, b)) return rc;
+    const bool dev_io = dev_kind(x);
+    cudaStream_t s = (dev_io && user_stream) ? user_stream : c->stream;
+    float* d_out = b.out;
+    if (dev_io) {
+        b.x = const_cast<float*>(x);
+        d_out = out;
+        b.out = out;
+    } else {
+        CK(cudaMemcpyAsync(b.x, x, sizeof(float) * (size_t)T * n_in, cudaMemcpyHostToDevice, s));
+    }
+    if (int rc = run_layer(c, a, T, b, s)) return rc;
+    if (dev_io) {
+        if (order_out) CK(cudaMemcpyAsync(order_out, b.rb.order, sizeof(int) * T * n_used, cudaMemcpyDeviceToDevice, s));
+        if (wtop_out) CK(cudaMemcpyAsync(wtop_out, b.rb.wtop, sizeof(float) * T * n_used, cudaMemcpyDeviceToDevice, s));
+        if (user_stream) return 0;
+    } else {
+        CK(cudaMemcpyAsync(out, d_out, sizeof(float) * (size_t)T * n_out, cudaMemcpyDeviceToHost, s));
+        if (order_out) CK(cudaMemcpyAsync(order_out, b.rb.order, sizeof(int) * T * n_used, cudaMemcpyDeviceToHost, s));
+        if (wtop_out) CK(cudaMemcpyAsync(wtop_out, b.rb.wtop, sizeof(float) * T * n_used, cudaMemcpyDeviceToHost, s));
+    }
+    if (int rc = check_route_err(c, b, s)) return rc;
+    m6_prof_t[23] += now_s() - t0;
+    m6_prof_n[23]++;
+    return 0;
+}
+
+template <typename T>
+int stage_in(Ctx* c, cudaStream_t s, size_t off, const T* h, size_t n) {
+    CK(cudaMemcpyAsync(c->ws + off, h, sizeof(T) * n, cudaMemcpyHostToDevice, s));
+    return 0;
+}
+
+}  // namespace
+
+// ===================================== Part 1 ==========================================
+extern "C" {
+
+void m6_granite_moe(const float* x0, const uint64_t* ptrs, const int* codes, const float* gate_inp, int n_exp,
+                    int n_used, int inter, int n_in, int n_out, float* scratch, float* out) {
+    (void)scratch;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (layer_call(x0, 1, ptrs, codes, gate_inp, nullptr, 0, n_exp, n_used, 1, 1, 1, 0.f, inter, n_in, n_out,
+                   nullptr, nullptr, 0, out, nullptr, nullptr, nullptr))
+        fail_void("m6_granite_moe", out, (size_t)(n_out > 0 ? n_out : 0));
+}
+
+void m6_bailing_moe(const float* x0, const uint64_t* ptrs, const int* codes, const float* gate_inp,
+                    const float* probs_b, int n_exp, int n_used, int n_group, int n_group_used, int norm_w,
+                    float w_scale, int inter, int n_in, int n_out, float* scratch, float* out) {
+    (void)scratch;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (layer_call(x0, 1, ptrs, codes, gate_inp, probs_b, 1, n_exp, n_used, n_group, n_group_used, norm_w, w_scale,
+                   inter, n_in, n_out, nullptr, nullptr, 0, out, nullptr, nullptr, nullptr))
+        fail_void("m6_bailing_moe", out, (size_t)(n_out > 0 ? n_out : 0));
+}
+
+void m6_moe_op(const float* xn, void* pv, float* out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const M6MoeP* p = (const M6MoeP*)pv;
+    const uint64_t sh3[3] = {(uint64_t)(uintptr_t)p->sh_g, (uint64_t)(uintptr_t)p->sh_u,
+                             (uint64_t)(uintptr_t)p->sh_d};
+    const int shc3[3] = {p->csg, p->csu, p->csd};
+    const bool has_sh = p->sh_g && p->sh_u && p->sh_d && p->sh_ff > 0;
+    if (layer_call(xn, 1, p->exp_ptrs, p->exp_codes, p->gate_inp, p->probs_b, 1, p->n_exp, p->n_used, p->n_group,
+                   p->n_group_used, p->norm_w, p->w_scale, p->inter, p->n_in, p->n_out, has_sh ? sh3 : nullptr,
+                   shc3, has_sh ? p->sh_ff : 0, out, nullptr, nullptr, nullptr))
+        fail_void("m6_moe_op", out, (size_t)(p->n_out > 0 ? p->n_out : 0));
+}
+
+static int shexp_impl(const float* x, const uint64_t* shp, const int* shc, float* sg, float* shg, float* out, int shi,
+                      int h) {
+    if (shc[3] != DRACO_CODE_F32) {
+        set_err("shared-expert gate row format %d unsupported (F32 = 9 expected)", shc[3]);
+        return -1;
+    }
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    Table* t = get_table(c, shp, shc, 1, shi, h, h);
+    if (!t) return -1;
+    const float* gw = (const float*)dev_range(c, (const void*)(uintptr_t)shp[3], sizeof(float) * h);
+    if (!gw) return -1;
+    Carver cv;
+    const size_t o_x = cv.take<float>(h), o_a = cv.take<float>(shi), o_y = cv.take<float>(h);
+    const size_t o_o = cv.take<float>(h), o_sg = cv.take<float>(1);
+    if (int rc = ensure_ws(c, cv.off)) return rc;
+    float* dx = (float*)(c->ws + o_x);
+    float* da = (float*)(c->ws + o_a);
+    float* dy = (float*)(c->ws + o_y);
+    float* dout = (float*)(c->ws + o_o);
+    float* dsg = (float*)(c->ws + o_sg);
+    cudaStream_t s = c->stream;
+    CK(cudaMemcpyAsync(dx, x, sizeof(float) * h, cudaMemcpyHostToDevice, s));
+    if (int rc = dense_ffn(c, t, 1, dx, shi, h, h, da, dy, s)) return rc;
+    launch_shexp_gate(dx, gw, h, dy, dsg, dout, 1, s);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(out, dout, sizeof(float) * h, cudaMemcpyDeviceToHost, s));
+    if (sg) CK(cudaMemcpyAsync(sg, dsg, sizeof(float), cudaMemcpyDeviceToHost, s));
+    if (shg) CK(cudaMemcpyAsync(shg, dy, sizeof(float) * h, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+void m6_granite_shexp(const float* x, const uint64_t* shp, const int* shc, float* sg, float* sh, float* shg,
+                      float* out, int shi, int h) {
+    (void)sh;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (shexp_impl(x, shp, shc, sg, shg, out, shi, h)) fail_void("m6_granite_shexp", out, (size_t)(h > 0 ? h : 0));
+}
+
+static int moe_tok_impl(const float* X, const int* order, const float* wtop, const uint64_t* ep, const int* ec, int T,
+                        int n_used, int inter, int n_in, int n_out, int n_exp, float* out) {
+    if (int rc = validate_shape(n_exp, n_used, inter, n_in, n_out, 1, 1)) return rc;
+    if (T <= 0) return 0;
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    const double t0 = now_s();
+    LayerArgs a;
+    a.E = n_exp;
+    a.K = n_used;
+    a.inter = inter;
+    a.n_in = n_in;
+    a.n_out = n_out;
+    a.tab = get_table(c, ep, ec, n_exp, inter, n_in, n_out);
+    if (!a.tab) return -1;
+    LayerBufs b;
+    if (int rc = carve_layer(c, a, T, b)) return rc;
+    cudaStream_t s = c->stream;
+    const size_t n = (size_t)T * n_used;
+    const bool dev_io = dev_kind(X);
+    if (dev_io) {
+        b.x = const_cast<float*>(X);
+        b.out = out;
+        CK(cudaMemcpyAsync(b.rb.order, order, sizeof(int) * n, cudaMemcpyDeviceToDevice, s));
+        CK(cudaMemcpyAsync(b.rb.wtop, wtop, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+    } else {
+        CK(cudaMemcpyAsync(b.x, X, sizeof(float) * (size_t)T * n_in, cudaMemcpyHostToDevice, s));
+        CK(cudaMemcpyAsync(b.rb.order, order, sizeof(int) * n, cudaMemcpyHostToDevice, s));
+        CK(cudaMemcpyAsync(b.rb.wtop, wtop, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+    }
+    if (int rc = run_layer(c, a, T, b, s)) return rc;
+    if (!dev_io) CK(cudaMemcpyAsync(out, b.out, sizeof(float) * (size_t)T * n_out, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    m6_prof_t[23] += now_s() - t0;
+    m6_prof_n[23]++;
+    return 0;
+}
+
+void m6_moe_tok(m6_dequant_fn DQ, m6_gemm_auto_fn GA, float* gwbuf, const float* X, const int* order,
+                const float* wtop, const uint64_t* ep, const int* ec, int T, int n_used, int inter, int n_in,
+                int n_out, int n_exp, float* out, float* work, int* iwork) {
+    (void)DQ;
+    (void)GA;
+    (void)gwbuf;
+    (void)work;
+    (void)iwork;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (moe_tok_impl(X, order, wtop, ep, ec, T, n_used, inter, n_in, n_out, n_exp, out))
+        fail_void("m6_moe_tok", dev_kind(out) ? nullptr : out, (size_t)(T > 0 && n_out > 0 ? (size_t)T * n_out : 0));
+}
+
+static int gemvn_impl(int code, const float* x, long x_stride, const uint8_t* W, const int* idx, long per,
+                      int n_out_e, int n_in, int n_exp, float* y) {
+    const int nb = n_in / 256;
+    if (nb <= 0 || n_in % 256 != 0 || (code == DRACO_CODE_Q4_K && nb > 256)) {
+        set_err("m5_gemvn: n_in %d must be a positive multiple of 256", n_in);
+        return -1;
+    }
+    if (n_exp <= 0 || n_out_e <= 0) return 0;
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    const size_t mb = (size_t)n_out_e * row_bytes(code, n_in);
+    const size_t xn = x_stride ? (size_t)x_stride * (n_exp - 1) + n_in : (size_t)n_in;
+    Carver cv;
+    const size_t o_x = cv.take<float>(xn), o_y = cv.take<float>((size_t)n_exp * n_out_e);
+    if (int rc = ensure_ws(c, cv.off)) return rc;
+    float* dx = (float*)(c->ws + o_x);
+    float* dy = (float*)(c->ws + o_y);
+    cudaStream_t s = c->stream;
+    CK(cudaMemcpyAsync(dx, x, sizeof(float) * xn, cudaMemcpyHostToDevice, s));
+    for (int e = 0; e < n_exp; e++) {
+        const uint8_t* dw = dev_range(c, W + (size_t)idx[e] * per, mb);
+        if (!dw) return -3;
+        launch_gemv_rows(code, dw, dx + (size_t)e * x_stride, n_in, 0, n_out_e, dy + (size_t)e * n_out_e, s);
+    }
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(y, dy, sizeof(float) * (size_t)n_exp * n_out_e, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int m5_gemvn_q4k(const float* x, long x_stride, const uint8_t* W, const int* idx, long per, int n_out_e, int n_in,
+                 int n_exp, float* y) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return gemvn_impl(DRACO_CODE_Q4_K, x, x_stride, W, idx, per, n_out_e, n_in, n_exp, y);
+}
+
+int m5_gemvn_q6k(const float* x, long x_stride, const uint8_t* W, const int* idx, long per, int n_out_e, int n_in,
+                 int n_exp, float* y) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return gemvn_impl(DRACO_CODE_Q6_K, x, x_stride, W, idx, per, n_out_e, n_in, n_exp, y);
+}
+
+int m5_scalar_supported(int code) { return code_supported(code) ? 1 : 0; }
+
+static int gemm_impl(int code, const float* X, const uint8_t* W, int T, int n_out, int n_in, float* Y, int o0,
+                     int o1) {
+    if (!code_supported(code)) {
+        set_err("unsupported format code %d", code);
+        return -1;
+    }
+    if (n_in % block_values(code) || (code != DRACO_CODE_Q8_0 && n_in % 256)) {
+        set_err("n_in %d not a multiple of the block size", n_in);
+        return -1;
+    }
+    if (T <= 0 || o1 <= o0) return 0;
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    const uint8_t* dw = dev_range(c, W, (size_t)n_out * row_bytes(code, n_in));
+    if (!dw) return -3;
+    Carver cv;
+    const size_t o_x = cv.take<float>((size_t)T * n_in), o_y = cv.take<float>((size_t)T * n_out);
+    if (int rc = ensure_ws(c, cv.off)) return rc;
+    float* dx = (float*)(c->ws + o_x);
+    float* dy = (float*)(c->ws + o_y);
+    cudaStream_t s = c->stream;
+    CK(cudaMemcpyAsync(dx, X, sizeof(float) * (size_t)T * n_in, cudaMemcpyHostToDevice, s));
+    if (T == 1) {
+        launch_gemv_rows(code, dw, dx, n_in, o0, o1, dy, s);
+        CK(cudaGetLastError());
+        CK(cudaMemcpyAsync(Y + o0, dy + o0, sizeof(float) * (o1 - o0), cudaMemcpyDeviceToHost, s));
+    } else {
+        launch_gemm_dense(code, dw, dx, T, n_out, n_in, dy, s);
+        CK(cudaGetLastError());
+        CK(cudaMemcpyAsync(Y, dy, sizeof(float) * (size_t)T * n_out, cudaMemcpyDeviceToHost, s));
+    }
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int m5_gemv(int code, const float* x, const uint8_t* W, int n_out, int n_in, float* y) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int rc = gemm_impl(code, x, W, 1, n_out, n_in, y, 0, n_out);
+    return rc == 0 ? 0 : -1;
+}
+
+int m5_gemv_range(int code, const float* x, const uint8_t* W, int n_out, int n_in, float* y, int o0, int o1) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (o0 < 0 || o1 > n_out) return -1;
+    const int rc = gemm_impl(code, x, W, 1, n_out, n_in, y, o0, o1);
+    return rc == 0 ? 0 : -1;
+}
+
+int m5_gemm(int code, const float* X, const uint8_t* W, int T, int n_out, int n_in, float* Y, float* wbuf) {
+    (void)wbuf;
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int rc = gemm_impl(code, X, W, T, n_out, n_in, Y, 0, n_out);
+    if (rc) fprintf(stderr, "[draco_moe_b200] m5_gemm: %s\n", g_err.c_str());
+    return 0;   // the reference's m5_gemm skips rows it cannot decode and returns 0
+}
+
+int m5_gemm_auto(int code, const float* X, const uint8_t* W, int c, int n_out, int n_in, float* Y) {
+    if (!code_supported(code)) return -1;
+    std::lock_guard<std::mutex> lk(g_mu);
+    return gemm_impl(code, X, W, c, n_out, n_in, Y, 0, n_out) == 0 ? 0 : -1;
+}
+
+#define DRACO_FUSED(FN, CODE)                                                                  \
+    void FN(const float* X, const uint8_t* W, int c, int n_out, int n_in, float* Y) {          \
+        std::lock_guard<std::mutex> lk(g_mu);                                                  \
+        if (gemm_impl(CODE, X, W, c, n_out, n_in, Y, 0, n_out))                                \
+            fail_void(#FN, Y, (size_t)(c > 0 && n_out > 0 ? (size_t)c * n_out : 0));            \
+    }
+DRACO_FUSED(m5_gemm_q80, DRACO_CODE_Q8_0)
+DRACO_FUSED(m5_gemm_q6k, DRACO_CODE_Q6_K)
+DRACO_FUSED(m5_gemm_q4k, DRACO_CODE_Q4_K)
+
+int m5_dequant_row(int code, const uint8_t* row, int n_in, float* out) {
+    if (!code_supported(code) || n_in % block_values(code) || (code != DRACO_CODE_Q8_0 && n_in % 256)) return -1;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx* c = get_ctx();
+    if (!c) return -1;
+    const size_t rb = row_bytes(code, n_in);
+    Carver cv;
+    const size_t o_w = cv.take<uint8_t>(rb), o_o = cv.take<float>(n_in);
+    if (ensure_ws(c, cv.off)) return -1;
+    cudaStream_t s = c->stream;
+    if (cudaMemcpyAsync(c->ws + o_w, row, rb, cudaMemcpyHostToDevice, s) != cudaSuccess) return -1;
+    launch_dequant(code, (const uint8_t*)(c->ws + o_w), 1, n_in, (float*)(c->ws + o_o), s);
+    if (cudaMemcpyAsync(out, c->ws + o_o, sizeof(float) * n_in, cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1;
+    return cudaStreamSynchronize(s) == cudaSuccess ? 0 : -1;
+}
+
+int m6_init_dl(const char* p012, const char* p3, const char* p4, const char* p56, const char* ps) {
+    (void)p012, (void)p3, (void)p4, (void)p56, (void)ps;
+    const char* mv = getenv("MOE_CHUNK");
+    if (mv) g_moe_chunk = atoi(mv);
+    return 0;
+}
+
+int m6_set_moe_chunk(int v) {
+    const int o = g_moe_chunk;
+    g_moe_chunk = v;
+    return o;
+}
+
+void m6_prof_reset(void) {
+    for (int i = 0; i < 24; i++) {
+        m6_prof_t[i] = 0;
+        m6_prof_n[i] = 0;
+    }
+}
+double m6_prof_get(int i) { return (i >= 0 && i < 24) ? m6_prof_t[i] : 0.0; }
+long m6_prof_cnt(int i) { return (i >= 0 && i < 24) ? m6_prof_n[i] : 0; }
+
+size_t m6_rowbytes(int code, int n_in) {
+    switch (code) {
+        case 0: return (size_t)(n_in / 32) * 34;
+        case 1: return (size_t)(n_in / 32) * 18;
+        case 2: return (size_t)(n_in / 256) * 110;
+        case 3: return (size_t)(n_in / 256) * 176;
+        case 4: return (size_t)(n_in / 256) * 210;
+        case 5: return (size_t)(n_in / 256) * 144;
+        case 6: return (size_t)(n_in / 256) * 136;
+        case 7: return (size_t)n_in * 2;
+        case 8: return (size_t)(n_in / 32) * 22;
+        case 9: return (size_t)n_in * 4;
+        default: return 0;
+    }
+}
+
+// ===================================== Part 2 ==========================================
+
+const char* draco_b200_last_error(void) { return g_err.c_str(); }
+const char* draco_b200_version(void) { return "draco_moe_b200/0.1 sm_100a"; }
+
+int draco_b200_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+int draco_b200_moe_forward(const DracoMoeLayer* L, const float* X, int T, float* out, int* order_out,
+                           float* wtop_out, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const uint64_t sh3[3] = {(uint64_t)(uintptr_t)L->sh_gate, (uint64_t)(uintptr_t)L->sh_up,
+                             (uint64_t)(uintptr_t)L->sh_down};
+    const int shc3[3] = {L->sh_code_g, L->sh_code_u, L->sh_code_d};
+    const bool has_sh = L->sh_gate && L->sh_up && L->sh_down && L->sh_ff > 0;
+    return layer_call(X, T, L->exp_ptrs, L->exp_codes, L->gate_inp, L->probs_b, L->scoring, L->n_exp, L->n_used,
+                      L->n_group, L->n_group_used, L->norm_w, L->w_scale, L->inter, L->n_in, L->n_out,
+                      has_sh ? sh3 : nullptr, shc3, has_sh ? L->sh_ff : 0, out, order_out, wtop_out,
+                      (cudaStream_t)stream);
+}
+
+int draco_b200_route(const DracoMoeLayer* L, const float* X, int T, int* order, float* wtop, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = validate_shape(L->n_exp, L->n_used, L->inter, L->n_in, L->n_out, L->scoring ? L->n_group : 1,
+                                L->n_group_used))
+        return rc;
+    if (T <= 0) return 0;
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    const float* d_gi = (const float*)dev_range(c, L->gate_inp, sizeof(float) * (size_t)L->n_exp * L->n_in);
+    if (!d_gi) return -1;
+    RouterParams rp{L->scoring, L->n_exp, L->n_used, L->n_in, L->scoring ? L->n_group : 1, L->n_group_used,
+                    L->norm_w, L->w_scale, nullptr};
+    if (L->scoring && L->probs_b) {
+        rp.probs_b = (const float*)dev_range(c, L->probs_b, sizeof(float) * L->n_exp);
+        if (!rp.probs_b) return -1;
+    }
+    const size_t n = (size_t)T * L->n_used;
+    Carver cv;
+    const size_t o_x = cv.take<float>((size_t)T * L->n_in), o_lg = cv.take<float>((size_t)T * L->n_exp);
+    const size_t o_o = cv.take<int>(n), o_w = cv.take<float>(n), o_e = cv.take<int>(1);
+    if (int rc = ensure_ws(c, cv.off)) return rc;
+    RouteBufs b{};
+    b.logits = (float*)(c->ws + o_lg);
+    b.order = (int*)(c->ws + o_o);
+    b.wtop = (float*)(c->ws + o_w);
+    b.err = (int*)(c->ws + o_e);
+    const bool dev_io = dev_kind(X);
+    cudaStream_t s = (dev_io && stream) ? (cudaStream_t)stream : c->stream;
+    const float* dx = X;
+    if (!dev_io) {
+        CK(cudaMemcpyAsync(c->ws + o_x, X, sizeof(float) * (size_t)T * L->n_in, cudaMemcpyHostToDevice, s));
+        dx = (const float*)(c->ws + o_x);
+    }
+    CK(cudaMemsetAsync(b.err, 0, sizeof(int), s));
+    launch_router_logits(dx, d_gi, T, L->n_exp, L->n_in, b.logits, s);
+    launch_router_select(rp, T, b, s);
+    CK(cudaGetLastError());
+    const cudaMemcpyKind k = dev_io ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+    CK(cudaMemcpyAsync(order, b.order, sizeof(int) * n, k, s));
+    CK(cudaMemcpyAsync(wtop, b.wtop, sizeof(float) * n, k, s));
+    if (dev_io && stream) return 0;
+    int h_err = 0;
+    CK(cudaMemcpyAsync(&h_err, b.err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    if (h_err) {
+        set_err("routing found fewer eligible experts than n_used, code %d", h_err);
+        return -2;
+    }
+    return 0;
+}
+
+int draco_b200_profile(int enable) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    resolve_prof();
+    const int o = g_prof ? 1 : 0;
+    g_prof = enable != 0;
+    for (int i = 0; i < kPhases; i++) {
+        g_phase_ms[i] = 0;
+        g_phase_n[i] = 0;
+    }
+    return o;
+}
+
+int draco_b200_profile_read(double* ms, long* counts, int n) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    resolve_prof();
+    for (int i = 0; i < n && i < kPhases; i++) {
+        if (ms) ms[i] = g_phase_ms[i];
+        if (counts) counts[i] = g_phase_n[i];
+    }
+    return kPhases;
+}
+
+long draco_b200_launch_count(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return g_launches;
+}
+
+int draco_b200_set_act_mode(int mode) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int o = g_act_mode;
+    if (mode == 0 || mode == 1) g_act_mode = mode;
+    return o;
+}
+
+int draco_b200_register(const void* host, size_t bytes) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    return dev_range(c, host, bytes) ? 0 : -1;
+}
+
+int draco_b200_forget(const void* host) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    auto it = c->regions.find((uintptr_t)host);
+    if (it == c->regions.end()) return -1;
+    cudaStreamSynchronize(c->stream);
+    // tables may point into this range: drop them all
+    for (auto& kv : c->tables) cudaFree((void*)kv.second.d_w);
+    c->tables.clear();
+    cudaFree(it->second.dev);
+    c->reg_bytes -= it->second.bytes;
+    c->regions.erase(it);
+    return 0;
+}
+
+void draco_b200_reset(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx* c = get_ctx();
+    if (!c) return;
+    cudaStreamSynchronize(c->stream);
+    for (auto& kv : c->tables) cudaFree((void*)kv.second.d_w);
+    c->tables.clear();
+    for (auto& kv : c->regions) cudaFree(kv.second.dev);
+    c->regions.clear();
+    c->reg_bytes = 0;
+    if (c->ws) cudaFree(c->ws);
+    c->ws = nullptr;
+    c->ws_cap = 0;
+}
+
+size_t draco_b200_registered_bytes(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx* c = get_ctx();
+    return c ? c->reg_bytes : 0;
+}
+
+// ---- test hooks: host arrays in, host arrays out ----
+int draco_b200_expf(const float* x, float* y, long n) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    Carver cv;
+    const size_t o_x = cv.take<float>(n), o_y = cv.take<float>(n);
+    if (int rc = ensure_ws(c, cv.off)) return rc;
+    cudaStream_t s = c->stream;
+    if (int rc = stage_in(c, s, o_x, x, n)) return rc;
+    launch_expf((const float*)(c->ws + o_x), (float*)(c->ws + o_y), n, s);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(y, c->ws + o_y, sizeof(float) * n, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int draco_b200_q8k_quantize(const float* x, int n, float* d, int8_t* q, int16_t* bsums) {
+    if (n % 256) return -1;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    const int nb = n / 256;
+    Carver cv;
+    const size_t o_x = cv.take<float>(n), o_d = cv.take<float>(nb), o_q = cv.take<int8_t>(n);
+    const size_t o_b = cv.take<int16_t>((size_t)nb * 16);
+    if (int rc = ensure_ws(c, cv.off)) return rc;
+    cudaStream_t s = c->stream;
+    if (int rc = stage_in(c, s, o_x, x, n)) return rc;
+    launch_q8k_quantize((const float*)(c->ws + o_x), 1, n, (float*)(c->ws + o_d), (int8_t*)(c->ws + o_q),
+                        (int16_t*)(c->ws + o_b), s);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(d, c->ws + o_d, sizeof(float) * nb, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(q, c->ws + o_q, n, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(bsums, c->ws + o_b, sizeof(int16_t) * nb * 16, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int draco_b200_q8k_block_dots(int code, const uint8_t* W, int rows, int n_in, const int8_t* q, const int16_t* bsums,
+                              int32_t* out2) {
+    if ((code != DRACO_CODE_Q4_K && code != DRACO_CODE_Q6_K) || n_in % 256) return -1;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    const int nb = n_in / 256;
+    const size_t wb = (size_t)rows * row_bytes(code, n_in);
+    Carver cv;
+    const size_t o_w = cv.take<uint8_t>(wb), o_q = cv.take<int8_t>(n_in), o_b = cv.take<int16_t>((size_t)nb * 16);
+    const size_t o_o = cv.take<int32_t>((size_t)rows * nb * 2);
+    if (int rc = ensure_ws(c, cv.off)) return rc;
+    cudaStream_t s = c->stream;
+    if (int rc = stage_in(c, s, o_w, W, wb)) return rc;
+    if (int rc = stage_in(c, s, o_q, q, n_in)) return rc;
+    if (int rc = stage_in(c, s, o_b, bsums, (size_t)nb * 16)) return rc;
+    launch_q8k_block_dots(code, (const uint8_t*)(c->ws + o_w), rows, n_in, (const int8_t*)(c->ws + o_q),
+                          (const int16_t*)(c->ws + o_b), (int32_t*)(c->ws + o_o), s);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(out2, c->ws + o_o, sizeof(int32_t) * rows * nb * 2, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int draco_b200_gemv_q8k(int code, const uint8_t* W, int rows, int n_in, const int8_t* q, const float* d,
+                        const int16_t* bsums, float* y) {
+    if ((code != DRACO_CODE_Q4_K && code != DRACO_CODE_Q6_K) || n_in % 256) return -1;
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    const int nb = n_in / 256;
+    const size_t wb = (size_t)rows * row_bytes(code, n_in);
+    Carver cv;
+    const size_t o_w = cv.take<uint8_t>(wb), o_q = cv.take<int8_t>(n_in), o_b = cv.take<int16_t>((size_t)nb * 16);
+    const size_t o_d = cv.take<float>(nb), o_y = cv.take<float>(rows);
+    if (int rc = ensure_ws(c, cv.off)) return rc;
+    cudaStream_t s = c->stream;
+    if (int rc = stage_in(c, s, o_w, W, wb)) return rc;
+    if (int rc = stage_in(c, s, o_q, q, n_in)) return rc;
+    if (int rc = stage_in(c, s, o_b, bsums, (size_t)nb * 16)) return rc;
+    if (int rc = stage_in(c, s, o_d, d, nb)) return rc;
+    launch_gemv_q8k(code, (const uint8_t*)(c->ws + o_w), rows, n_in, (const int8_t*)(c->ws + o_q),
+                    (const float*)(c->ws + o_d), (const int16_t*)(c->ws + o_b), (float*)(c->ws + o_y), s);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(y, c->ws + o_y, sizeof(float) * rows, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,471 @@
+// Grouped dequant-GEMV / small-batch GEMM on CUDA cores, fp32 activations.
+//
+// Lane layout: a warp walks a weight row one 256-value superblock at a time; each lane owns
+// 8 values of the superblock and loads exactly the bytes they live in (Q4_K: one aligned u32
+// of nibbles; Q6_K: three u16 (two ql pairs + one qh pair); Q8_0: four u16), so a warp's
+// loads of one superblock are contiguous.  Values are decoded to fp32 as the reference does
+// (src/m5_kern_scalar.c:69-142) and multiplied into per-lane fp32 partial sums that a warp
+// reduction finishes.  Rows are taken RPW at a time per warp so the x fragment loaded for a
+// superblock is reused by every row.
+#include "kernels.cuh"
+
+namespace draco {
+
+// value position p (0..255 within the superblock) of the lane's j-th value
+template <int CODE>
+__device__ __forceinline__ int lane_pos(int lane, int j);
+
+template <>
+__device__ __forceinline__ int lane_pos<DRACO_CODE_Q4_K>(int lane, int j) {
+    // qs bytes 4*lane..+3: low nibbles -> sub-block 2g, high nibbles -> 2g+1, g = lane/8
+    return ((lane >> 3) * 2 + (j >> 2)) * 32 + (lane & 7) * 4 + (j & 3);
+}
+template <>
+__device__ __forceinline__ int lane_pos<DRACO_CODE_Q6_K>(int lane, int j) {
+    // qh pair 2*(lane%16) of half lane/16; j = 2*s + i  ->  p = h*128 + 32*s + kk + i
+    return (lane >> 4) * 128 + 32 * (j >> 1) + 2 * (lane & 15) + (j & 1);
+}
+template <>
+__device__ __forceinline__ int lane_pos<DRACO_CODE_Q8_0>(int lane, int j) {
+    return (lane >> 2) * 32 + (lane & 3) * 8 + j;
+}
+
+// the lane's 8 fp32 x values of superblock sb (x already offset to the row of x)
+template <int CODE>
+__device__ __forceinline__ void lane_x(const float* __restrict__ x, int sb, int lane, float v[8]) {
+    const float* b = x + sb * 256;
+    if (CODE == DRACO_CODE_Q4_K) {
+        const float4 a = *reinterpret_cast<const float4*>(b + lane_pos<CODE>(lane, 0));
+        const float4 c = *reinterpret_cast<const float4*>(b + lane_pos<CODE>(lane, 4));
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+    } else if (CODE == DRACO_CODE_Q6_K) {
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            const float2 a = *reinterpret_cast<const float2*>(b + lane_pos<CODE>(lane, 2 * s));
+            v[2 * s] = a.x;
+            v[2 * s + 1] = a.y;
+        }
+    } else {
+        const float4 a = *reinterpret_cast<const float4*>(b + lane_pos<CODE>(lane, 0));
+        const float4 c = *reinterpret_cast<const float4*>(b + lane_pos<CODE>(lane, 4));
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+    }
+}
+
+__device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) {
+    return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p));
+}
+
+// the lane's 8 dequantised weights of superblock sb of `row`
+template <int CODE>
+__device__ __forceinline__ void lane_w(const uint8_t* __restrict__ row, int sb, int lane, float w[8]) {
+    if (CODE == DRACO_CODE_Q4_K) {
+        const uint8_t* blk = row + (size_t)sb * 144;
+        const uint32_t hd = __ldg(reinterpret_cast<const unsigned int*>(blk));
+        const uint32_t s0 = __ldg(reinterpret_cast<const unsigned int*>(blk + 4));
+        const uint32_t s1 = __ldg(reinterpret_cast<const unsigned int*>(blk + 8));
+        const uint32_t s2 = __ldg(reinterpret_cast<const unsigned int*>(blk + 12));
+        const uint32_t qs = __ldg(reinterpret_cast<const unsigned int*>(blk + 16 + 4 * lane));
+        const float d = h2f((uint16_t)(hd & 0xffff)), dmin = h2f((uint16_t)(hd >> 16));
+        uint8_t sb12[12];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            sb12[i] = (uint8_t)(s0 >> (8 * i));
+            sb12[4 + i] = (uint8_t)(s1 >> (8 * i));
+            sb12[8 + i] = (uint8_t)(s2 >> (8 * i));
+        }
+        const int g = lane >> 3;
+        int sc0, m0, sc1, m1;
+        q4k_sm(sb12, 2 * g, sc0, m0);
+        q4k_sm(sb12, 2 * g + 1, sc1, m1);
+        const float ds0 = d * (float)sc0, dm0 = dmin * (float)m0;
+        const float ds1 = d * (float)sc1, dm1 = dmin * (float)m1;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            w[i] = fmaf(ds0, (float)((qs >> (8 * i)) & 15), -dm0);
+            w[4 + i] = fmaf(ds1, (float)((qs >> (8 * i + 4)) & 15), -dm1);
+        }
+    } else if (CODE == DRACO_CODE_Q6_K) {
+        const uint8_t* blk = row + (size_t)sb * 210;
+        const int h = lane >> 4, kk = 2 * (lane & 15);
+        const uint32_t qlA = ld_u16(blk + h * 64 + kk);
+        const uint32_t qlB = ld_u16(blk + h * 64 + 32 + kk);
+        const uint32_t qh = ld_u16(blk + 128 + h * 32 + kk);
+        const float d = h2f((uint16_t)ld_u16(blk + 208));
+        const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            const uint32_t ql = (s & 1) ? qlB : qlA;
+            const float dsc = d * (float)__ldg(sc + h * 8 + 2 * s + (kk >> 4));
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int lo = (ql >> (8 * i + 4 * (s >> 1))) & 15;
+                const int hi = (qh >> (8 * i + 2 * s)) & 3;
+                w[2 * s + i] = dsc * (float)((lo | (hi << 4)) - 32);
+            }
+        }
+    } else {
+        const uint8_t* blk = row + (size_t)(sb * 8 + (lane >> 2)) * 34;
+        const float d = h2f((uint16_t)ld_u16(blk));
+        const uint8_t* q = blk + 2 + (lane & 3) * 8;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t v = ld_u16(q + 2 * i);
+            w[2 * i] = d * (float)(int8_t)(v & 0xff);
+            w[2 * i + 1] = d * (float)(int8_t)(v >> 8);
+        }
+    }
+}
+
+// number of superblock steps of a row and whether a lane's step is in range (Q8_0 rows may
+// end inside a 256-value step)
+__device__ __forceinline__ int n_steps(int n_in) { return (n_in + 255) / 256; }
+template <int CODE>
+__device__ __forceinline__ bool lane_live(int sb, int lane, int n_in) {
+    if (CODE == DRACO_CODE_Q8_0) return (sb * 8 + (lane >> 2)) * 32 < n_in;
+    return true;
+}
+
+constexpr int kRPW = 4;     // rows per warp
+constexpr int kCT = 4;      // tokens per pass
+constexpr int kWarps = 4;   // warps per block
+constexpr int kRowsPerItem = kRPW * kWarps;
+
+// ------------------------------------------------------------------------------------------
+// gate/up + SwiGLU: act[p][r] = silu(gate_e[r] . x_t) * (up_e[r] . x_t) for the tokens of each
+// active expert; p is the sorted position of the assignment, t = ilist[p] / tok_div.
+// ------------------------------------------------------------------------------------------
+template <int CG, int CU>
+__global__ void __launch_bounds__(32 * kWarps) gateup_kernel(ExpertTable tab, const int* __restrict__ active,
+                                                            const int* __restrict__ n_active_p,
+                                                            const int* __restrict__ off,
+                                                            const int* __restrict__ ilist, int tok_div,
+                                                            const float* __restrict__ X, int inter, int n_in,
+                                                            float* __restrict__ act) {
+    const int n_active = *n_active_p;
+    const int nrb = (inter + kRowsPerItem - 1) / kRowsPerItem;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t rbg = row_bytes(CG, n_in), rbu = row_bytes(CU, n_in);
+    const int steps = n_steps(n_in);
+    for (int item = blockIdx.x; item < n_active * nrb; item += gridDim.x) {
+        const int a = item / nrb, rb = item % nrb;
+        const int e = active[a];
+        const int p0 = off[e], c = off[e + 1] - p0;
+        const uint8_t* G = tab.w[3 * e];
+        const uint8_t* U = tab.w[3 * e + 1];
+        const int r0 = rb * kRowsPerItem + warp * kRPW;
+        for (int tc = 0; tc < c; tc += kCT) {
+            const int nt = min(kCT, c - tc);
+            const float* xr[kCT];
+#pragma unroll
+            for (int j = 0; j < kCT; j++) {
+                const int pj = p0 + tc + min(j, nt - 1);
+                const int t = ilist ? ilist[pj] / tok_div : pj;
+                xr[j] = X + (size_t)t * n_in;
+            }
+            float ag[kRPW][kCT], au[kRPW][kCT];
+#pragma unroll
+            for (int r = 0; r < kRPW; r++)
+#pragma unroll
+                for (int j = 0; j < kCT; j++) ag[r][j] = au[r][j] = 0.f;
+            for (int sb = 0; sb < steps; sb++) {
+                float xv[kCT][8];
+#pragma unroll
+                for (int j = 0; j < kCT; j++) {
+                    if (CG == CU && lane_live<CG>(sb, lane, n_in)) lane_x<CG>(xr[j], sb, lane, xv[j]);
+                }
+#pragma unroll
+                for (int r = 0; r < kRPW; r++) {
+                    const int row = r0 + r;
+                    if (row >= inter) break;
+                    float w[8];
+                    if (lane_live<CG>(sb, lane, n_in)) {
+                        if (CG != CU) {
+#pragma unroll
+                            for (int j = 0; j < kCT; j++) lane_x<CG>(xr[j], sb, lane, xv[j]);
+                        }
+                        lane_w<CG>(G + rbg * row, sb, lane, w);
+#pragma unroll
+                        for (int j = 0; j < kCT; j++)
+#pragma unroll
+                            for (int i = 0; i < 8; i++) ag[r][j] = fmaf(w[i], xv[j][i], ag[r][j]);
+                    }
+                    if (lane_live<CU>(sb, lane, n_in)) {
+                        if (CG != CU) {
+#pragma unroll
+                            for (int j = 0; j < kCT; j++) lane_x<CU>(xr[j], sb, lane, xv[j]);
+                        }
+                        lane_w<CU>(U + rbu * row, sb, lane, w);
+#pragma unroll
+                        for (int j = 0; j < kCT; j++)
+#pragma unroll
+                            for (int i = 0; i < 8; i++) au[r][j] = fmaf(w[i], xv[j][i], au[r][j]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kRPW; r++)
+#pragma unroll
+                for (int j = 0; j < kCT; j++) {
+                    const float g = warp_sum(ag[r][j]);
+                    const float u = warp_sum(au[r][j]);
+                    const int row = r0 + r;
+                    if (lane == 0 && row < inter && j < nt)
+                        act[(size_t)(p0 + tc + j) * inter + row] = silu_mul(g, u);
+                }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// down: y[p][r] = down_e[r] . act[p] for every sorted assignment p of each active expert
+// ------------------------------------------------------------------------------------------
+template <int CD>
+__global__ void __launch_bounds__(32 * kWarps) down_kernel(ExpertTable tab, const int* __restrict__ active,
+                                                          const int* __restrict__ n_active_p,
+                                                          const int* __restrict__ off,
+                                                          const float* __restrict__ act, int inter,
+                                                          int n_out, float* __restrict__ y) {
+    const int n_active = *n_active_p;
+    const int nrb = (n_out + kRowsPerItem - 1) / kRowsPerItem;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t rbd = row_bytes(CD, inter);
+    const int steps = n_steps(inter);
+    for (int item = blockIdx.x; item < n_active * nrb; item += gridDim.x) {
+        const int a = item / nrb, rb = item % nrb;
+        const int e = active[a];
+        const int p0 = off[e], c = off[e + 1] - p0;
+        const uint8_t* D = tab.w[3 * e + 2];
+        const int r0 = rb * kRowsPerItem + warp * kRPW;
+        for (int tc = 0; tc < c; tc += kCT) {
+            const int nt = min(kCT, c - tc);
+            float ad[kRPW][kCT];
+#pragma unroll
+            for (int r = 0; r < kRPW; r++)
+#pragma unroll
+                for (int j = 0; j < kCT; j++) ad[r][j] = 0.f;
+            for (int sb = 0; sb < steps; sb++) {
+                if (!lane_live<CD>(sb, lane, inter)) continue;
+                float xv[kCT][8];
+#pragma unroll
+                for (int j = 0; j < kCT; j++)
+                    lane_x<CD>(act + (size_t)(p0 + tc + min(j, nt - 1)) * inter, sb, lane, xv[j]);
+#pragma unroll
+                for (int r = 0; r < kRPW; r++) {
+                    const int row = r0 + r;
+                    if (row >= n_out) break;
+                    float w[8];
+                    lane_w<CD>(D + rbd * row, sb, lane, w);
+#pragma unroll
+                    for (int j = 0; j < kCT; j++)
+#pragma unroll
+                        for (int i = 0; i < 8; i++) ad[r][j] = fmaf(w[i], xv[j][i], ad[r][j]);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kRPW; r++)
+#pragma unroll
+                for (int j = 0; j < kCT; j++) {
+                    const float v = warp_sum(ad[r][j]);
+                    const int row = r0 + r;
+                    if (lane == 0 && row < n_out && j < nt) y[(size_t)(p0 + tc + j) * n_out + row] = v;
+                }
+        }
+    }
+}
+
+static int grid_for(int items) { return max(1, min(items, 148 * 8)); }
+
+#define DRACO_GU(A, B)                                                                           \
+    gateup_kernel<A, B><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, ilist, tok_div, X, \
+                                                      inter, n_in, act)
+
+void launch_gateup_codes(const ExpertTable& tab, int cg, int cu, const int* active, const int* n_active,
+                         int n_active_max, const int* off, const int* ilist, int tok_div, const float* X,
+                         int inter, int n_in, float* act, cudaStream_t s) {
+    const int grid = grid_for(n_active_max * ((inter + kRowsPerItem - 1) / kRowsPerItem));
+    constexpr int A = DRACO_CODE_Q4_K, B = DRACO_CODE_Q6_K, C = DRACO_CODE_Q8_0;
+    if (cg == A && cu == A) DRACO_GU(A, A);
+    else if (cg == B && cu == B) DRACO_GU(B, B);
+    else if (cg == C && cu == C) DRACO_GU(C, C);
+    else if (cg == A && cu == B) DRACO_GU(A, B);
+    else if (cg == A && cu == C) DRACO_GU(A, C);
+    else if (cg == B && cu == A) DRACO_GU(B, A);
+    else if (cg == B && cu == C) DRACO_GU(B, C);
+    else if (cg == C && cu == A) DRACO_GU(C, A);
+    else DRACO_GU(C, B);
+}
+
+void launch_down_code(const ExpertTable& tab, int cd, const int* active, const int* n_active,
+                      int n_active_max, const int* off, const float* act, int inter, int n_out, float* y,
+                      cudaStream_t s) {
+    const int grid = grid_for(n_active_max * ((n_out + kRowsPerItem - 1) / kRowsPerItem));
+    if (cd == DRACO_CODE_Q4_K)
+        down_kernel<DRACO_CODE_Q4_K><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, act, inter, n_out, y);
+    else if (cd == DRACO_CODE_Q6_K)
+        down_kernel<DRACO_CODE_Q6_K><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, act, inter, n_out, y);
+    else
+        down_kernel<DRACO_CODE_Q8_0><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, act, inter, n_out, y);
+}
+
+// ------------------------------------------------------------------------------------------
+// plain row dot products over a dense batch: Y[t][r] = W[r] . X[t]
+// ------------------------------------------------------------------------------------------
+template <int CODE>
+__global__ void __launch_bounds__(32 * kWarps) dense_kernel(const uint8_t* __restrict__ W,
+                                                           const float* __restrict__ X, int T, int n_out,
+                                                           int n_in, long x_stride, int o0,
+                                                           float* __restrict__ Y, long y_stride) {
+    const int nrb = (n_out - o0 + kRowsPerItem - 1) / kRowsPerItem;
+    const int ntc = (T + kCT - 1) / kCT;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t rb = row_bytes(CODE, n_in);
+    const int steps = n_steps(n_in);
+    for (int item = blockIdx.x; item < nrb * ntc; item += gridDim.x) {
+        const int rbi = item % nrb, tc = (item / nrb) * kCT;
+        const int nt = min(kCT, T - tc);
+        const int r0 = o0 + rbi * kRowsPerItem + warp * kRPW;
+        float acc[kRPW][kCT];
+#pragma unroll
+        for (int r = 0; r < kRPW; r++)
+#pragma unroll
+            for (int j = 0; j < kCT; j++) acc[r][j] = 0.f;
+        for (int sb = 0; sb < steps; sb++) {
+            if (!lane_live<CODE>(sb, lane, n_in)) continue;
+            float xv[kCT][8];
+#pragma unroll
+            for (int j = 0; j < kCT; j++) lane_x<CODE>(X + (size_t)(tc + min(j, nt - 1)) * x_stride, sb, lane, xv[j]);
+#pragma unroll
+            for (int r = 0; r < kRPW; r++) {
+                const int row = r0 + r;
+                if (row >= n_out) break;
+                float w[8];
+                lane_w<CODE>(W + rb * row, sb, lane, w);
+#pragma unroll
+                for (int j = 0; j < kCT; j++)
+#pragma unroll
+                    for (int i = 0; i < 8; i++) acc[r][j] = fmaf(w[i], xv[j][i], acc[r][j]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kRPW; r++)
+#pragma unroll
+            for (int j = 0; j < kCT; j++) {
+                const float v = warp_sum(acc[r][j]);
+                const int row = r0 + r;
+                if (lane == 0 && row < n_out && j < nt) Y[(size_t)(tc + j) * y_stride + row] = v;
+            }
+    }
+}
+
+static void dense_launch(int code, const uint8_t* W, const float* X, int T, int n_out, int n_in, long x_stride,
+                         int o0, float* Y, long y_stride, cudaStream_t s) {
+    const int items = ((n_out - o0 + kRowsPerItem - 1) / kRowsPerItem) * ((T + kCT - 1) / kCT);
+    const int grid = grid_for(items);
+    if (code == DRACO_CODE_Q4_K)
+        dense_kernel<DRACO_CODE_Q4_K><<<grid, 32 * kWarps, 0, s>>>(W, X, T, n_out, n_in, x_stride, o0, Y, y_stride);
+    else if (code == DRACO_CODE_Q6_K)
+        dense_kernel<DRACO_CODE_Q6_K><<<grid, 32 * kWarps, 0, s>>>(W, X, T, n_out, n_in, x_stride, o0, Y, y_stride);
+    else
+        dense_kernel<DRACO_CODE_Q8_0><<<grid, 32 * kWarps, 0, s>>>(W, X, T, n_out, n_in, x_stride, o0, Y, y_stride);
+}
+
+void launch_gemv_rows(int code, const uint8_t* W, const float* x, int n_in, int o0, int o1, float* y,
+                      cudaStream_t s) {
+    if (o1 > o0) dense_launch(code, W, x, 1, o1, n_in, n_in, o0, y, o1, s);
+}
+
+void launch_gemm_dense(int code, const uint8_t* W, const float* X, int T, int n_out, int n_in, float* Y,
+                       cudaStream_t s) {
+    dense_launch(code, W, X, T, n_out, n_in, n_in, 0, Y, n_out, s);
+}
+
+// multi-expert gemv: one dense launch per selected expert (y_e = W_{idx[e]} x_e)
+void launch_gemvn(int code, const uint8_t* W, const int* idx_host, long per, const float* x, long x_stride,
+                  int n_out_e, int n_in, int n_exp, float* y, cudaStream_t s) {
+    for (int e = 0; e < n_exp; e++)
+        dense_launch(code, W + (size_t)idx_host[e] * per, x + (size_t)e * x_stride, 1, n_out_e, n_in, n_in, 0,
+                     y + (size_t)e * n_out_e, n_out_e, s);
+}
+
+// ------------------------------------------------------------------------------------------
+// dequantise rows to fp32
+// ------------------------------------------------------------------------------------------
+template <int CODE>
+__global__ void dequant_kernel(const uint8_t* __restrict__ W, int rows, int n_in, float* __restrict__ out) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    const size_t rb = row_bytes(CODE, n_in);
+    const int steps = n_steps(n_in);
+    for (int it = warp; it < rows * steps; it += nwarps) {
+        const int r = it / steps, sb = it % steps;
+        if (!lane_live<CODE>(sb, lane, n_in)) continue;
+        float w[8];
+        lane_w<CODE>(W + rb * r, sb, lane, w);
+#pragma unroll
+        for (int j = 0; j < 8; j++) out[(size_t)r * n_in + sb * 256 + lane_pos<CODE>(lane, j)] = w[j];
+    }
+}
+
+void launch_dequant(int code, const uint8_t* W, int rows, int n_in, float* out, cudaStream_t s) {
+    const int grid = max(1, min(148 * 4, (rows * ((n_in + 255) / 256) + 7) / 8));
+    if (code == DRACO_CODE_Q4_K) dequant_kernel<DRACO_CODE_Q4_K><<<grid, 256, 0, s>>>(W, rows, n_in, out);
+    else if (code == DRACO_CODE_Q6_K) dequant_kernel<DRACO_CODE_Q6_K><<<grid, 256, 0, s>>>(W, rows, n_in, out);
+    else dequant_kernel<DRACO_CODE_Q8_0><<<grid, 256, 0, s>>>(W, rows, n_in, out);
+}
+
+// ------------------------------------------------------------------------------------------
+// combine: out[t][r] = fma(w[t,K-1], y, ... fma(w[t,0], y, 0)) (+ shared[t][r])
+// (src/m6_moe_tok.c:148-159; the ungated shared expert is added after, src/m6_engine.c:348)
+// ------------------------------------------------------------------------------------------
+__global__ void combine_kernel(const float* __restrict__ y, const int* __restrict__ order,
+                               const float* __restrict__ wtop, const int* __restrict__ pos_of, int T, int K,
+                               int E, int n_out, const float* __restrict__ shared, float* __restrict__ out) {
+    const int t = blockIdx.y;
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n_out; r += gridDim.x * blockDim.x) {
+        float acc = 0.f;
+        for (int k = 0; k < K; k++) {
+            const int i = t * K + k;
+            const int e = order[i];
+            if (e < 0 || e >= E) continue;
+            acc = fmaf(wtop[i], y[(size_t)pos_of[i] * n_out + r], acc);
+        }
+        if (shared) acc = __fadd_rn(acc, shared[(size_t)t * n_out + r]);
+        out[(size_t)t * n_out + r] = acc;
+    }
+}
+
+void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T, int K, int E,
+                    int n_out, const float* shared, float* out, cudaStream_t s) {
+    dim3 grid((n_out + 255) / 256, T);
+    combine_kernel<<<grid, 256, 0, s>>>(y, order, wtop, pos_of, T, K, E, n_out, shared, out);
+}
+
+// ------------------------------------------------------------------------------------------
+// scalar-gated shared expert (src/m6_engine.c:1113-1127): out = y * sigmoid(gw . x)
+// ------------------------------------------------------------------------------------------
+__global__ void shexp_gate_kernel(const float* __restrict__ x, const float* __restrict__ gw, int h,
+                                  const float* __restrict__ y, float* __restrict__ sg, float* __restrict__ out) {
+    const int t = blockIdx.x;
+    __shared__ float s_gate;
+    if (threadIdx.x < 32) {
+        float acc = 0.f;
+        for (int i = threadIdx.x; i < h; i += 32) acc = fmaf(gw[i], x[(size_t)t * h + i], acc);
+        acc = warp_sum(acc);
+        if (threadIdx.x == 0) {
+            sg[t] = acc;
+            s_gate = __fdiv_rn(1.0f, __fadd_rn(1.0f, host_expf(-acc)));
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < h; i += blockDim.x) out[(size_t)t * h + i] = y[(size_t)t * h + i] * s_gate;
+}
+
+void launch_shexp_gate(const float* x, const float* gw, int h, const float* y, float* sg, float* out, int T,
+                       cudaStream_t s) {
+    shexp_gate_kernel<<<T, 256, 0, s>>>(x, gw, h, y, sg, out);
+}
+
+}  // namespace draco

@@ -1,0 +1,87 @@
+// Kernel entry points of the B200 MoE FFN path, launched by the C-ABI layer (abi.cu).
+#pragma once
+#include "common.cuh"
+
+namespace draco {
+
+// Router/dispatch scratch for one call, all device memory.
+struct RouteBufs {
+    float* logits;      // [T][E]
+    int* order;         // [T][K]    selected experts, selection order
+    float* wtop;        // [T][K]    gate weights
+    int* counts;        // [E]
+    int* off;           // [E+1]     exclusive prefix of counts
+    int* ilist;         // [T*K]     assignment ids i = t*K + k sorted by (expert, i)
+    int* pos_of;        // [T*K]     sorted position of assignment i
+    int* active;        // [E]       experts with count > 0, ascending
+    int* n_active;      // [1]
+    int* err;           // [1]       nonzero: routing produced an invalid selection
+};
+
+// Router parameters (semantics of src/m6_layer.c:771-796 and :823-866).
+struct RouterParams {
+    int scoring;        // 0 softmax + renorm (granite), 1 sigmoid (+bias, groups) (bailing)
+    int n_exp, n_used, n_in;
+    int n_group, n_group_used, norm_w;
+    float w_scale;
+    const float* probs_b;   // device [E] or nullptr
+};
+
+// Weight table: 3 device pointers per expert (gate, up, down) and their format codes.
+struct ExpertTable {
+    const uint8_t* const* w;   // device array [3 * n_exp] of device pointers (gate, up, down)
+};
+
+void launch_router_logits(const float* X, const float* gate_inp, int T, int E, int H, float* logits,
+                          cudaStream_t s);
+void launch_router_select(const RouterParams& p, int T, RouteBufs& b, cudaStream_t s);
+void launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s);
+
+// gate/up (+SwiGLU) over grouped assignments.  Token of sorted position p is
+// ilist[p] / tok_div (ilist == nullptr: identity).  act is [positions][inter] in sorted order.
+// cg/cu: uniform format codes of the gate and up matrices.
+void launch_gateup_codes(const ExpertTable& tab, int cg, int cu, const int* active, const int* n_active,
+                         int n_active_max, const int* off, const int* ilist, int tok_div, const float* X,
+                         int inter, int n_in, float* act, cudaStream_t s);
+// down over grouped assignments: y[p][r] = dot(down_e row r, act[p])
+void launch_down_code(const ExpertTable& tab, int cd, const int* active, const int* n_active,
+                      int n_active_max, const int* off, const float* act, int inter, int n_out, float* y,
+                      cudaStream_t s);
+// out[t][r] = sum_k w[t,k] * y[pos_of[t*K+k]][r] (k ascending, fused multiply-add),
+// then + shared[t][r] when shared != nullptr
+void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T,
+                    int K, int E, int n_out, const float* shared, float* out, cudaStream_t s);
+// rows y[r] = dot(W row r, x) for r in [o0, o1), any supported code, one vector
+void launch_gemv_rows(int code, const uint8_t* W, const float* x, int n_in, int o0, int o1, float* y,
+                      cudaStream_t s);
+// Y[t][r] = dot(W row r, X[t]) for a dense token batch (m5_gemm semantics)
+void launch_gemm_dense(int code, const uint8_t* W, const float* X, int T, int n_out, int n_in,
+                       float* Y, cudaStream_t s);
+// multi-expert gemv (m5_gemvn semantics): y[e][o] = dot(W + idx[e]*per row o, x + e*x_stride)
+void launch_gemvn(int code, const uint8_t* W, const int* idx_host, long per, const float* x, long x_stride,
+                  int n_out_e, int n_in, int n_exp, float* y, cudaStream_t s);
+// dequantise rows to fp32
+void launch_dequant(int code, const uint8_t* W, int rows, int n_in, float* out, cudaStream_t s);
+// out[i] = y[i] * sigmoid(dot(gw, x)) for the scalar-gated shared expert; writes the gate
+// logit to sg
+void launch_shexp_gate(const float* x, const float* gw, int h, const float* y, float* sg, float* out,
+                       int T, cudaStream_t s);
+// host expf replica over an array (test hook)
+void launch_expf(const float* x, float* y, long n, cudaStream_t s);
+
+// ---- Q8_K activation mode ----
+void launch_q8k_quantize(const float* x, int rows, int n, float* d, int8_t* q, int16_t* bsums,
+                         cudaStream_t s);
+// integer superblock dots of W rows with one Q8_K vector: Q4_K -> (isc, imn) pairs,
+// Q6_K -> isum (second entry 0)
+void launch_q8k_block_dots(int code, const uint8_t* W, int rows, int n_in, const int8_t* q,
+                           const int16_t* bsums, int32_t* out2, cudaStream_t s);
+// gate/up over grouped assignments with Q8_K activations (xq/xd/xbs: per token row)
+void launch_gateup_q8k(const ExpertTable& tab, int cg, const int* active, const int* n_active,
+                       int n_active_max, const int* off, const int* ilist, int tok_div,
+                       const int8_t* xq, const float* xd, const int16_t* xbs, int inter, int n_in,
+                       float* act, cudaStream_t s);
+void launch_gemv_q8k(int code, const uint8_t* W, int rows, int n_in, const int8_t* q, const float* d,
+                     const int16_t* bsums, float* y, cudaStream_t s);
+
+}  // namespace draco

@@ -1,0 +1,184 @@
+/* draco_moe_b200.h -- C ABI of the B200 MoE FFN library (libdraco_moe_b200.so).
+ *
+ * Part 1 re-exports the reference engine's MoE entry points with their exact signatures and
+ * argument meaning, so the reference's numpy/ctypes drivers bind this library instead of the
+ * CPU one.  Each declaration cites the reference interface it replaces (paths inside the
+ * reference project).  Part 2 adds entry points the reference has no counterpart for.
+ *
+ * Common behaviour:
+ *   - Weights are addressed by the caller's pointers, as in the reference (host virtual
+ *     addresses into a GGUF mmap or numpy buffer).  The first call that sees a weight range
+ *     copies it to device memory once; later calls reuse the copy.  Device addresses are
+ *     accepted as well and used in place.  Registered host weights must stay unchanged while
+ *     registered (draco_b200_forget / draco_b200_reset drop copies).
+ *   - Activations/outputs may be host or device memory; host calls are synchronous, like the
+ *     reference.
+ *   - The `void` entry points keep the reference's signature, which has no error path: on an
+ *     error they print one line to stderr, fill the output with NaN and record the message for
+ *     draco_b200_last_error().  DRACO_B200_STRICT=1 aborts the process instead.
+ *   - Format codes: 0 Q8_0, 4 Q6_K, 5 Q4_K (9 F32 for the shared-expert gate row).
+ */
+#ifndef DRACO_MOE_B200_H
+#define DRACO_MOE_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ============================ Part 1: reference entry points ============================ */
+
+/* softmax router (max-subtracted, stable top-k, renormalised, clamp 2^-14) + experts
+ * replaces src/m6_layer.c:771-802 (m6_granite_moe); `scratch` is accepted and unused */
+void m6_granite_moe(const float* x0, const uint64_t* ptrs, const int* codes, const float* gate_inp,
+                    int n_exp, int n_used, int inter, int n_in, int n_out, float* scratch, float* out);
+
+/* sigmoid router (+probs_b for selection, n_group/n_group_used group limit, optional renorm,
+ * w_scale) + experts.  replaces src/m6_layer.c:823-873 (m6_bailing_moe) */
+void m6_bailing_moe(const float* x0, const uint64_t* ptrs, const int* codes, const float* gate_inp,
+                    const float* probs_b, int n_exp, int n_used, int n_group, int n_group_used,
+                    int norm_w, float w_scale, int inter, int n_in, int n_out, float* scratch,
+                    float* out);
+
+/* op-pointer MoE with ungated shared expert; field order of src/m6_engine.c:306-316 */
+typedef struct M6MoeP {
+    const uint64_t* exp_ptrs;
+    const int* exp_codes;
+    const float *gate_inp, *probs_b;
+    int n_exp, n_used, n_group, n_group_used, norm_w;
+    float w_scale;
+    int inter, n_in, n_out;
+    const uint8_t *sh_g, *sh_u, *sh_d;
+    int csg, csu, csd, sh_ff;
+    float* scratch;
+} M6MoeP;
+/* replaces src/m6_engine.c:318-349 (m6_moe_op) */
+void m6_moe_op(const float* xn, void* pv, float* out);
+
+/* scalar sigmoid-gated shared expert: out = down(silu(gate x) * up x) * sigmoid(gate_inp . x);
+ * shp/shc = [gate, up, down, gate_inp(F32)].  sg[0] receives the gate logit and shg the
+ * ungated expert output; sh is accepted and unused.
+ * replaces src/m6_engine.c:1113-1127 (m6_granite_shexp) */
+void m6_granite_shexp(const float* x, const uint64_t* shp, const int* shc, float* sg, float* sh,
+                      float* shg, float* out, int shi, int h);
+
+/* chunked-prefill MoE over T tokens with caller-made routing (order/wtop [T][n_used]);
+ * out[t] = sum_k wtop[t,k] * expert_{order[t,k]}(X[t]), k ascending.  DQ, GA, gwbuf, work
+ * and iwork are accepted and unused (the device path is self-contained).
+ * replaces src/m6_moe_tok.c:44-161 (m6_moe_tok) */
+typedef int (*m6_dequant_fn)(int, const uint8_t*, int, float*);
+typedef int (*m6_gemm_auto_fn)(int, const float*, const uint8_t*, int, int, int, float*);
+void m6_moe_tok(m6_dequant_fn DQ, m6_gemm_auto_fn GA, float* gwbuf, const float* X,
+                const int* order, const float* wtop, const uint64_t* ep, const int* ec, int T,
+                int n_used, int inter, int n_in, int n_out, int n_exp, float* out, float* work,
+                int* iwork);
+
+/* N selected experts' GEMV: y[e][o] = sum_i x_e[i] * W[idx[e]][o][i], x_e = x + e*x_stride.
+ * Returns 0, -1 (shape), -3 (device error).
+ * replaces src/m5/m5_batch8_k.c:80-114 (m5_gemvn_q4k) and :170-183 (m5_gemvn_q6k) */
+int m5_gemvn_q4k(const float* x, long x_stride, const uint8_t* W, const int* idx, long per,
+                 int n_out_e, int n_in, int n_exp, float* y);
+int m5_gemvn_q6k(const float* x, long x_stride, const uint8_t* W, const int* idx, long per,
+                 int n_out_e, int n_in, int n_exp, float* y);
+
+/* row GEMV for codes 0/4/5; returns 0 or -1 (unsupported code)
+ * replaces src/m5_kern_scalar.c:146-165 (m5_scalar_supported, m5_gemv, m5_gemv_range) */
+int m5_scalar_supported(int code);
+int m5_gemv(int code, const float* x, const uint8_t* W, int n_out, int n_in, float* y);
+int m5_gemv_range(int code, const float* x, const uint8_t* W, int n_out, int n_in, float* y,
+                  int o0, int o1);
+
+/* dense prefill projections Y[T][n_out] = X[T][n_in] . W^T and row dequantisation
+ * replaces src/m5/m5_gemm.c:55-235 (m5_dequant_row), :249-272 (m5_gemm),
+ *          src/m5/m5_gemm_fused.c:211-241 (m5_gemm_q80/q6k/q4k, m5_gemm_auto) */
+int m5_dequant_row(int code, const uint8_t* row, int n_in, float* out);
+int m5_gemm(int code, const float* X, const uint8_t* W, int T, int n_out, int n_in, float* Y,
+            float* wbuf);
+int m5_gemm_auto(int code, const float* X, const uint8_t* W, int c, int n_out, int n_in, float* Y);
+void m5_gemm_q80(const float* X, const uint8_t* W, int c, int n_out, int n_in, float* Y);
+void m5_gemm_q6k(const float* X, const uint8_t* W, int c, int n_out, int n_in, float* Y);
+void m5_gemm_q4k(const float* X, const uint8_t* W, int c, int n_out, int n_in, float* Y);
+
+/* kernel-library loading is a no-op here (returns 0); chunk width is recorded only.
+ * replaces src/m6_layer.c:123-140 (m6_init_dl), :46 (m6_set_moe_chunk) */
+int m6_init_dl(const char* p012, const char* p3, const char* p4, const char* p56, const char* ps);
+int m6_set_moe_chunk(int v);
+
+/* host wall time per MoE call: slot 22 routing (only with DRACO_B200_PROF=1, which adds a
+ * synchronisation), slot 23 whole call.  replaces src/m6_layer.c:18-27 */
+extern double m6_prof_t[24];
+extern long m6_prof_n[24];
+void m6_prof_reset(void);
+double m6_prof_get(int i);
+long m6_prof_cnt(int i);
+
+/* bytes of one row of n_in values; replaces src/m6_engine.c:40-54 (m6_rowbytes) */
+size_t m6_rowbytes(int code, int n_in);
+
+/* ============================ Part 2: extensions ============================ */
+
+/* Last error message of this thread's most recent failing call ("" if none). */
+const char* draco_b200_last_error(void);
+/* Library version string. */
+const char* draco_b200_version(void);
+/* Number of visible CUDA devices (0 if none). */
+int draco_b200_device_count(void);
+
+/* Whole MoE layer on T tokens: routing (softmax or sigmoid/groups as in m6_granite_moe /
+ * m6_bailing_moe, bit-identical selection and weights), grouped experts, combine in k order,
+ * optional ungated shared expert (sh_ff > 0).  X/out may be host or device memory; with
+ * device pointers and a non-null stream the call is asynchronous on that stream.
+ * order_out/wtop_out (optional, [T][n_used], same memory kind as X) receive the routing. */
+typedef struct DracoMoeLayer {
+    int n_exp, n_used, inter, n_in, n_out;
+    const uint64_t* exp_ptrs;   /* [3*n_exp] gate, up, down (host array of host or device addresses) */
+    const int* exp_codes;       /* [3*n_exp] */
+    const float* gate_inp;      /* [n_exp][n_in] fp32 */
+    const float* probs_b;       /* [n_exp] or NULL (sigmoid scoring only) */
+    int scoring;                /* 0 softmax (granite), 1 sigmoid (bailing) */
+    int n_group, n_group_used, norm_w;
+    float w_scale;
+    const void *sh_gate, *sh_up, *sh_down;  /* shared expert or NULL */
+    int sh_code_g, sh_code_u, sh_code_d, sh_ff;
+} DracoMoeLayer;
+int draco_b200_moe_forward(const DracoMoeLayer* L, const float* X, int T, float* out,
+                           int* order_out, float* wtop_out, void* stream);
+
+/* Routing only: order/wtop [T][n_used] (host or device, like X). */
+int draco_b200_route(const DracoMoeLayer* L, const float* X, int T, int* order, float* wtop,
+                     void* stream);
+
+/* Activation mode for gate/up: 0 fp32 (reference semantics, default), 1 Q8_K (int8
+ * activations, integer superblock dots).  Returns the previous mode. */
+int draco_b200_set_act_mode(int mode);
+
+/* Per-phase device timing with CUDA events on the launching stream (enable != 0 turns it on
+ * and clears the totals).  profile_read fills ms[i] (total milliseconds) and counts[i] for
+ * phases 0 route, 1 dispatch, 2 gate/up, 3 down, 4 shared expert, 5 combine; returns the
+ * number of phases. */
+int draco_b200_profile(int enable);
+int draco_b200_profile_read(double* ms, long* counts, int n);
+/* Number of kernels this library has launched since it was loaded. */
+long draco_b200_launch_count(void);
+
+/* Copy a host weight range to device memory now (otherwise done on first use). */
+int draco_b200_register(const void* host, size_t bytes);
+/* Drop the device copy of the range starting at `host`; 0 if found. */
+int draco_b200_forget(const void* host);
+/* Drop every device copy, cached table and workspace of the current device. */
+void draco_b200_reset(void);
+/* Bytes of device memory held for weight copies on the current device. */
+size_t draco_b200_registered_bytes(void);
+
+/* Test hooks (device arrays or host arrays, synchronous). */
+int draco_b200_expf(const float* x, float* y, long n);
+int draco_b200_q8k_quantize(const float* x, int n, float* d, int8_t* q, int16_t* bsums);
+int draco_b200_q8k_block_dots(int code, const uint8_t* W, int rows, int n_in, const int8_t* q,
+                              const int16_t* bsums, int32_t* out2);
+int draco_b200_gemv_q8k(int code, const uint8_t* W, int rows, int n_in, const int8_t* q,
+                        const float* d, const int16_t* bsums, float* y);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
