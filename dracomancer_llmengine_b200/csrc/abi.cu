@@ -9,6 +9,7 @@
 #include "../../include/draco_moe_b200.h"
 #include "kernels.cuh"
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdarg>
@@ -130,15 +131,37 @@ double now_s() {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// A device copy of one host range.  `subs` records, for every exact (address, length) range a
+// caller has asked for inside it, the content signature of those host bytes when they were
+// last copied.  Only the bytes of the range named in the current call are ever read: a range
+// whose signature changed (the caller freed its buffer and a new one took the address, or
+// rewrote it) is copied again into the same device bytes, so device addresses stay stable.
 struct Region {
     uintptr_t host;
     size_t bytes;
     void* dev;
+    std::map<std::pair<uintptr_t, size_t>, uint64_t> subs;
 };
+
+// Signature of a host range from 16 sampled 8-byte words (first, last, evenly between).
+uint64_t host_sig(const void* p, size_t bytes) {
+    const uint8_t* b = (const uint8_t*)p;
+    uint64_t h = 1469598103934665603ull ^ (uint64_t)bytes;
+    const int S = 16;
+    for (int i = 0; i < S; i++) {
+        const size_t off = bytes <= 8 ? 0 : (size_t)((unsigned __int128)(bytes - 8) * i / (S - 1));
+        uint64_t w = 0;
+        memcpy(&w, b + off, bytes < 8 ? bytes : 8);
+        h = (h ^ w) * 1099511628211ull;
+    }
+    return h;
+}
 
 struct Table {
     std::vector<uint64_t> ptrs;
     std::vector<int> codes;
+    // caller ranges the table points into, with the device address each resolved to
+    std::vector<std::tuple<uintptr_t, size_t, const uint8_t*>> ranges;
     int n = 0;
     const uint8_t** d_w = nullptr;   // device array of 3n device addresses
     int cg = 0, cu = 0, cd = 0;
@@ -154,6 +177,7 @@ struct Ctx {
     size_t ws_cap = 0;
     int* d_consts = nullptr;     // [0] = 0, [1] = 1, [2..3] = {0, T} (dense single-expert lists)
     int* h_consts = nullptr;     // pinned mirror of d_consts[2..3]
+    unsigned long gen = 0;       // bumped whenever cached tables are dropped
 };
 
 Ctx* g_ctx[64];
@@ -196,7 +220,22 @@ Ctx* get_ctx() {
     return g_ctx[dev];
 }
 
-// device address of host range [host, host+bytes): existing copy, or a new one
+void drop_tables(Ctx* c) {
+    for (auto& kv : c->tables) cudaFree((void*)kv.second.d_w);
+    c->tables.clear();
+    c->gen++;
+}
+
+void drop_region(Ctx* c, std::map<uintptr_t, Region>::iterator it) {
+    cudaDeviceSynchronize();
+    drop_tables(c);   // tables may point into the range
+    cudaFree(it->second.dev);
+    c->reg_bytes -= it->second.bytes;
+    c->regions.erase(it);
+}
+
+// device address of host range [host, host+bytes): existing copy (refreshed if the host
+// bytes changed), or a new one.
 const uint8_t* dev_range(Ctx* c, const void* host, size_t bytes) {
     if (!host || bytes == 0) {
         set_err("null or empty weight range");
@@ -206,11 +245,27 @@ const uint8_t* dev_range(Ctx* c, const void* host, size_t bytes) {
     auto it = c->regions.upper_bound(h);
     while (it != c->regions.begin()) {
         --it;
-        const Region& r = it->second;
-        if (r.host <= h && h + bytes <= r.host + r.bytes) return (const uint8_t*)r.dev + (h - r.host);
+        Region& r = it->second;
+        if (r.host <= h && h + bytes <= r.host + r.bytes) {
+            const uint64_t sig = host_sig(host, bytes);
+            auto sub = r.subs.find(std::make_pair(h, bytes));
+            uint8_t* d = (uint8_t*)r.dev + (h - r.host);
+            if (sub == r.subs.end() || sub->second != sig) {
+                // new or changed contents at a known address: copy them again, in place
+                cudaDeviceSynchronize();
+                if (cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+                    set_err("weight refresh failed: %s", cudaGetErrorString(cudaGetLastError()));
+                    return nullptr;
+                }
+                r.subs[std::make_pair(h, bytes)] = sig;
+            }
+            return d;
+        }
         if (r.host + (size_t(1) << 40) < h) break;   // regions are never that large
     }
     if (is_device_ptr(host)) return (const uint8_t*)host;
+    auto same = c->regions.find(h);
+    if (same != c->regions.end()) drop_region(c, same);   // a longer range now starts here
     void* d = nullptr;
     if (cudaMalloc(&d, bytes) != cudaSuccess) {
         set_err("cudaMalloc of %zu weight bytes failed: %s", bytes, cudaGetErrorString(cudaGetLastError()));
@@ -221,9 +276,23 @@ const uint8_t* dev_range(Ctx* c, const void* host, size_t bytes) {
         cudaFree(d);
         return nullptr;
     }
-    c->regions[h] = Region{h, bytes, d};
+    Region r{h, bytes, d, {}};
+    r.subs[std::make_pair(h, bytes)] = host_sig(host, bytes);
+    c->regions[h] = std::move(r);
     c->reg_bytes += bytes;
     return (const uint8_t*)d;
+}
+
+// A cached table is valid while each of its ranges still resolves to the same device bytes
+// (contents are refreshed in place by dev_range when they changed).
+bool table_fresh(Ctx* c, const Table& t) {
+    const unsigned long gen0 = c->gen;
+    const auto ranges = t.ranges;   // dev_range may drop tables (t included): iterate a copy
+    for (const auto& rg : ranges) {
+        const uint8_t* d = dev_range(c, (const void*)std::get<0>(rg), std::get<1>(rg));
+        if (c->gen != gen0 || d != std::get<2>(rg)) return false;
+    }
+    return true;
 }
 
 // activations/outputs: device pointers are used in place, host ones staged
@@ -231,16 +300,22 @@ bool dev_kind(const void* p) { return is_device_ptr(p); }
 
 // Resolve a [3n] (gate, up, down) pointer table to device addresses; cached per table
 // address and validated against its current contents on every call.
-Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inter, int n_in, int n_out) {
-    auto key = std::make_tuple((uintptr_t)ptrs, n, inter, n_in, n_out);
+Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inter, int n_in, int n_out,
+                 uintptr_t key_addr = 0) {
+    auto key = std::make_tuple(key_addr ? key_addr : (uintptr_t)ptrs, n, inter, n_in, n_out);
     auto it = c->tables.find(key);
     if (it != c->tables.end()) {
         Table& t = it->second;
         if (memcmp(t.ptrs.data(), ptrs, sizeof(uint64_t) * 3 * n) == 0 &&
-            memcmp(t.codes.data(), codes, sizeof(int) * 3 * n) == 0)
-            return &t;
-        cudaFree((void*)t.d_w);
-        c->tables.erase(it);
+            memcmp(t.codes.data(), codes, sizeof(int) * 3 * n) == 0) {
+            const unsigned long gen0 = c->gen;
+            if (table_fresh(c, t)) return &t;
+            if (c->gen != gen0) it = c->tables.find(key);   // tables were dropped meanwhile
+        }
+        if (it != c->tables.end()) {
+            cudaFree((void*)it->second.d_w);
+            c->tables.erase(it);
+        }
     }
     Table t;
     t.n = n;
@@ -280,13 +355,16 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
         for (int e = 2; stacked && e < n; e++)
             if (ptrs[3 * e + k] != base + per * (uint64_t)e) stacked = false;
         if (stacked) {
-            const uint8_t* d = dev_range(c, (const void*)(uintptr_t)base, per * (n - 1) + mat[k]);
+            const size_t len = per * (n - 1) + mat[k];
+            const uint8_t* d = dev_range(c, (const void*)(uintptr_t)base, len);
             if (!d) return nullptr;
+            t.ranges.emplace_back((uintptr_t)base, len, d);
             for (int e = 0; e < n; e++) dptr[3 * e + k] = (uint64_t)(uintptr_t)(d + per * e);
         } else {
             for (int e = 0; e < n; e++) {
                 const uint8_t* d = dev_range(c, (const void*)(uintptr_t)ptrs[3 * e + k], mat[k]);
                 if (!d) return nullptr;
+                t.ranges.emplace_back((uintptr_t)ptrs[3 * e + k], mat[k], d);
                 dptr[3 * e + k] = (uint64_t)(uintptr_t)d;
             }
         }
@@ -294,6 +372,13 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
     for (int e = 0; e < 3 * n; e++)
         if (dptr[e] % 2 || ((e % 3 != 2 ? t.cg : t.cd) == DRACO_CODE_Q4_K && dptr[e] % 16)) {
             set_err("weight address 0x%llx misaligned for its format", (unsigned long long)dptr[e]);
+            return nullptr;
+        }
+    // a range upload made while building this table may have dropped cached tables; the
+    // ranges resolved above stay valid (only this call's own uploads happened since)
+    for (auto& rg : t.ranges)
+        if (dev_range(c, (const void*)std::get<0>(rg), std::get<1>(rg)) != std::get<2>(rg)) {
+            set_err("weight ranges moved while resolving the expert table");
             return nullptr;
         }
     if (cudaMalloc((void**)&t.d_w, sizeof(uint64_t) * 3 * n) != cudaSuccess ||
@@ -497,15 +582,32 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
     a.inter = inter;
     a.n_in = n_in;
     a.n_out = n_out;
-    a.tab = get_table(c, ptrs, codes, n_exp, inter, n_in, n_out);
-    if (!a.tab) return -1;
-    if (sh3 && sh_ff > 0) {
-        a.sh = get_table(c, sh3, shc3, 1, sh_ff, n_in, n_out);
-        if (!a.sh) return -1;
-        a.sh_ff = sh_ff;
+    // resolve every weight range; an upload that replaced a changed range drops cached
+    // tables, so repeat until one pass completes without that
+    unsigned long gen0 = 0;
+    for (int attempt = 0; attempt < 3; attempt++) {
+        gen0 = c->gen;
+        a.d_gi = (const float*)dev_range(c, gate_inp, sizeof(float) * (size_t)n_exp * n_in);
+        if (!a.d_gi) return -1;
+        a.rp.probs_b = nullptr;
+        if (scoring && probs_b) {
+            a.rp.probs_b = (const float*)dev_range(c, probs_b, sizeof(float) * n_exp);
+            if (!a.rp.probs_b) return -1;
+        }
+        a.tab = get_table(c, ptrs, codes, n_exp, inter, n_in, n_out);
+        if (!a.tab) return -1;
+        a.sh = nullptr;
+        if (sh3 && sh_ff > 0) {
+            a.sh = get_table(c, sh3, shc3, 1, sh_ff, n_in, n_out, (uintptr_t)sh3[0]);
+            if (!a.sh) return -1;
+            a.sh_ff = sh_ff;
+        }
+        if (c->gen == gen0) break;
     }
-    a.d_gi = (const float*)dev_range(c, gate_inp, sizeof(float) * (size_t)n_exp * n_in);
-    if (!a.d_gi) return -1;
+    if (c->gen != gen0) {
+        set_err("weight ranges keep changing under the call");
+        return -1;
+    }
     a.rp.scoring = scoring;
     a.rp.n_exp = n_exp;
     a.rp.n_used = n_used;
@@ -514,11 +616,6 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
     a.rp.n_group_used = n_group_used;
     a.rp.norm_w = norm_w;
     a.rp.w_scale = w_scale;
-    a.rp.probs_b = nullptr;
-    if (scoring && probs_b) {
-        a.rp.probs_b = (const float*)dev_range(c, probs_b, sizeof(float) * n_exp);
-        if (!a.rp.probs_b) return -1;
-    }
     LayerBufs b;
     if (int rc = carve_layer(c, a, T, b)) return rc;
     const bool dev_io = dev_kind(x);
@@ -598,10 +695,16 @@ static int shexp_impl(const float* x, const uint64_t* shp, const int* shc, float
     }
     Ctx* c = get_ctx();
     if (!c) return -3;
-    Table* t = get_table(c, shp, shc, 1, shi, h, h);
-    if (!t) return -1;
     const float* gw = (const float*)dev_range(c, (const void*)(uintptr_t)shp[3], sizeof(float) * h);
     if (!gw) return -1;
+    const unsigned long gen0 = c->gen;
+    Table* t = get_table(c, shp, shc, 1, shi, h, h, (uintptr_t)shp[0]);
+    if (!t) return -1;
+    if (c->gen != gen0) {   // the table upload replaced a range: resolve the gate row again
+        gw = (const float*)dev_range(c, (const void*)(uintptr_t)shp[3], sizeof(float) * h);
+        t = get_table(c, shp, shc, 1, shi, h, h, (uintptr_t)shp[0]);
+        if (!gw || !t) return -1;
+    }
     Carver cv;
     const size_t o_x = cv.take<float>(h), o_a = cv.take<float>(shi), o_y = cv.take<float>(h);
     const size_t o_o = cv.take<float>(h), o_sg = cv.take<float>(1);
@@ -976,13 +1079,7 @@ int draco_b200_forget(const void* host) {
     if (!c) return -3;
     auto it = c->regions.find((uintptr_t)host);
     if (it == c->regions.end()) return -1;
-    cudaStreamSynchronize(c->stream);
-    // tables may point into this range: drop them all
-    for (auto& kv : c->tables) cudaFree((void*)kv.second.d_w);
-    c->tables.clear();
-    cudaFree(it->second.dev);
-    c->reg_bytes -= it->second.bytes;
-    c->regions.erase(it);
+    drop_region(c, it);
     return 0;
 }
 

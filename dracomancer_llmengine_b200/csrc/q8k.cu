@@ -1,7 +1,7 @@
 // Q8_K activation mode: activations quantised per 256 values to int8 with one fp32 scale and
 // int16 group sums (the block_q8_K format of ggml), multiplied with Q4_K / Q6_K weights in
 // integer arithmetic.  The reference engine keeps fp32 activations throughout; this mode is
-// an optional fast decode path, bit-exact with its CPU restatement (oracle/moe_oracle.c):
+// an optional fast decode path, bit-exact with its CPU restatement in the test checker:
 // integer superblock sums are exact, and their float combination runs per row in
 // superblock order on one lane.
 #include "kernels.cuh"

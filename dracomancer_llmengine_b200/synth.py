@@ -161,11 +161,18 @@ ZIPF_COLUMN = 0      # hidden column that carries the per-expert popularity offs
 def make_layer(hidden: int, n_exp: int, n_used: int, inter: int, scoring: str = "softmax",
                n_group: int = 1, n_group_used: int = 1, w_scale: float = 0.0,
                shared_inter: int = 0, bias: bool = False, zipf: bool = False, seed: int = 0,
-               code_gu: int = CODE_Q4_K, code_d: int = CODE_Q6_K, **_unused) -> MoELayer:
-    rng = np.random.default_rng(seed)
-    gate = quant_matrix(rng, code_gu, n_exp, inter, hidden)
-    up = quant_matrix(rng, code_gu, n_exp, inter, hidden)
-    down = quant_matrix(rng, code_d, n_exp, hidden, inter)
+               code_gu: int = CODE_Q4_K, code_d: int = CODE_Q6_K, weights: bool = True,
+               **_unused) -> MoELayer:
+    """Expert weights, router and shared expert come from independent seeded streams, so
+    `weights=False` (router only, empty expert tensors) routes exactly like the full layer."""
+    rng = np.random.default_rng([seed, 0])
+    if weights:
+        gate = quant_matrix(rng, code_gu, n_exp, inter, hidden)
+        up = quant_matrix(rng, code_gu, n_exp, inter, hidden)
+        down = quant_matrix(rng, code_d, n_exp, hidden, inter)
+    else:
+        gate = up = down = np.zeros((n_exp, 0), np.uint8)
+    rng = np.random.default_rng([seed, 1])
     gi = (rng.standard_normal((n_exp, hidden), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
     if zipf:
         ranks = np.arange(1, n_exp + 1, dtype=np.float64)
@@ -180,7 +187,8 @@ def make_layer(hidden: int, n_exp: int, n_used: int, inter: int, scoring: str = 
                      down=down, gate_inp=gi, code_gu=code_gu, code_d=code_d, scoring=scoring,
                      probs_b=probs_b, n_group=n_group, n_group_used=n_group_used, norm_w=1,
                      w_scale=w_scale)
-    if shared_inter:
+    if shared_inter and weights:
+        rng = np.random.default_rng([seed, 2])
         layer.shared_inter = shared_inter
         layer.sh_gate = quant_matrix(rng, code_gu, 1, shared_inter, hidden)[0]
         layer.sh_up = quant_matrix(rng, code_gu, 1, shared_inter, hidden)[0]
@@ -197,9 +205,9 @@ def make_tokens(layer: MoELayer, tokens: int, seed: int, zipf: bool = False) -> 
     return x
 
 
-def make_config(name: str, tokens: int | None = None):
+def make_config(name: str, tokens: int | None = None, weights: bool = True):
     """(layer, X) for a named configuration; `tokens` overrides the token count."""
     c = dict(CONFIGS[name])
-    layer = make_layer(**c)
+    layer = make_layer(weights=weights, **c)
     x = make_tokens(layer, c["tokens"] if tokens is None else tokens, c["seed"], c["zipf"])
     return layer, x
