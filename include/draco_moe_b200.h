@@ -104,8 +104,9 @@ void m5_gemm_q4k(const float* X, const uint8_t* W, int c, int n_out, int n_in, f
 int m6_init_dl(const char* p012, const char* p3, const char* p4, const char* p56, const char* ps);
 int m6_set_moe_chunk(int v);
 
-/* host wall time per MoE call: slot 22 routing (only with DRACO_B200_PROF=1, which adds a
- * synchronisation), slot 23 whole call.  replaces src/m6_layer.c:18-27 */
+/* host wall time of each synchronous MoE layer call accumulates in slot 23 (the reference's
+ * "experts total" slot); per-phase device times come from draco_b200_profile_read.
+ * replaces src/m6_layer.c:18-27 */
 extern double m6_prof_t[24];
 extern long m6_prof_n[24];
 void m6_prof_reset(void);
