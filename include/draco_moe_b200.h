@@ -149,6 +149,21 @@ int draco_b200_moe_forward(const DracoMoeLayer* L, const float* X, int T, float*
 int draco_b200_route(const DracoMoeLayer* L, const float* X, int T, int* order, float* wtop,
                      void* stream);
 
+/* Allocation-free m6_moe_tok, for callers that cannot let a library allocate device memory
+ * (an engine that reserves HBM for weights and KV cache up front and forbids allocations
+ * outside its pool; a decode loop that cannot take cudaMalloc's implicit synchronisation).
+ * No counterpart in the reference.  All pointers are device memory except ep_dev (a host array
+ * of 3*n_exp DEVICE addresses of the gate, up and down matrices) and ec (host codes).  Scratch
+ * is a fixed 32 MiB device array inside the library, held by every GPU that loads it until the
+ * process exits: calls needing more (T*n_used*(inter+n_out)*4 bytes plus small lists) return -4
+ * without running.  All calls share that array and it keeps the last call's contents; calls that
+ * overlap on the GPU race on it.  The first call on a device looks up the array's address (make
+ * it before any stream capture).  Asynchronous on `stream`.  Returns 0, -1 (shape or
+ * arguments), -3 (CUDA error), -4 (exceeds the scratch maximum); messages go to stderr. */
+int draco_b200_moe_tok_noalloc(const float* X, const int* order, const float* wtop,
+                               const uint64_t* ep_dev, const int* ec, int T, int n_used, int inter,
+                               int n_in, int n_out, int n_exp, float* out, void* stream);
+
 /* Activation mode for gate/up: 0 fp32 (reference semantics, default), 1 Q8_K (int8
  * activations, integer superblock dots).  Returns the previous mode. */
 int draco_b200_set_act_mode(int mode);
