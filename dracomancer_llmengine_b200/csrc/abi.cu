@@ -141,6 +141,11 @@ struct Region {
     size_t bytes;
     void* dev;
     std::map<std::pair<uintptr_t, size_t>, uint64_t> subs;
+    // Q6_K copy padded to 224-byte superblocks: n_mats matrices of rows x nb superblocks, host_per
+    // bytes apart on the host side, dev_per apart on the device.  rows == 0: plain byte copy.
+    int rows = 0, nb = 0, n_mats = 0;
+    size_t host_per = 0, dev_per = 0;
+    bool from_device = false;   // copied from caller device memory (no host bytes to re-check)
 };
 
 // Signature of a host range from 16 sampled 8-byte words (first, last, evenly between).
@@ -157,14 +162,28 @@ uint64_t host_sig(const void* p, size_t bytes) {
     return h;
 }
 
+// one weight-matrix request: host base, format, rows, row length, matrices, host stride
+struct MatKey {
+    uintptr_t host;
+    int code, rows, n_in, n_mats;
+    size_t host_per;
+    const uint8_t* dev;    // what it resolved to
+    size_t dev_per;
+};
+
 struct Table {
     std::vector<uint64_t> ptrs;
     std::vector<int> codes;
-    // caller ranges the table points into, with the device address each resolved to
-    std::vector<std::tuple<uintptr_t, size_t, const uint8_t*>> ranges;
+    std::vector<MatKey> mats;        // the caller ranges the table points into
     int n = 0;
     const uint8_t** d_w = nullptr;   // device array of 3n device addresses
     int cg = 0, cu = 0, cd = 0;
+    int q6s = kQ6Padded;             // Q6_K superblock stride of the device copies
+    bool stacked = false;            // each matrix kind is base + e * dev_per[k]
+    const uint8_t* base[3] = {nullptr, nullptr, nullptr};
+    size_t dev_per[3] = {0, 0, 0};
+    int inter = 0, n_in = 0, n_out = 0;
+    void* tc = nullptr;              // tensor-core path state (tensor maps), owned by tc_gemm.cu
 };
 
 struct Ctx {
@@ -246,7 +265,7 @@ const uint8_t* dev_range(Ctx* c, const void* host, size_t bytes) {
     while (it != c->regions.begin()) {
         --it;
         Region& r = it->second;
-        if (r.host <= h && h + bytes <= r.host + r.bytes) {
+        if (r.rows == 0 && r.host <= h && h + bytes <= r.host + r.bytes) {
             const uint64_t sig = host_sig(host, bytes);
             auto sub = r.subs.find(std::make_pair(h, bytes));
             uint8_t* d = (uint8_t*)r.dev + (h - r.host);
@@ -283,14 +302,106 @@ const uint8_t* dev_range(Ctx* c, const void* host, size_t bytes) {
     return (const uint8_t*)d;
 }
 
-// A cached table is valid while each of its ranges still resolves to the same device bytes
-// (contents are refreshed in place by dev_range when they changed).
+// Copy n_mats Q6_K matrices (rows x nb superblocks each, src_per bytes apart, host or device
+// memory) into dst with 224-byte superblocks.
+int upload_q6(void* dst, const void* src, bool src_dev, int n_mats, size_t src_per, int rows, int nb) {
+    const size_t mat = (size_t)rows * nb * kQ6File;
+    if (src_dev) {
+        launch_q6_pad((const uint8_t*)src, src_per, n_mats, rows, nb, (uint8_t*)dst, 0);
+        CK(cudaGetLastError());
+        CK(cudaDeviceSynchronize());
+        return 0;
+    }
+    uint8_t* tmp = nullptr;
+    CK(cudaMalloc((void**)&tmp, mat * n_mats));
+    cudaError_t e = cudaMemcpy2D(tmp, mat, src, src_per, mat, n_mats, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        launch_q6_pad(tmp, mat, n_mats, rows, nb, (uint8_t*)dst, 0);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(tmp);
+    if (e != cudaSuccess) {
+        set_err("Q6_K weight upload failed: %s", cudaGetErrorString(e));
+        return -3;
+    }
+    return 0;
+}
+
+// Device copy of n_mats weight matrices of `code` (rows x n_in values each, host_per bytes
+// apart) starting at `host`; *dev_per receives the device distance between matrices.  Q6_K
+// copies are padded to 224-byte superblocks; other formats are byte copies (dev_range).
+const uint8_t* dev_matrix(Ctx* c, const void* host, int code, int rows, int n_in, int n_mats, size_t host_per,
+                          size_t* dev_per) {
+    const size_t mat = (size_t)rows * row_bytes(code, n_in);
+    if (n_mats <= 1) host_per = mat;
+    const size_t bytes = host_per * (n_mats - 1) + mat;
+    if (code != DRACO_CODE_Q6_K) {
+        *dev_per = host_per;
+        return dev_range(c, host, bytes);
+    }
+    const int nb = n_in / 256;
+    const uintptr_t h = (uintptr_t)host;
+    auto it = c->regions.upper_bound(h);
+    while (it != c->regions.begin()) {
+        --it;
+        Region& r = it->second;
+        if (r.rows == rows && r.nb == nb && r.host <= h && h + bytes <= r.host + r.bytes &&
+            (h - r.host) % r.host_per == 0 && (n_mats == 1 || host_per == r.host_per)) {
+            const size_t m0 = (h - r.host) / r.host_per;
+            if (m0 + n_mats <= (size_t)r.n_mats) {
+                uint8_t* d = (uint8_t*)r.dev + m0 * r.dev_per;
+                if (!r.from_device) {
+                    const uint64_t sig = host_sig(host, bytes);
+                    auto sub = r.subs.find(std::make_pair(h, bytes));
+                    if (sub == r.subs.end() || sub->second != sig) {
+                        cudaDeviceSynchronize();
+                        if (upload_q6(d, host, false, n_mats, host_per, rows, nb)) return nullptr;
+                        r.subs[std::make_pair(h, bytes)] = sig;
+                    }
+                }
+                *dev_per = r.dev_per;
+                return d;
+            }
+        }
+        if (r.host + (size_t(1) << 40) < h) break;
+    }
+    const bool src_dev = is_device_ptr(host);
+    auto same = c->regions.find(h);
+    if (same != c->regions.end()) drop_region(c, same);
+    const size_t dper = (size_t)rows * nb * kQ6Padded;
+    void* d = nullptr;
+    if (cudaMalloc(&d, dper * n_mats) != cudaSuccess) {
+        set_err("cudaMalloc of %zu weight bytes failed: %s", dper * n_mats, cudaGetErrorString(cudaGetLastError()));
+        return nullptr;
+    }
+    if (upload_q6(d, host, src_dev, n_mats, host_per, rows, nb)) {
+        cudaFree(d);
+        return nullptr;
+    }
+    Region r{h, bytes, d, {}};
+    r.rows = rows;
+    r.nb = nb;
+    r.n_mats = n_mats;
+    r.host_per = host_per;
+    r.dev_per = dper;
+    r.from_device = src_dev;
+    if (!src_dev) r.subs[std::make_pair(h, bytes)] = host_sig(host, bytes);
+    c->regions[h] = std::move(r);
+    c->reg_bytes += dper * n_mats;
+    *dev_per = dper;
+    return (const uint8_t*)d;
+}
+
+// A cached table is valid while each of its matrices still resolves to the same device bytes
+// (contents are refreshed in place when they changed).
 bool table_fresh(Ctx* c, const Table& t) {
     const unsigned long gen0 = c->gen;
-    const auto ranges = t.ranges;   // dev_range may drop tables (t included): iterate a copy
-    for (const auto& rg : ranges) {
-        const uint8_t* d = dev_range(c, (const void*)std::get<0>(rg), std::get<1>(rg));
-        if (c->gen != gen0 || d != std::get<2>(rg)) return false;
+    const auto mats = t.mats;   // resolving may drop tables (t included): iterate a copy
+    for (const auto& m : mats) {
+        size_t dp = 0;
+        const uint8_t* d = dev_matrix(c, (const void*)m.host, m.code, m.rows, m.n_in, m.n_mats, m.host_per, &dp);
+        if (c->gen != gen0 || d != m.dev) return false;
     }
     return true;
 }
@@ -343,29 +454,44 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
         set_err("K-quant rows need multiples of 256 values");
         return nullptr;
     }
-    const size_t mat[3] = {(size_t)inter * row_bytes(t.cg, n_in), (size_t)inter * row_bytes(t.cu, n_in),
-                           (size_t)n_out * row_bytes(t.cd, inter)};
+    const int kcode[3] = {t.cg, t.cu, t.cd};
+    const int krows[3] = {inter, inter, n_out};
+    const int kin[3] = {n_in, n_in, inter};
+    t.inter = inter;
+    t.n_in = n_in;
+    t.n_out = n_out;
+    t.stacked = n > 1;
     std::vector<uint64_t> dptr(3 * n);
     for (int k = 0; k < 3; k++) {
         // stacked experts base + e*per (the GGUF layout) are copied as one range
+        const size_t mat = (size_t)krows[k] * row_bytes(kcode[k], kin[k]);
         bool stacked = n > 1;
         const uint64_t base = ptrs[k];
         const uint64_t per = n > 1 ? ptrs[3 + k] - base : 0;
-        if (n > 1 && (ptrs[3 + k] <= base || per < mat[k])) stacked = false;
+        if (n > 1 && (ptrs[3 + k] <= base || per < mat)) stacked = false;
         for (int e = 2; stacked && e < n; e++)
             if (ptrs[3 * e + k] != base + per * (uint64_t)e) stacked = false;
         if (stacked) {
-            const size_t len = per * (n - 1) + mat[k];
-            const uint8_t* d = dev_range(c, (const void*)(uintptr_t)base, len);
+            size_t dp = 0;
+            const uint8_t* d = dev_matrix(c, (const void*)(uintptr_t)base, kcode[k], krows[k], kin[k], n, per, &dp);
             if (!d) return nullptr;
-            t.ranges.emplace_back((uintptr_t)base, len, d);
-            for (int e = 0; e < n; e++) dptr[3 * e + k] = (uint64_t)(uintptr_t)(d + per * e);
+            t.mats.push_back(MatKey{(uintptr_t)base, kcode[k], krows[k], kin[k], n, per, d, dp});
+            t.base[k] = d;
+            t.dev_per[k] = dp;
+            for (int e = 0; e < n; e++) dptr[3 * e + k] = (uint64_t)(uintptr_t)(d + dp * e);
         } else {
+            t.stacked = false;
             for (int e = 0; e < n; e++) {
-                const uint8_t* d = dev_range(c, (const void*)(uintptr_t)ptrs[3 * e + k], mat[k]);
+                size_t dp = 0;
+                const uint8_t* d = dev_matrix(c, (const void*)(uintptr_t)ptrs[3 * e + k], kcode[k], krows[k], kin[k],
+                                              1, mat, &dp);
                 if (!d) return nullptr;
-                t.ranges.emplace_back((uintptr_t)ptrs[3 * e + k], mat[k], d);
+                t.mats.push_back(MatKey{(uintptr_t)ptrs[3 * e + k], kcode[k], krows[k], kin[k], 1, mat, d, dp});
                 dptr[3 * e + k] = (uint64_t)(uintptr_t)d;
+            }
+            if (n == 1) {
+                t.base[k] = (const uint8_t*)(uintptr_t)dptr[k];
+                t.dev_per[k] = mat;
             }
         }
     }
@@ -374,13 +500,15 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
             set_err("weight address 0x%llx misaligned for its format", (unsigned long long)dptr[e]);
             return nullptr;
         }
-    // a range upload made while building this table may have dropped cached tables; the
-    // ranges resolved above stay valid (only this call's own uploads happened since)
-    for (auto& rg : t.ranges)
-        if (dev_range(c, (const void*)std::get<0>(rg), std::get<1>(rg)) != std::get<2>(rg)) {
+    // an upload made while building this table may have dropped cached tables; the matrices
+    // resolved above must still resolve to the same device bytes
+    for (auto& m : t.mats) {
+        size_t dp = 0;
+        if (dev_matrix(c, (const void*)m.host, m.code, m.rows, m.n_in, m.n_mats, m.host_per, &dp) != m.dev) {
             set_err("weight ranges moved while resolving the expert table");
             return nullptr;
         }
+    }
     if (cudaMalloc((void**)&t.d_w, sizeof(uint64_t) * 3 * n) != cudaSuccess ||
         cudaMemcpy((void*)t.d_w, dptr.data(), sizeof(uint64_t) * 3 * n, cudaMemcpyHostToDevice) != cudaSuccess) {
         set_err("pointer table upload failed: %s", cudaGetErrorString(cudaGetLastError()));
@@ -478,8 +606,8 @@ int dense_ffn(Ctx* c, Table* t, int T, const float* x, int ff, int n_in, int n_o
     {
         PhaseScope ps(kShared, s);
         launch_gateup_codes(et, t->cg, t->cu, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, nullptr, 1, x, ff,
-                            n_in, act, s);
-        launch_down_code(et, t->cd, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, act, ff, n_out, y, s);
+                            n_in, act, s, t->q6s);
+        launch_down_code(et, t->cd, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, act, ff, n_out, y, s, t->q6s);
     }
     g_launches += 2;
     CK(cudaGetLastError());
@@ -512,17 +640,18 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
             (a.tab->cg == DRACO_CODE_Q4_K || a.tab->cg == DRACO_CODE_Q6_K) && a.n_in % 256 == 0) {
             launch_q8k_quantize(b.x, T, a.n_in, b.xd, b.xq, b.xbs, s);
             launch_gateup_q8k(et, a.tab->cg, rb.active, rb.n_active, na_max, rb.off, rb.ilist, a.K, b.xq, b.xd,
-                              b.xbs, a.inter, a.n_in, b.act, s);
+                              b.xbs, a.inter, a.n_in, b.act, s, a.tab->q6s);
             g_launches += 2;
         } else {
             launch_gateup_codes(et, a.tab->cg, a.tab->cu, rb.active, rb.n_active, na_max, rb.off, rb.ilist, a.K,
-                                b.x, a.inter, a.n_in, b.act, s);
+                                b.x, a.inter, a.n_in, b.act, s, a.tab->q6s);
             g_launches += 1;
         }
     }
     {
         PhaseScope ps(kDown, s);
-        launch_down_code(et, a.tab->cd, rb.active, rb.n_active, na_max, rb.off, b.act, a.inter, a.n_out, b.y, s);
+        launch_down_code(et, a.tab->cd, rb.active, rb.n_active, na_max, rb.off, b.act, a.inter, a.n_out, b.y, s,
+                         a.tab->q6s);
         g_launches += 1;
     }
     CK(cudaGetLastError());
@@ -794,7 +923,6 @@ static int gemvn_impl(int code, const float* x, long x_stride, const uint8_t* W,
     if (n_exp <= 0 || n_out_e <= 0) return 0;
     Ctx* c = get_ctx();
     if (!c) return -3;
-    const size_t mb = (size_t)n_out_e * row_bytes(code, n_in);
     const size_t xn = x_stride ? (size_t)x_stride * (n_exp - 1) + n_in : (size_t)n_in;
     Carver cv;
     const size_t o_x = cv.take<float>(xn), o_y = cv.take<float>((size_t)n_exp * n_out_e);
@@ -804,9 +932,11 @@ static int gemvn_impl(int code, const float* x, long x_stride, const uint8_t* W,
     cudaStream_t s = c->stream;
     CK(cudaMemcpyAsync(dx, x, sizeof(float) * xn, cudaMemcpyHostToDevice, s));
     for (int e = 0; e < n_exp; e++) {
-        const uint8_t* dw = dev_range(c, W + (size_t)idx[e] * per, mb);
+        size_t dp = 0;
+        const uint8_t* dw = dev_matrix(c, W + (size_t)idx[e] * per, code, n_out_e, n_in, 1, 0, &dp);
         if (!dw) return -3;
-        launch_gemv_rows(code, dw, dx + (size_t)e * x_stride, n_in, 0, n_out_e, dy + (size_t)e * n_out_e, s);
+        launch_gemv_rows(code, dw, dx + (size_t)e * x_stride, n_in, 0, n_out_e, dy + (size_t)e * n_out_e, s,
+                         kQ6Padded);
     }
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(y, dy, sizeof(float) * (size_t)n_exp * n_out_e, cudaMemcpyDeviceToHost, s));
@@ -841,7 +971,8 @@ static int gemm_impl(int code, const float* X, const uint8_t* W, int T, int n_ou
     if (T <= 0 || o1 <= o0) return 0;
     Ctx* c = get_ctx();
     if (!c) return -3;
-    const uint8_t* dw = dev_range(c, W, (size_t)n_out * row_bytes(code, n_in));
+    size_t dp = 0;
+    const uint8_t* dw = dev_matrix(c, W, code, n_out, n_in, 1, 0, &dp);
     if (!dw) return -3;
     Carver cv;
     const size_t o_x = cv.take<float>((size_t)T * n_in), o_y = cv.take<float>((size_t)T * n_out);
@@ -851,11 +982,11 @@ static int gemm_impl(int code, const float* X, const uint8_t* W, int T, int n_ou
     cudaStream_t s = c->stream;
     CK(cudaMemcpyAsync(dx, X, sizeof(float) * (size_t)T * n_in, cudaMemcpyHostToDevice, s));
     if (T == 1) {
-        launch_gemv_rows(code, dw, dx, n_in, o0, o1, dy, s);
+        launch_gemv_rows(code, dw, dx, n_in, o0, o1, dy, s, kQ6Padded);
         CK(cudaGetLastError());
         CK(cudaMemcpyAsync(Y + o0, dy + o0, sizeof(float) * (o1 - o0), cudaMemcpyDeviceToHost, s));
     } else {
-        launch_gemm_dense(code, dw, dx, T, n_out, n_in, dy, s);
+        launch_gemm_dense(code, dw, dx, T, n_out, n_in, dy, s, kQ6Padded);
         CK(cudaGetLastError());
         CK(cudaMemcpyAsync(Y, dy, sizeof(float) * (size_t)T * n_out, cudaMemcpyDeviceToHost, s));
     }
@@ -911,7 +1042,7 @@ int m5_dequant_row(int code, const uint8_t* row, int n_in, float* out) {
     if (ensure_ws(c, cv.off)) return -1;
     cudaStream_t s = c->stream;
     if (cudaMemcpyAsync(c->ws + o_w, row, rb, cudaMemcpyHostToDevice, s) != cudaSuccess) return -1;
-    launch_dequant(code, (const uint8_t*)(c->ws + o_w), 1, n_in, (float*)(c->ws + o_o), s);
+    launch_dequant(code, (const uint8_t*)(c->ws + o_w), 1, n_in, (float*)(c->ws + o_o), s, kQ6File);
     if (cudaMemcpyAsync(out, c->ws + o_o, sizeof(float) * n_in, cudaMemcpyDeviceToHost, s) != cudaSuccess) return -1;
     return cudaStreamSynchronize(s) == cudaSuccess ? 0 : -1;
 }
@@ -1160,7 +1291,7 @@ int draco_b200_q8k_block_dots(int code, const uint8_t* W, int rows, int n_in, co
     if (int rc = stage_in(c, s, o_q, q, n_in)) return rc;
     if (int rc = stage_in(c, s, o_b, bsums, (size_t)nb * 16)) return rc;
     launch_q8k_block_dots(code, (const uint8_t*)(c->ws + o_w), rows, n_in, (const int8_t*)(c->ws + o_q),
-                          (const int16_t*)(c->ws + o_b), (int32_t*)(c->ws + o_o), s);
+                          (const int16_t*)(c->ws + o_b), (int32_t*)(c->ws + o_o), s, kQ6File);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(out2, c->ws + o_o, sizeof(int32_t) * rows * nb * 2, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
@@ -1185,7 +1316,7 @@ int draco_b200_gemv_q8k(int code, const uint8_t* W, int rows, int n_in, const in
     if (int rc = stage_in(c, s, o_b, bsums, (size_t)nb * 16)) return rc;
     if (int rc = stage_in(c, s, o_d, d, nb)) return rc;
     launch_gemv_q8k(code, (const uint8_t*)(c->ws + o_w), rows, n_in, (const int8_t*)(c->ws + o_q),
-                    (const float*)(c->ws + o_d), (const int16_t*)(c->ws + o_b), (float*)(c->ws + o_y), s);
+                    (const float*)(c->ws + o_d), (const int16_t*)(c->ws + o_b), (float*)(c->ws + o_y), s, kQ6File);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(y, c->ws + o_y, sizeof(float) * rows, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));

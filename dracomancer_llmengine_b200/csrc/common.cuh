@@ -21,7 +21,13 @@ __host__ __device__ inline int block_bytes(int code) {
 __host__ __device__ inline int block_values(int code) {
     return code == DRACO_CODE_Q8_0 ? 32 : 256;
 }
-__host__ __device__ inline size_t row_bytes(int code, int n) {
+// Q6_K superblocks are 210 B in GGUF files; copies held by the library's weight registry pad
+// them to 224 B so every superblock starts on a 16-byte boundary (TMA-addressable).
+constexpr int kQ6File = 210;
+constexpr int kQ6Padded = 224;
+// bytes of one row of n values; q6s = Q6_K superblock stride of the buffer (210 or 224)
+__host__ __device__ inline size_t row_bytes(int code, int n, int q6s = kQ6File) {
+    if (code == DRACO_CODE_Q6_K) return (size_t)(n / 256) * (size_t)q6s;
     const int bv = block_values(code);
     return (size_t)(n / bv) * (size_t)block_bytes(code);
 }

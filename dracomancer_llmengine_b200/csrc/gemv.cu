@@ -9,6 +9,8 @@
 // superblock is reused by every row.
 #include "kernels.cuh"
 
+#include <algorithm>
+
 namespace draco {
 
 // value position p (0..255 within the superblock) of the lane's j-th value
@@ -60,7 +62,7 @@ __device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) {
 
 // the lane's 8 dequantised weights of superblock sb of `row`
 template <int CODE>
-__device__ __forceinline__ void lane_w(const uint8_t* __restrict__ row, int sb, int lane, float w[8]) {
+__device__ __forceinline__ void lane_w(const uint8_t* __restrict__ row, int sb, int lane, float w[8], int q6s) {
     if (CODE == DRACO_CODE_Q4_K) {
         const uint8_t* blk = row + (size_t)sb * 144;
         const uint32_t hd = __ldg(reinterpret_cast<const unsigned int*>(blk));
@@ -88,7 +90,7 @@ __device__ __forceinline__ void lane_w(const uint8_t* __restrict__ row, int sb, 
             w[4 + i] = fmaf(ds1, (float)((qs >> (8 * i + 4)) & 15), -dm1);
         }
     } else if (CODE == DRACO_CODE_Q6_K) {
-        const uint8_t* blk = row + (size_t)sb * 210;
+        const uint8_t* blk = row + (size_t)sb * q6s;
         const int h = lane >> 4, kk = 2 * (lane & 15);
         const uint32_t qlA = ld_u16(blk + h * 64 + kk);
         const uint32_t qlB = ld_u16(blk + h * 64 + 32 + kk);
@@ -143,11 +145,11 @@ __global__ void __launch_bounds__(32 * kWarps) gateup_kernel(ExpertTable tab, co
                                                             const int* __restrict__ off,
                                                             const int* __restrict__ ilist, int tok_div,
                                                             const float* __restrict__ X, int inter, int n_in,
-                                                            float* __restrict__ act) {
+                                                            float* __restrict__ act, int q6s) {
     const int n_active = *n_active_p;
     const int nrb = (inter + kRowsPerItem - 1) / kRowsPerItem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t rbg = row_bytes(CG, n_in), rbu = row_bytes(CU, n_in);
+    const size_t rbg = row_bytes(CG, n_in, q6s), rbu = row_bytes(CU, n_in, q6s);
     const int steps = n_steps(n_in);
     for (int item = blockIdx.x; item < n_active * nrb; item += gridDim.x) {
         const int a = item / nrb, rb = item % nrb;
@@ -186,7 +188,7 @@ __global__ void __launch_bounds__(32 * kWarps) gateup_kernel(ExpertTable tab, co
 #pragma unroll
                             for (int j = 0; j < kCT; j++) lane_x<CG>(xr[j], sb, lane, xv[j]);
                         }
-                        lane_w<CG>(G + rbg * row, sb, lane, w);
+                        lane_w<CG>(G + rbg * row, sb, lane, w, q6s);
 #pragma unroll
                         for (int j = 0; j < kCT; j++)
 #pragma unroll
@@ -197,7 +199,7 @@ __global__ void __launch_bounds__(32 * kWarps) gateup_kernel(ExpertTable tab, co
 #pragma unroll
                             for (int j = 0; j < kCT; j++) lane_x<CU>(xr[j], sb, lane, xv[j]);
                         }
-                        lane_w<CU>(U + rbu * row, sb, lane, w);
+                        lane_w<CU>(U + rbu * row, sb, lane, w, q6s);
 #pragma unroll
                         for (int j = 0; j < kCT; j++)
 #pragma unroll
@@ -227,11 +229,11 @@ __global__ void __launch_bounds__(32 * kWarps) down_kernel(ExpertTable tab, cons
                                                           const int* __restrict__ n_active_p,
                                                           const int* __restrict__ off,
                                                           const float* __restrict__ act, int inter,
-                                                          int n_out, float* __restrict__ y) {
+                                                          int n_out, float* __restrict__ y, int q6s) {
     const int n_active = *n_active_p;
     const int nrb = (n_out + kRowsPerItem - 1) / kRowsPerItem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t rbd = row_bytes(CD, inter);
+    const size_t rbd = row_bytes(CD, inter, q6s);
     const int steps = n_steps(inter);
     for (int item = blockIdx.x; item < n_active * nrb; item += gridDim.x) {
         const int a = item / nrb, rb = item % nrb;
@@ -257,7 +259,7 @@ __global__ void __launch_bounds__(32 * kWarps) down_kernel(ExpertTable tab, cons
                     const int row = r0 + r;
                     if (row >= n_out) break;
                     float w[8];
-                    lane_w<CD>(D + rbd * row, sb, lane, w);
+                    lane_w<CD>(D + rbd * row, sb, lane, w, q6s);
 #pragma unroll
                     for (int j = 0; j < kCT; j++)
 #pragma unroll
@@ -280,11 +282,11 @@ static int grid_for(int items) { return max(1, min(items, 148 * 8)); }
 
 #define DRACO_GU(A, B)                                                                           \
     gateup_kernel<A, B><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, ilist, tok_div, X, \
-                                                      inter, n_in, act)
+                                                      inter, n_in, act, q6s)
 
 void launch_gateup_codes(const ExpertTable& tab, int cg, int cu, const int* active, const int* n_active,
                          int n_active_max, const int* off, const int* ilist, int tok_div, const float* X,
-                         int inter, int n_in, float* act, cudaStream_t s) {
+                         int inter, int n_in, float* act, cudaStream_t s, int q6s) {
     const int grid = grid_for(n_active_max * ((inter + kRowsPerItem - 1) / kRowsPerItem));
     constexpr int A = DRACO_CODE_Q4_K, B = DRACO_CODE_Q6_K, C = DRACO_CODE_Q8_0;
     if (cg == A && cu == A) DRACO_GU(A, A);
@@ -300,14 +302,14 @@ void launch_gateup_codes(const ExpertTable& tab, int cg, int cu, const int* acti
 
 void launch_down_code(const ExpertTable& tab, int cd, const int* active, const int* n_active,
                       int n_active_max, const int* off, const float* act, int inter, int n_out, float* y,
-                      cudaStream_t s) {
+                      cudaStream_t s, int q6s) {
     const int grid = grid_for(n_active_max * ((n_out + kRowsPerItem - 1) / kRowsPerItem));
     if (cd == DRACO_CODE_Q4_K)
-        down_kernel<DRACO_CODE_Q4_K><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, act, inter, n_out, y);
+        down_kernel<DRACO_CODE_Q4_K><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, act, inter, n_out, y, q6s);
     else if (cd == DRACO_CODE_Q6_K)
-        down_kernel<DRACO_CODE_Q6_K><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, act, inter, n_out, y);
+        down_kernel<DRACO_CODE_Q6_K><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, act, inter, n_out, y, q6s);
     else
-        down_kernel<DRACO_CODE_Q8_0><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, act, inter, n_out, y);
+        down_kernel<DRACO_CODE_Q8_0><<<grid, 32 * kWarps, 0, s>>>(tab, active, n_active, off, act, inter, n_out, y, q6s);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -317,11 +319,11 @@ template <int CODE>
 __global__ void __launch_bounds__(32 * kWarps) dense_kernel(const uint8_t* __restrict__ W,
                                                            const float* __restrict__ X, int T, int n_out,
                                                            int n_in, long x_stride, int o0,
-                                                           float* __restrict__ Y, long y_stride) {
+                                                           float* __restrict__ Y, long y_stride, int q6s) {
     const int nrb = (n_out - o0 + kRowsPerItem - 1) / kRowsPerItem;
     const int ntc = (T + kCT - 1) / kCT;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t rb = row_bytes(CODE, n_in);
+    const size_t rb = row_bytes(CODE, n_in, q6s);
     const int steps = n_steps(n_in);
     for (int item = blockIdx.x; item < nrb * ntc; item += gridDim.x) {
         const int rbi = item % nrb, tc = (item / nrb) * kCT;
@@ -342,7 +344,7 @@ __global__ void __launch_bounds__(32 * kWarps) dense_kernel(const uint8_t* __res
                 const int row = r0 + r;
                 if (row >= n_out) break;
                 float w[8];
-                lane_w<CODE>(W + rb * row, sb, lane, w);
+                lane_w<CODE>(W + rb * row, sb, lane, w, q6s);
 #pragma unroll
                 for (int j = 0; j < kCT; j++)
 #pragma unroll
@@ -361,59 +363,51 @@ __global__ void __launch_bounds__(32 * kWarps) dense_kernel(const uint8_t* __res
 }
 
 static void dense_launch(int code, const uint8_t* W, const float* X, int T, int n_out, int n_in, long x_stride,
-                         int o0, float* Y, long y_stride, cudaStream_t s) {
+                         int o0, float* Y, long y_stride, cudaStream_t s, int q6s) {
     const int items = ((n_out - o0 + kRowsPerItem - 1) / kRowsPerItem) * ((T + kCT - 1) / kCT);
     const int grid = grid_for(items);
     if (code == DRACO_CODE_Q4_K)
-        dense_kernel<DRACO_CODE_Q4_K><<<grid, 32 * kWarps, 0, s>>>(W, X, T, n_out, n_in, x_stride, o0, Y, y_stride);
+        dense_kernel<DRACO_CODE_Q4_K><<<grid, 32 * kWarps, 0, s>>>(W, X, T, n_out, n_in, x_stride, o0, Y, y_stride, q6s);
     else if (code == DRACO_CODE_Q6_K)
-        dense_kernel<DRACO_CODE_Q6_K><<<grid, 32 * kWarps, 0, s>>>(W, X, T, n_out, n_in, x_stride, o0, Y, y_stride);
+        dense_kernel<DRACO_CODE_Q6_K><<<grid, 32 * kWarps, 0, s>>>(W, X, T, n_out, n_in, x_stride, o0, Y, y_stride, q6s);
     else
-        dense_kernel<DRACO_CODE_Q8_0><<<grid, 32 * kWarps, 0, s>>>(W, X, T, n_out, n_in, x_stride, o0, Y, y_stride);
+        dense_kernel<DRACO_CODE_Q8_0><<<grid, 32 * kWarps, 0, s>>>(W, X, T, n_out, n_in, x_stride, o0, Y, y_stride, q6s);
 }
 
 void launch_gemv_rows(int code, const uint8_t* W, const float* x, int n_in, int o0, int o1, float* y,
-                      cudaStream_t s) {
-    if (o1 > o0) dense_launch(code, W, x, 1, o1, n_in, n_in, o0, y, o1, s);
+                      cudaStream_t s, int q6s) {
+    if (o1 > o0) dense_launch(code, W, x, 1, o1, n_in, n_in, o0, y, o1, s, q6s);
 }
 
 void launch_gemm_dense(int code, const uint8_t* W, const float* X, int T, int n_out, int n_in, float* Y,
-                       cudaStream_t s) {
-    dense_launch(code, W, X, T, n_out, n_in, n_in, 0, Y, n_out, s);
-}
-
-// multi-expert gemv: one dense launch per selected expert (y_e = W_{idx[e]} x_e)
-void launch_gemvn(int code, const uint8_t* W, const int* idx_host, long per, const float* x, long x_stride,
-                  int n_out_e, int n_in, int n_exp, float* y, cudaStream_t s) {
-    for (int e = 0; e < n_exp; e++)
-        dense_launch(code, W + (size_t)idx_host[e] * per, x + (size_t)e * x_stride, 1, n_out_e, n_in, n_in, 0,
-                     y + (size_t)e * n_out_e, n_out_e, s);
+                       cudaStream_t s, int q6s) {
+    dense_launch(code, W, X, T, n_out, n_in, n_in, 0, Y, n_out, s, q6s);
 }
 
 // ------------------------------------------------------------------------------------------
 // dequantise rows to fp32
 // ------------------------------------------------------------------------------------------
 template <int CODE>
-__global__ void dequant_kernel(const uint8_t* __restrict__ W, int rows, int n_in, float* __restrict__ out) {
+__global__ void dequant_kernel(const uint8_t* __restrict__ W, int rows, int n_in, float* __restrict__ out, int q6s) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int nwarps = (gridDim.x * blockDim.x) >> 5;
-    const size_t rb = row_bytes(CODE, n_in);
+    const size_t rb = row_bytes(CODE, n_in, q6s);
     const int steps = n_steps(n_in);
     for (int it = warp; it < rows * steps; it += nwarps) {
         const int r = it / steps, sb = it % steps;
         if (!lane_live<CODE>(sb, lane, n_in)) continue;
         float w[8];
-        lane_w<CODE>(W + rb * r, sb, lane, w);
+        lane_w<CODE>(W + rb * r, sb, lane, w, q6s);
 #pragma unroll
         for (int j = 0; j < 8; j++) out[(size_t)r * n_in + sb * 256 + lane_pos<CODE>(lane, j)] = w[j];
     }
 }
 
-void launch_dequant(int code, const uint8_t* W, int rows, int n_in, float* out, cudaStream_t s) {
+void launch_dequant(int code, const uint8_t* W, int rows, int n_in, float* out, cudaStream_t s, int q6s) {
     const int grid = max(1, min(148 * 4, (rows * ((n_in + 255) / 256) + 7) / 8));
-    if (code == DRACO_CODE_Q4_K) dequant_kernel<DRACO_CODE_Q4_K><<<grid, 256, 0, s>>>(W, rows, n_in, out);
-    else if (code == DRACO_CODE_Q6_K) dequant_kernel<DRACO_CODE_Q6_K><<<grid, 256, 0, s>>>(W, rows, n_in, out);
-    else dequant_kernel<DRACO_CODE_Q8_0><<<grid, 256, 0, s>>>(W, rows, n_in, out);
+    if (code == DRACO_CODE_Q4_K) dequant_kernel<DRACO_CODE_Q4_K><<<grid, 256, 0, s>>>(W, rows, n_in, out, q6s);
+    else if (code == DRACO_CODE_Q6_K) dequant_kernel<DRACO_CODE_Q6_K><<<grid, 256, 0, s>>>(W, rows, n_in, out, q6s);
+    else dequant_kernel<DRACO_CODE_Q8_0><<<grid, 256, 0, s>>>(W, rows, n_in, out, q6s);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -466,6 +460,31 @@ __global__ void shexp_gate_kernel(const float* __restrict__ x, const float* __re
 void launch_shexp_gate(const float* x, const float* gw, int h, const float* y, float* sg, float* out, int T,
                        cudaStream_t s) {
     shexp_gate_kernel<<<T, 256, 0, s>>>(x, gw, h, y, sg, out);
+}
+
+// ------------------------------------------------------------------------------------------
+// Q6_K copies with 224-byte superblocks: src holds n_mats matrices of rows x nb superblocks of
+// 210 B (src_per bytes apart); dst gets them densely with every superblock padded to 224 B
+// (pad bytes zero).  One warp per superblock, u16 copies (GGUF superblocks are 2-aligned).
+// ------------------------------------------------------------------------------------------
+__global__ void q6_pad_kernel(const uint8_t* __restrict__ src, size_t src_per, int n_mats, int rows, int nb,
+                              uint8_t* __restrict__ dst) {
+    const int lane = threadIdx.x & 31;
+    const long total = (long)n_mats * rows * nb;
+    const long nw = ((long)gridDim.x * blockDim.x) >> 5;
+    for (long b = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < total; b += nw) {
+        const long mat = b / ((long)rows * nb), rem = b % ((long)rows * nb);
+        const unsigned short* s16 =
+            reinterpret_cast<const unsigned short*>(src + (size_t)mat * src_per + (size_t)rem * kQ6File);
+        unsigned short* d16 = reinterpret_cast<unsigned short*>(dst + (size_t)b * kQ6Padded);
+        for (int i = lane; i < kQ6Padded / 2; i += 32) d16[i] = i < kQ6File / 2 ? s16[i] : (unsigned short)0;
+    }
+}
+
+void launch_q6_pad(const uint8_t* src, size_t src_per, int n_mats, int rows, int nb, uint8_t* dst, cudaStream_t s) {
+    const long total = (long)n_mats * rows * nb;
+    const int grid = (int)std::min<long>(148L * 16, (total + 7) / 8);
+    q6_pad_kernel<<<grid > 0 ? grid : 1, 256, 0, s>>>(src, src_per, n_mats, rows, nb, dst);
 }
 
 }  // namespace draco

@@ -42,26 +42,26 @@ void launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s);
 // cg/cu: uniform format codes of the gate and up matrices.
 void launch_gateup_codes(const ExpertTable& tab, int cg, int cu, const int* active, const int* n_active,
                          int n_active_max, const int* off, const int* ilist, int tok_div, const float* X,
-                         int inter, int n_in, float* act, cudaStream_t s);
+                         int inter, int n_in, float* act, cudaStream_t s, int q6s);
 // down over grouped assignments: y[p][r] = dot(down_e row r, act[p])
 void launch_down_code(const ExpertTable& tab, int cd, const int* active, const int* n_active,
                       int n_active_max, const int* off, const float* act, int inter, int n_out, float* y,
-                      cudaStream_t s);
+                      cudaStream_t s, int q6s);
 // out[t][r] = sum_k w[t,k] * y[pos_of[t*K+k]][r] (k ascending, fused multiply-add),
 // then + shared[t][r] when shared != nullptr
 void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T,
                     int K, int E, int n_out, const float* shared, float* out, cudaStream_t s);
 // rows y[r] = dot(W row r, x) for r in [o0, o1), any supported code, one vector
 void launch_gemv_rows(int code, const uint8_t* W, const float* x, int n_in, int o0, int o1, float* y,
-                      cudaStream_t s);
+                      cudaStream_t s, int q6s);
 // Y[t][r] = dot(W row r, X[t]) for a dense token batch (m5_gemm semantics)
 void launch_gemm_dense(int code, const uint8_t* W, const float* X, int T, int n_out, int n_in,
-                       float* Y, cudaStream_t s);
-// multi-expert gemv (m5_gemvn semantics): y[e][o] = dot(W + idx[e]*per row o, x + e*x_stride)
-void launch_gemvn(int code, const uint8_t* W, const int* idx_host, long per, const float* x, long x_stride,
-                  int n_out_e, int n_in, int n_exp, float* y, cudaStream_t s);
+                       float* Y, cudaStream_t s, int q6s);
 // dequantise rows to fp32
-void launch_dequant(int code, const uint8_t* W, int rows, int n_in, float* out, cudaStream_t s);
+void launch_dequant(int code, const uint8_t* W, int rows, int n_in, float* out, cudaStream_t s, int q6s);
+// repack Q6_K matrices from 210-byte to 224-byte superblocks (registry copies)
+void launch_q6_pad(const uint8_t* src, size_t src_per, int n_mats, int rows, int nb, uint8_t* dst,
+                   cudaStream_t s);
 // out[i] = y[i] * sigmoid(dot(gw, x)) for the scalar-gated shared expert; writes the gate
 // logit to sg
 void launch_shexp_gate(const float* x, const float* gw, int h, const float* y, float* sg, float* out,
@@ -75,13 +75,13 @@ void launch_q8k_quantize(const float* x, int rows, int n, float* d, int8_t* q, i
 // integer superblock dots of W rows with one Q8_K vector: Q4_K -> (isc, imn) pairs,
 // Q6_K -> isum (second entry 0)
 void launch_q8k_block_dots(int code, const uint8_t* W, int rows, int n_in, const int8_t* q,
-                           const int16_t* bsums, int32_t* out2, cudaStream_t s);
+                           const int16_t* bsums, int32_t* out2, cudaStream_t s, int q6s);
 // gate/up over grouped assignments with Q8_K activations (xq/xd/xbs: per token row)
 void launch_gateup_q8k(const ExpertTable& tab, int cg, const int* active, const int* n_active,
                        int n_active_max, const int* off, const int* ilist, int tok_div,
                        const int8_t* xq, const float* xd, const int16_t* xbs, int inter, int n_in,
-                       float* act, cudaStream_t s);
+                       float* act, cudaStream_t s, int q6s);
 void launch_gemv_q8k(int code, const uint8_t* W, int rows, int n_in, const int8_t* q, const float* d,
-                     const int16_t* bsums, float* y, cudaStream_t s);
+                     const int16_t* bsums, float* y, cudaStream_t s, int q6s);
 
 }  // namespace draco

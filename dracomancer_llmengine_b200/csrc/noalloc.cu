@@ -127,8 +127,8 @@ extern "C" int draco_b200_moe_tok_noalloc(const float* X, const int* order, cons
     ExpertTable et{(const uint8_t* const*)d_ptrs};
     const int na_max = n_exp < T * n_used ? n_exp : T * n_used;
     launch_gateup_codes(et, cg, cu, rb.active, rb.n_active, na_max, rb.off, rb.ilist, n_used, X, inter, n_in, act,
-                        s);
-    launch_down_code(et, cd, rb.active, rb.n_active, na_max, rb.off, act, inter, n_out, y, s);
+                        s, kQ6File);
+    launch_down_code(et, cd, rb.active, rb.n_active, na_max, rb.off, act, inter, n_out, y, s, kQ6File);
     launch_combine(y, order, wtop, rb.pos_of, T, n_used, n_exp, n_out, nullptr, out, s);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(-3, "launch failed: ", cudaGetErrorString(e));

@@ -96,8 +96,8 @@ __device__ __forceinline__ void q4k_q8k_sb(const uint8_t* __restrict__ row, int 
 
 // isum = sum_g sc_g * sum_{k in 16-group g} (q6 - 32) * q8 for superblock sb of a Q6_K row
 __device__ __forceinline__ int q6k_q8k_sb(const uint8_t* __restrict__ row, int sb, int lane,
-                                          const int8_t* __restrict__ q8) {
-    const uint8_t* blk = row + (size_t)sb * 210;
+                                          const int8_t* __restrict__ q8, int q6s) {
+    const uint8_t* blk = row + (size_t)sb * q6s;
     const int h = lane >> 4, kk = 2 * (lane & 15);
     const uint32_t qlA = (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(blk + h * 64 + kk));
     const uint32_t qlB = (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(blk + h * 64 + 32 + kk));
@@ -122,16 +122,16 @@ __device__ __forceinline__ int q6k_q8k_sb(const uint8_t* __restrict__ row, int s
 
 __global__ void q8k_block_dots_kernel(int code, const uint8_t* __restrict__ W, int rows, int n_in,
                                       const int8_t* __restrict__ q, const int16_t* __restrict__ bs,
-                                      int32_t* __restrict__ out2) {
+                                      int32_t* __restrict__ out2, int q6s) {
     const int lane = threadIdx.x & 31;
     const int nb = n_in / 256;
     const int nw = (gridDim.x * blockDim.x) >> 5;
-    const size_t rb = row_bytes(code, n_in);
+    const size_t rb = row_bytes(code, n_in, q6s);
     for (int it = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; it < rows * nb; it += nw) {
         const int r = it / nb, sb = it % nb;
         int a, m = 0;
         if (code == DRACO_CODE_Q4_K) q4k_q8k_sb(W + rb * r, sb, lane, q, bs, a, m);
-        else a = q6k_q8k_sb(W + rb * r, sb, lane, q);
+        else a = q6k_q8k_sb(W + rb * r, sb, lane, q, q6s);
         if (lane == 0) {
             out2[(size_t)it * 2] = a;
             out2[(size_t)it * 2 + 1] = m;
@@ -140,16 +140,17 @@ __global__ void q8k_block_dots_kernel(int code, const uint8_t* __restrict__ W, i
 }
 
 void launch_q8k_block_dots(int code, const uint8_t* W, int rows, int n_in, const int8_t* q, const int16_t* bsums,
-                           int32_t* out2, cudaStream_t s) {
+                           int32_t* out2, cudaStream_t s, int q6s) {
     const int items = rows * (n_in / 256);
-    q8k_block_dots_kernel<<<max(1, min(148 * 8, (items + 7) / 8)), 256, 0, s>>>(code, W, rows, n_in, q, bsums, out2);
+    q8k_block_dots_kernel<<<max(1, min(148 * 8, (items + 7) / 8)), 256, 0, s>>>(code, W, rows, n_in, q, bsums, out2,
+                                                                                q6s);
 }
 
 // row dot in Q8_K mode, float combination in superblock order (the order of orc_gemv_q8k)
 template <int CODE>
 __device__ __forceinline__ float q8k_row_dot(const uint8_t* __restrict__ row, int nb, int lane,
                                              const int8_t* __restrict__ q, const float* __restrict__ d8,
-                                             const int16_t* __restrict__ bs) {
+                                             const int16_t* __restrict__ bs, int q6s) {
     float dot = 0.f;
     for (int sb = 0; sb < nb; sb++) {
         if (CODE == DRACO_CODE_Q4_K) {
@@ -160,8 +161,8 @@ __device__ __forceinline__ float q8k_row_dot(const uint8_t* __restrict__ row, in
             const float v = fmaf(d, (float)isc, -__fmul_rn(dmin, (float)imn));
             dot = fmaf(d8[sb], v, dot);
         } else {
-            const int is = q6k_q8k_sb(row, sb, lane, q);
-            const float d6 = h2f(__ldg(reinterpret_cast<const unsigned short*>(row + (size_t)sb * 210 + 208)));
+            const int is = q6k_q8k_sb(row, sb, lane, q, q6s);
+            const float d6 = h2f(__ldg(reinterpret_cast<const unsigned short*>(row + (size_t)sb * q6s + 208)));
             dot = fmaf(__fmul_rn(d8[sb], d6), (float)is, dot);
         }
     }
@@ -170,21 +171,24 @@ __device__ __forceinline__ float q8k_row_dot(const uint8_t* __restrict__ row, in
 
 template <int CODE>
 __global__ void gemv_q8k_kernel(const uint8_t* __restrict__ W, int rows, int n_in, const int8_t* __restrict__ q,
-                                const float* __restrict__ d, const int16_t* __restrict__ bs, float* __restrict__ y) {
+                                const float* __restrict__ d, const int16_t* __restrict__ bs, float* __restrict__ y,
+                                int q6s) {
     const int lane = threadIdx.x & 31;
     const int nw = (gridDim.x * blockDim.x) >> 5;
-    const size_t rb = row_bytes(CODE, n_in);
+    const size_t rb = row_bytes(CODE, n_in, q6s);
     for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += nw) {
-        const float v = q8k_row_dot<CODE>(W + rb * r, n_in / 256, lane, q, d, bs);
+        const float v = q8k_row_dot<CODE>(W + rb * r, n_in / 256, lane, q, d, bs, q6s);
         if (lane == 0) y[r] = v;
     }
 }
 
 void launch_gemv_q8k(int code, const uint8_t* W, int rows, int n_in, const int8_t* q, const float* d,
-                     const int16_t* bsums, float* y, cudaStream_t s) {
+                     const int16_t* bsums, float* y, cudaStream_t s, int q6s) {
     const int grid = max(1, min(148 * 8, (rows + 7) / 8));
-    if (code == DRACO_CODE_Q4_K) gemv_q8k_kernel<DRACO_CODE_Q4_K><<<grid, 256, 0, s>>>(W, rows, n_in, q, d, bsums, y);
-    else gemv_q8k_kernel<DRACO_CODE_Q6_K><<<grid, 256, 0, s>>>(W, rows, n_in, q, d, bsums, y);
+    if (code == DRACO_CODE_Q4_K)
+        gemv_q8k_kernel<DRACO_CODE_Q4_K><<<grid, 256, 0, s>>>(W, rows, n_in, q, d, bsums, y, q6s);
+    else
+        gemv_q8k_kernel<DRACO_CODE_Q6_K><<<grid, 256, 0, s>>>(W, rows, n_in, q, d, bsums, y, q6s);
 }
 
 // grouped gate/up + SwiGLU with Q8_K activations of the assignment's token
@@ -192,13 +196,14 @@ template <int CG, int CU>
 __global__ void gateup_q8k_kernel(ExpertTable tab, const int* __restrict__ active, const int* __restrict__ n_active_p,
                                   const int* __restrict__ off, const int* __restrict__ ilist, int tok_div,
                                   const int8_t* __restrict__ xq, const float* __restrict__ xd,
-                                  const int16_t* __restrict__ xbs, int inter, int n_in, float* __restrict__ act) {
+                                  const int16_t* __restrict__ xbs, int inter, int n_in, float* __restrict__ act,
+                                  int q6s) {
     const int n_active = *n_active_p;
     constexpr int kRows = 8;   // one warp per row, 8 warps per item
     const int nrb = (inter + kRows - 1) / kRows;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = n_in / 256;
-    const size_t rbg = row_bytes(CG, n_in), rbu = row_bytes(CU, n_in);
+    const size_t rbg = row_bytes(CG, n_in, q6s), rbu = row_bytes(CU, n_in, q6s);
     for (int item = blockIdx.x; item < n_active * nrb; item += gridDim.x) {
         const int a = item / nrb, rbi = item % nrb;
         const int e = active[a];
@@ -212,8 +217,8 @@ __global__ void gateup_q8k_kernel(ExpertTable tab, const int* __restrict__ activ
             const int8_t* q = xq + (size_t)t * n_in;
             const float* d = xd + (size_t)t * nb;
             const int16_t* bs = xbs + (size_t)t * nb * 16;
-            const float g = q8k_row_dot<CG>(G, nb, lane, q, d, bs);
-            const float u = q8k_row_dot<CU>(U, nb, lane, q, d, bs);
+            const float g = q8k_row_dot<CG>(G, nb, lane, q, d, bs, q6s);
+            const float u = q8k_row_dot<CU>(U, nb, lane, q, d, bs, q6s);
             if (lane == 0) act[(size_t)(p0 + j) * inter + row] = silu_mul(g, u);
         }
     }
@@ -221,14 +226,14 @@ __global__ void gateup_q8k_kernel(ExpertTable tab, const int* __restrict__ activ
 
 void launch_gateup_q8k(const ExpertTable& tab, int cg, const int* active, const int* n_active, int n_active_max,
                        const int* off, const int* ilist, int tok_div, const int8_t* xq, const float* xd,
-                       const int16_t* xbs, int inter, int n_in, float* act, cudaStream_t s) {
+                       const int16_t* xbs, int inter, int n_in, float* act, cudaStream_t s, int q6s) {
     const int grid = max(1, min(148 * 8, n_active_max * ((inter + 7) / 8)));
     if (cg == DRACO_CODE_Q4_K)
         gateup_q8k_kernel<DRACO_CODE_Q4_K, DRACO_CODE_Q4_K><<<grid, 256, 0, s>>>(tab, active, n_active, off, ilist,
-                                                                                 tok_div, xq, xd, xbs, inter, n_in, act);
+                                                                                 tok_div, xq, xd, xbs, inter, n_in, act, q6s);
     else
         gateup_q8k_kernel<DRACO_CODE_Q6_K, DRACO_CODE_Q6_K><<<grid, 256, 0, s>>>(tab, active, n_active, off, ilist,
-                                                                                 tok_div, xq, xd, xbs, inter, n_in, act);
+                                                                                 tok_div, xq, xd, xbs, inter, n_in, act, q6s);
 }
 
 }  // namespace draco

@@ -1,0 +1,623 @@
+// Grouped expert GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulators, TMA).
+//
+// One work item = (expert e, 128-row tile of its weight matrix, up to 128 of its tokens in
+// expert-sorted order).  Per item the CTA computes D[row][tok] = sum_k W[row][k] * B[tok][k]
+// with K = the matrix row length:
+//   gate/up mode: two matrices (gate, up) share B = the tokens' activations; the epilogue writes
+//                 act = silu(gate) * up as fp16, the B operand of the down GEMM;
+//   down mode:    one matrix, B = act; the epilogue writes y (fp32) for the combine.
+//
+// Data path per 256-value superblock column of a matrix:
+//   TMA (no multicast) copies the 128 rows' raw superblocks (Q4_K 144 B, Q6_K 224 B padded)
+//   into a shared-memory ring -> 16 dequant warps (4 warpgroups, thread = weight row) decode
+//   64 values at a time to fp16 in registers and store them into TMEM (tcgen05.st), where
+//   they are the MMA's A operand -> one elected thread issues tcgen05.mma.kind::f16 with the
+//   activations' fp16 tile (TMA, 128-byte swizzle) as the B operand and fp32 accumulators in
+//   TMEM -> the dequant warps read the accumulators back (tcgen05.ld) for the epilogue.
+// Every wait on an mbarrier is bounded; on a timeout the CTA records an error code, stops
+// issuing work, drains what it issued and frees its TMEM.
+//
+// Weights are decoded as the reference decodes them (src/m5_kern_scalar.c:69-142) in fp32 and
+// rounded once to fp16; activations are rounded to fp16; accumulation is fp32.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "kernels.cuh"
+#include "tc_gemm.cuh"
+
+#include <cstdio>
+
+namespace draco {
+namespace tc {
+
+constexpr int kDeqWarps = 16;                 // 4 warpgroups
+constexpr int kProdWarp = 16;                 // TMA producer
+constexpr int kMmaWarp = 17;                  // MMA issuer, TMEM owner
+constexpr int kThreads = 32 * 18;
+constexpr int kRawStages = 4;                 // raw superblock-column stages (one matrix each)
+constexpr int kBStages = 4;                   // k64 activation stages
+constexpr int kASlots = 8;                    // k64 A slots in TMEM
+constexpr int kBStageBytes = 128 * 128;       // 128 tokens x 64 halves
+constexpr int kTmemCols = 512;
+constexpr int kAccCols = 128;                 // per accumulator (N <= 128)
+constexpr int kABase = 256;                   // A slots start here (after 2 accumulators)
+constexpr long kSpinLimit = 1L << 23;         // bounded waits (~seconds)
+
+// error codes written to *err
+constexpr int kErrTimeout = 0x100;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: returns false (and raises the CTA's abort flag) on timeout or when another
+// role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int where) {
+    for (long i = 0; i < kSpinLimit; i++) {
+        if (mbar_try(bar, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    *abort_flag = 1;
+    atomicOr(err, kErrTimeout | where);
+    return false;
+}
+
+// ---------------------------------------------------------------- TMA
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16, fp32 accumulate
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]),
+        "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]),
+        "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// instruction descriptor: D fp32, A/B fp16, both K-major, M = 128, N = n
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+// shared-memory descriptor of a K-major, 128-byte-swizzled operand tile (rows of 128 B,
+// 8-row atoms of 1024 B stacked densely): start >> 4, LBO 16 B, SBO 1024 B, version 1, SW128
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// ---------------------------------------------------------------- dequantisation (fp32 -> fp16)
+// float 2 + q/64 from a byte q (0..63) placed in bits 16..23 under exponent byte 0x40: one PRMT
+__device__ __forceinline__ float q_as_float(uint32_t bytes4, int i) {
+    // selector nibbles (low to high): y.b0, y.b0, x.b_i, y.b3 -> bytes (0, 0, q, 0x40)
+    const uint32_t sel = 0x7044u | ((uint32_t)i << 8);
+    return __uint_as_float(__byte_perm(bytes4, 0x40000000u, sel));
+}
+// value = scale * q - offset computed as fma(2 + q/64, 64 * scale, -(128 * scale + offset))
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Q4_K: 64 values [64*kc, 64*kc+64) of one superblock row -> 32 packed fp16 pairs
+__device__ __forceinline__ void deq_q4k(const uint8_t* blk, int kc, uint32_t (&out)[32]) {
+    const uint4 hd = *reinterpret_cast<const uint4*>(blk);
+    const float d = h2f((uint16_t)(hd.x & 0xffff)), dmin = h2f((uint16_t)(hd.x >> 16));
+    uint8_t s12[12];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        s12[i] = (uint8_t)(hd.y >> (8 * i));
+        s12[4 + i] = (uint8_t)(hd.z >> (8 * i));
+        s12[8 + i] = (uint8_t)(hd.w >> (8 * i));
+    }
+    int sc0, m0, sc1, m1;
+    q4k_sm(s12, 2 * kc, sc0, m0);
+    q4k_sm(s12, 2 * kc + 1, sc1, m1);
+    const float ds0 = d * (float)sc0, dm0 = dmin * (float)m0;
+    const float ds1 = d * (float)sc1, dm1 = dmin * (float)m1;
+    const float a0 = 64.f * ds0, b0 = -(128.f * ds0 + dm0);
+    const float a1 = 64.f * ds1, b1 = -(128.f * ds1 + dm1);
+    const uint4* qv = reinterpret_cast<const uint4*>(blk + 16 + 32 * kc);
+    const uint4 q0 = qv[0], q1 = qv[1];
+    const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        const uint32_t lo = words[w] & 0x0F0F0F0Fu, hi = (words[w] >> 4) & 0x0F0F0F0Fu;
+        // low nibbles: values 4w..4w+3 of sub-block 2kc; high nibbles: of sub-block 2kc+1
+        out[2 * w] = pack2(fmaf(q_as_float(lo, 0), a0, b0), fmaf(q_as_float(lo, 1), a0, b0));
+        out[2 * w + 1] = pack2(fmaf(q_as_float(lo, 2), a0, b0), fmaf(q_as_float(lo, 3), a0, b0));
+        out[16 + 2 * w] = pack2(fmaf(q_as_float(hi, 0), a1, b1), fmaf(q_as_float(hi, 1), a1, b1));
+        out[16 + 2 * w + 1] = pack2(fmaf(q_as_float(hi, 2), a1, b1), fmaf(q_as_float(hi, 3), a1, b1));
+    }
+}
+
+// Q6_K (224-byte padded superblock): values p in [64*kc, 64*kc+64)
+//   ql byte (p>>7)*64 + (p&63), high nibble if (p>>6)&1; qh byte (p>>7)*32 + (p&31), shift
+//   ((p>>5)&3)*2; scale sc[p>>4]; w = d * sc * (q - 32)   (src/m5_kern_scalar.c:115-142)
+__device__ __forceinline__ void deq_q6k(const uint8_t* blk, int kc, uint32_t (&out)[32]) {
+    const int h = kc >> 1, nhi = kc & 1;
+    const uint4* qlv = reinterpret_cast<const uint4*>(blk + h * 64);
+    const uint4* qhv = reinterpret_cast<const uint4*>(blk + 128 + h * 32);
+    const uint4 l0 = qlv[0], l1 = qlv[1], l2 = qlv[2], l3 = qlv[3];
+    const uint4 g0 = qhv[0], g1 = qhv[1];
+    const uint32_t ql[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w,
+                             l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
+    const uint32_t qh[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const uint32_t scw = *reinterpret_cast<const uint32_t*>(blk + 192 + 4 * kc);
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(blk + 208));
+    // 4 groups of 16 values: group g covers p = 64kc + 16g .. +16, scale sc[4kc + g]
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+        const float ds = d * (float)(int8_t)(scw >> (8 * g));
+        const float a = 64.f * ds, b = -(128.f * ds + 32.f * ds);
+        // p & 63 = 16g' with g' = g (within the 64-value half chosen by nhi) ... p = 64kc + 16g + i
+        // ql index (p & 63) = 16*(g) + i  (bytes 16g .. 16g+15 of this half's 64 ql bytes)
+        // qh index (p & 31) = 16*(g & 1) + i, shift = ((p >> 5) & 3) * 2 = (2*nhi + (g >> 1)) * 2
+        const int shift = (2 * nhi + (g >> 1)) * 2;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const uint32_t lw = ql[4 * g + w];
+            const uint32_t nib = nhi ? ((lw >> 4) & 0x0F0F0F0Fu) : (lw & 0x0F0F0F0Fu);
+            const uint32_t hw = qh[4 * (g & 1) + w];
+            const uint32_t two = (hw >> shift) & 0x03030303u;
+            const uint32_t q6 = nib | (two << 4);
+            out[8 * g + 2 * w] = pack2(fmaf(q_as_float(q6, 0), a, b), fmaf(q_as_float(q6, 1), a, b));
+            out[8 * g + 2 * w + 1] = pack2(fmaf(q_as_float(q6, 2), a, b), fmaf(q_as_float(q6, 3), a, b));
+        }
+    }
+}
+
+// ---------------------------------------------------------------- the kernel
+struct SmemLayout {
+    static constexpr int raw_bytes(int bb) { return kRawStages * 128 * bb; }
+};
+
+template <int MODE, int CODE>
+struct Cfg {
+    static constexpr int kMats = MODE == 0 ? 2 : 1;
+    static constexpr int kBB = CODE == DRACO_CODE_Q4_K ? 144 : kQ6Padded;   // raw bytes per row superblock
+    static constexpr int kRawStage = 128 * kBB;
+    // raw stage consumers: gate/up -> 2 warpgroups x 4 warps; down -> 4 x 4
+    static constexpr int kRawConsumers = MODE == 0 ? 8 : 16;
+    static constexpr int kBOff = kRawStages * kRawStage;                 // 1024-aligned below
+    static constexpr int kBOffAligned = (kBOff + 1023) / 1024 * 1024;
+    static constexpr int kBarOff = kBOffAligned + kBStages * kBStageBytes;
+    static constexpr int kSmem = kBarOff + 1024 + 1024;                    // barriers + alignment slack
+};
+
+struct Bars {
+    uint64_t raw_full[kRawStages], raw_empty[kRawStages];
+    uint64_t b_full[kBStages], b_empty[kBStages];
+    uint64_t a_full[kASlots], a_empty[kASlots];
+    uint64_t acc_full, acc_empty, drain;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+template <int MODE, int CODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
+                  const __grid_constant__ CUtensorMap tmB, const int4* __restrict__ items,
+                  const int* __restrict__ n_items_p, int rows_per_expert, int K, int out_ld,
+                  __half* __restrict__ act_out, float* __restrict__ y_out, int* __restrict__ err) {
+    using C = Cfg<MODE, CODE>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-align the dynamic shared memory base (swizzled tiles need it)
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* raw = smem;
+    uint8_t* bt = smem + C::kBOffAligned;
+    Bars* bars = reinterpret_cast<Bars*>(smem + C::kBarOff);
+    volatile int* abort_flag = &bars->abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_items = *n_items_p;
+    const int nb = K / 256;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRawStages; i++) {
+            mbar_init(&bars->raw_full[i], 1);
+            mbar_init(&bars->raw_empty[i], C::kRawConsumers);
+        }
+        for (int i = 0; i < kBStages; i++) {
+            mbar_init(&bars->b_full[i], 1);
+            mbar_init(&bars->b_empty[i], 1);
+        }
+        for (int i = 0; i < kASlots; i++) {
+            mbar_init(&bars->a_full[i], 4);
+            mbar_init(&bars->a_empty[i], 1);
+        }
+        mbar_init(&bars->acc_full, 1);
+        mbar_init(&bars->acc_empty, kDeqWarps);
+        mbar_init(&bars->drain, 1);
+        bars->abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&bars->tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == kProdWarp) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t rq = 0, bq = 0;   // fills issued so far (raw, B)
+            for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
+                const int4 item = items[it];
+                const int e = item.x, mt = item.y, p0 = item.z, ntok = item.w;
+                const int nbox = (ntok + 15) >> 4;
+                const int arow = e * rows_per_expert + mt * 128;
+                for (int sb = 0; sb < nb && !*abort_flag; sb++) {
+                    for (int m = 0; m < C::kMats; m++, rq++) {
+                        const int s = rq % kRawStages;
+                        if (!mbar_wait(&bars->raw_empty[s], ((rq / kRawStages) & 1) ^ 1, abort_flag, err, 1)) break;
+                        mbar_expect_tx(&bars->raw_full[s], C::kRawStage);
+                        tma_load_2d(raw + s * C::kRawStage, m == 0 ? &tmA0 : &tmA1, sb * (C::kBB / 4), arow,
+                                    &bars->raw_full[s]);
+                    }
+                    for (int kc = 0; kc < 4; kc++, bq++) {
+                        const int s = bq % kBStages;
+                        if (!mbar_wait(&bars->b_empty[s], ((bq / kBStages) & 1) ^ 1, abort_flag, err, 2)) break;
+                        mbar_expect_tx(&bars->b_full[s], nbox * 16 * 128);
+                        for (int j = 0; j < nbox; j++)
+                            tma_load_2d(bt + s * kBStageBytes + j * 2048, &tmB, sb * 256 + kc * 64, p0 + 16 * j,
+                                        &bars->b_full[s]);
+                    }
+                }
+            }
+            if (*abort_flag) {
+                // drain: wait (bounded) for the most recent fills to land before the CTA exits
+                for (uint32_t k = 0; k < kRawStages && k < rq; k++) {
+                    const uint32_t q = rq - 1 - k;
+                    for (long i = 0; i < kSpinLimit / 16 && !mbar_try(&bars->raw_full[q % kRawStages],
+                                                                      (q / kRawStages) & 1); i++) {
+                    }
+                }
+                for (uint32_t k = 0; k < kBStages && k < bq; k++) {
+                    const uint32_t q = bq - 1 - k;
+                    for (long i = 0; i < kSpinLimit / 16 && !mbar_try(&bars->b_full[q % kBStages],
+                                                                      (q / kBStages) & 1); i++) {
+                    }
+                }
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t u = 0, bq = 0, n_done = 0;
+            bool ok = true;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, n_done++) {
+                const int4 item = items[it];
+                const int ntok = item.w;
+                const int nmma = ((ntok + 15) >> 4) << 4;
+                const uint32_t idesc = idesc_f16(nmma);
+                if (n_done > 0) {
+                    // the epilogue of the previous item must have read the accumulators
+                    if (!(ok = mbar_wait(&bars->acc_empty, (n_done - 1) & 1, abort_flag, err, 3))) break;
+                    tc_fence_after();
+                }
+                for (int sb = 0; sb < nb && ok; sb++) {
+                    for (int kc = 0; kc < 4 && ok; kc++, bq++) {
+                        const int bs = bq % kBStages;
+                        if (!(ok = mbar_wait(&bars->b_full[bs], (bq / kBStages) & 1, abort_flag, err, 4))) break;
+                        const uint32_t b_addr = smem_u32(bt + bs * kBStageBytes);
+                        for (int m = 0; m < C::kMats; m++, u++) {
+                            const int as = u % kASlots;
+                            if (!(ok = mbar_wait(&bars->a_full[as], (u / kASlots) & 1, abort_flag, err, 5))) break;
+                            tc_fence_after();
+                            const uint32_t a_tm = tmem + kABase + 32 * as;
+                            const uint32_t d_tm = tmem + m * kAccCols;
+#pragma unroll
+                            for (int j = 0; j < 4; j++)
+                                tc_mma_ts(d_tm, a_tm + 8 * j, sdesc_sw128(b_addr + 32 * j), idesc,
+                                          (sb | kc | j) != 0 ? 1u : 0u);
+                            tc_commit(&bars->a_empty[as]);
+                        }
+                        if (ok) tc_commit(&bars->b_empty[bs]);
+                    }
+                }
+                if (ok) tc_commit(&bars->acc_full);
+            }
+            // every issued MMA must finish before TMEM is released
+            tc_commit(&bars->drain);
+            mbar_wait(&bars->drain, 0, abort_flag, err, 6);
+        }
+    } else {
+        // ------------------------------------------------------------ dequant + epilogue
+        const int wg = warp >> 2, quarter = warp & 3;
+        const int row = quarter * 32 + lane;                         // tile row = TMEM lane
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        uint32_t u = 0, rq = 0, n_done = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, n_done++) {
+            const int4 item = items[it];
+            const int mt = item.y, p0 = item.z, ntok = item.w;
+            for (int sb = 0; sb < nb && ok; sb++) {
+                const uint32_t rq0 = rq;
+                rq += C::kMats;
+                for (int kc = 0; kc < 4 && ok; kc++) {
+                    for (int m = 0; m < C::kMats && ok; m++, u++) {
+                        if ((int)(u & 3) != wg) continue;
+                        const uint32_t q = rq0 + m;
+                        const int rs = q % kRawStages;
+                        if (!(ok = mbar_wait(&bars->raw_full[rs], (q / kRawStages) & 1, abort_flag, err, 7))) break;
+                        const int as = u % kASlots;
+                        if (!(ok = mbar_wait(&bars->a_empty[as], ((u / kASlots) & 1) ^ 1, abort_flag, err, 8))) break;
+                        tc_fence_after();
+                        uint32_t v[32];
+                        const uint8_t* blk = raw + rs * C::kRawStage + row * C::kBB;
+                        if (CODE == DRACO_CODE_Q4_K) deq_q4k(blk, kc, v);
+                        else deq_q6k(blk, kc, v);
+                        tc_st32(tmem + lane_base + kABase + 32 * as, v);
+                        tc_wait_st();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bars->a_full[as]);
+                        // last use of this raw stage by this warpgroup: release it
+                        const bool last = MODE == 0 ? (kc >= 2) : true;
+                        if (last) {
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&bars->raw_empty[rs]);
+                        }
+                    }
+                }
+            }
+            if (!ok) break;
+            // epilogue: this warpgroup's 32-token column block of the accumulators
+            if (!(ok = mbar_wait(&bars->acc_full, n_done & 1, abort_flag, err, 9))) break;
+            tc_fence_after();
+            const int t0 = wg * 32;
+            uint32_t g[32], up[32];
+            if (t0 < ntok) {
+                tc_ld32(tmem + lane_base + t0, g);
+                if (MODE == 0) tc_ld32(tmem + lane_base + kAccCols + t0, up);
+                tc_wait_ld();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->acc_empty);
+            if (t0 < ntok) {
+                const int nt = min(32, ntok - t0);
+                const int orow = mt * 128 + row;
+                if (MODE == 0) {
+                    for (int t = 0; t < nt; t++) {
+                        const float gv = __uint_as_float(g[t]), uv = __uint_as_float(up[t]);
+                        const float a = gv / (1.f + __expf(-gv)) * uv;
+                        act_out[(size_t)(p0 + t0 + t) * out_ld + orow] = __float2half_rn(a);
+                    }
+                } else {
+                    for (int t = 0; t < nt; t++) y_out[(size_t)(p0 + t0 + t) * out_ld + orow] = __uint_as_float(g[t]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------- helpers
+// work items: per active expert, token tiles of <= 128 sorted positions x 128-row weight tiles
+__global__ void build_items_kernel(const int* __restrict__ off, const int* __restrict__ active,
+                                   const int* __restrict__ n_active_p, int mtiles, int4* __restrict__ items,
+                                   int* __restrict__ n_items) {
+    __shared__ int cnt[512];
+    const int n_active = *n_active_p;
+    const int a = threadIdx.x;
+    int c = 0, e = 0;
+    if (a < n_active) {
+        e = active[a];
+        c = off[e + 1] - off[e];
+        cnt[a] = ((c + 127) / 128) * mtiles;
+    } else {
+        cnt[a] = 0;
+    }
+    __syncthreads();
+    for (int o = 1; o < 512; o <<= 1) {   // inclusive scan
+        const int v = a >= o ? cnt[a - o] : 0;
+        __syncthreads();
+        cnt[a] += v;
+        __syncthreads();
+    }
+    if (a < n_active) {
+        int k = cnt[a] - ((c + 127) / 128) * mtiles;
+        for (int nt = 0; nt * 128 < c; nt++)
+            for (int mt = 0; mt < mtiles; mt++) items[k++] = make_int4(e, mt, off[e] + nt * 128, min(128, c - nt * 128));
+    }
+    if (a == 511) *n_items = cnt[511];
+}
+
+// fp16 copy of the token rows in expert-sorted order: Xs[p] = X[ilist[p] / tok_div]
+__global__ void gather_half_kernel(const float* __restrict__ X, const int* __restrict__ ilist, int tok_div, int P,
+                                   int H, __half* __restrict__ Xs) {
+    const int per_row = H / 8;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < (long)P * per_row;
+         i += (long)gridDim.x * blockDim.x) {
+        const int p = (int)(i / per_row), c8 = (int)(i % per_row) * 8;
+        const int t = ilist ? ilist[p] / tok_div : p;
+        const float4 a = *reinterpret_cast<const float4*>(X + (size_t)t * H + c8);
+        const float4 b = *reinterpret_cast<const float4*>(X + (size_t)t * H + c8 + 4);
+        uint4 o;
+        o.x = pack2(a.x, a.y);
+        o.y = pack2(a.z, a.w);
+        o.z = pack2(b.x, b.y);
+        o.w = pack2(b.z, b.w);
+        *reinterpret_cast<uint4*>(Xs + (size_t)p * H + c8) = o;
+    }
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------------------ host side
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+bool get_encode() {
+    if (g_encode) return true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+        return false;
+    g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    return true;
+}
+
+// weights [rows_total][row_bytes] viewed as uint32 elements, box = one superblock column x 128 rows
+bool map_weights(CUtensorMap* m, const void* base, size_t rows_total, size_t row_bytes_, int bb) {
+    const cuuint64_t dims[2] = {row_bytes_ / 4, rows_total};
+    const cuuint64_t strides[1] = {row_bytes_};
+    const cuuint32_t box[2] = {(cuuint32_t)(bb / 4), 128};
+    const cuuint32_t es[2] = {1, 1};
+    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// activations [P][K] fp16, box 64 x 16 rows, 128-byte swizzle (the UMMA K-major SW128 layout)
+bool map_acts(CUtensorMap* m, const void* base, size_t P, size_t K) {
+    const cuuint64_t dims[2] = {K, P};
+    const cuuint64_t strides[1] = {K * 2};
+    const cuuint32_t box[2] = {64, 16};
+    const cuuint32_t es[2] = {1, 1};
+    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int MODE, int CODE>
+cudaError_t launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b, const int4* items,
+                      const int* n_items, int grid, int rows_per_expert, int K, int out_ld, __half* act, float* y,
+                      int* err, cudaStream_t s) {
+    using C = tc::Cfg<MODE, CODE>;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(tc::moe_tc_kernel<MODE, CODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             C::kSmem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    tc::moe_tc_kernel<MODE, CODE><<<grid, tc::kThreads, C::kSmem, s>>>(a0, a1, b, items, n_items, rows_per_expert, K,
+                                                                       out_ld, act, y, err);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tc_supported(int cg, int cu, int cd, int inter, int n_in, int n_out) {
+    auto ok = [](int c) { return c == DRACO_CODE_Q4_K || c == DRACO_CODE_Q6_K; };
+    return ok(cg) && cg == cu && ok(cd) && inter % 256 == 0 && n_in % 256 == 0 && inter % 128 == 0 &&
+           n_out % 128 == 0 && get_encode();
+}
+
+int tc_make_weight_maps(TcMaps* maps, const uint8_t* gate, const uint8_t* up, const uint8_t* down, int n_exp, int cg,
+                        int cd, int inter, int n_in, int n_out) {
+    if (!get_encode()) return -1;
+    const int bbg = cg == DRACO_CODE_Q4_K ? 144 : kQ6Padded, bbd = cd == DRACO_CODE_Q4_K ? 144 : kQ6Padded;
+    const size_t rg = (size_t)(n_in / 256) * bbg, rd = (size_t)(inter / 256) * bbd;
+    if (!map_weights(&maps->gate, gate, (size_t)n_exp * inter, rg, bbg)) return -2;
+    if (!map_weights(&maps->up, up, (size_t)n_exp * inter, rg, bbg)) return -2;
+    if (!map_weights(&maps->down, down, (size_t)n_exp * n_out, rd, bbd)) return -2;
+    return 0;
+}
+
+int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, int n_out, const float* X,
+           const int* ilist, int tok_div, int P, const int* off, const int* active, const int* n_active,
+           __half* Xs, __half* act_h, float* y, int4* items_gu, int* n_items_gu, int4* items_dn, int* n_items_dn,
+           int* err, cudaStream_t s) {
+    if (P <= 0) return 0;
+    CUtensorMap mx, ma;
+    if (!map_acts(&mx, Xs, (size_t)P, (size_t)n_in) || !map_acts(&ma, act_h, (size_t)P, (size_t)inter)) return -2;
+    tc::gather_half_kernel<<<148 * 8, 256, 0, s>>>(X, ilist, tok_div, P, n_in, Xs);
+    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, inter / 128, items_gu, n_items_gu);
+    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, n_out / 128, items_dn, n_items_dn);
+    cudaError_t e;
+    if (cg == DRACO_CODE_Q4_K)
+        e = launch_tc<0, DRACO_CODE_Q4_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, inter, n_in, inter, act_h,
+                                          nullptr, err, s);
+    else
+        e = launch_tc<0, DRACO_CODE_Q6_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, inter, n_in, inter, act_h,
+                                          nullptr, err, s);
+    if (e != cudaSuccess) return -3;
+    if (cd == DRACO_CODE_Q4_K)
+        e = launch_tc<1, DRACO_CODE_Q4_K>(maps.down, maps.down, ma, items_dn, n_items_dn, 148, n_out, inter, n_out,
+                                          nullptr, y, err, s);
+    else
+        e = launch_tc<1, DRACO_CODE_Q6_K>(maps.down, maps.down, ma, items_dn, n_items_dn, 148, n_out, inter, n_out,
+                                          nullptr, y, err, s);
+    return e == cudaSuccess ? 0 : -3;
+}
+
+}  // namespace draco
