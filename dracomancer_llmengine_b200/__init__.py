@@ -89,6 +89,7 @@ _SIGS = {
     "draco_b200_moe_forward": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, _vp, _vp], ct.c_int),
     "draco_b200_route": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, _vp], ct.c_int),
     "draco_b200_set_act_mode": ([ct.c_int], ct.c_int),
+    "draco_b200_set_gemm_path": ([ct.c_int], ct.c_int),
     "draco_b200_profile": ([ct.c_int], ct.c_int),
     "draco_b200_profile_read": ([ct.POINTER(ct.c_double), ct.POINTER(ct.c_long), ct.c_int], ct.c_int),
     "draco_b200_launch_count": ([], ct.c_long),

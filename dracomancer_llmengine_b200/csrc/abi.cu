@@ -8,6 +8,7 @@
 // once, on first use, and found again by address on later calls.
 #include "../../include/draco_moe_b200.h"
 #include "kernels.cuh"
+#include "tc_gemm.cuh"
 
 #include <algorithm>
 #include <chrono>
@@ -35,6 +36,23 @@ thread_local std::string g_err;
 std::mutex g_mu;
 int g_act_mode = 0;
 int g_moe_chunk = 64;
+// grouped GEMM path: 0 automatic, 1 CUDA cores, 2 tensor cores (where supported)
+int g_gemm_path = -1;
+int gemm_path() {
+    if (g_gemm_path < 0) {
+        const char* v = getenv("DRACO_B200_GEMM");
+        g_gemm_path = v ? atoi(v) : 0;
+    }
+    return g_gemm_path;
+}
+int tc_min_assignments() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("DRACO_B200_TC_MIN_P");
+        v = e ? atoi(e) : 128;
+    }
+    return v;
+}
 long g_launches = 0;          // kernels this library launched (all devices)
 
 // Optional per-phase device timing: CUDA events recorded around each phase on the launching
@@ -239,8 +257,14 @@ Ctx* get_ctx() {
     return g_ctx[dev];
 }
 
+void free_table(Table& t) {
+    cudaFree((void*)t.d_w);
+    delete (TcMaps*)t.tc;
+    t.tc = nullptr;
+}
+
 void drop_tables(Ctx* c) {
-    for (auto& kv : c->tables) cudaFree((void*)kv.second.d_w);
+    for (auto& kv : c->tables) free_table(kv.second);
     c->tables.clear();
     c->gen++;
 }
@@ -424,7 +448,7 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
             if (c->gen != gen0) it = c->tables.find(key);   // tables were dropped meanwhile
         }
         if (it != c->tables.end()) {
-            cudaFree((void*)it->second.d_w);
+            free_table(it->second);
             c->tables.erase(it);
         }
     }
@@ -514,6 +538,15 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
         set_err("pointer table upload failed: %s", cudaGetErrorString(cudaGetLastError()));
         return nullptr;
     }
+    // tensor-core path: stacked, densely packed copies of supported formats
+    if (t.stacked && n > 1 && tc_supported(t.cg, t.cu, t.cd, inter, n_in, n_out) &&
+        t.dev_per[0] == (size_t)inter * row_bytes(t.cg, n_in, t.q6s) &&
+        t.dev_per[1] == (size_t)inter * row_bytes(t.cu, n_in, t.q6s) &&
+        t.dev_per[2] == (size_t)n_out * row_bytes(t.cd, inter, t.q6s)) {
+        TcMaps* m = new TcMaps();
+        if (tc_make_weight_maps(m, t.base[0], t.base[1], t.base[2], n, t.cg, t.cd, inter, n_in, n_out) == 0) t.tc = m;
+        else delete m;
+    }
     auto res = c->tables.emplace(key, std::move(t));
     return &res.first->second;
 }
@@ -556,7 +589,18 @@ struct LayerBufs {
     int8_t* xq;
     float* xd;
     int16_t* xbs;
+    __half *xs_h, *act_h;          // tensor-core path operands
+    int4 *items_gu, *items_dn;
+    int *n_items, *tc_err;
+    bool use_tc = false;
 };
+
+bool want_tc(const LayerArgs& a, int T) {
+    const int mode = gemm_path();
+    if (mode == 1 || !a.tab || !a.tab->tc || g_act_mode == 1) return false;
+    if (mode == 2) return true;
+    return T * a.K >= tc_min_assignments();
+}
 
 int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
     const size_t n = (size_t)T * a.K;
@@ -572,8 +616,21 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
     const size_t o_xq = cv.take<int8_t>(q8 ? (size_t)T * a.n_in : 0);
     const size_t o_xd = cv.take<float>(q8 ? (size_t)T * (a.n_in / 256) : 0);
     const size_t o_xbs = cv.take<int16_t>(q8 ? (size_t)T * (a.n_in / 256) * 16 : 0);
+    b.use_tc = want_tc(a, T);
+    const int na_max = std::min(a.E, (int)n);
+    const size_t o_xs = cv.take<__half>(b.use_tc ? n * a.n_in : 0);
+    const size_t o_ah = cv.take<__half>(b.use_tc ? n * a.inter : 0);
+    const size_t o_igu = cv.take<int4>(b.use_tc ? tc_items_capacity((int)n, na_max, a.inter / 128) : 0);
+    const size_t o_idn = cv.take<int4>(b.use_tc ? tc_items_capacity((int)n, na_max, a.n_out / 128) : 0);
+    const size_t o_ni = cv.take<int>(2), o_terr = cv.take<int>(1);
     if (int rc = ensure_ws(c, cv.off)) return rc;
     char* w = c->ws;
+    b.xs_h = (__half*)(w + o_xs);
+    b.act_h = (__half*)(w + o_ah);
+    b.items_gu = (int4*)(w + o_igu);
+    b.items_dn = (int4*)(w + o_idn);
+    b.n_items = (int*)(w + o_ni);
+    b.tc_err = (int*)(w + o_terr);
     b.x = (float*)(w + o_x);
     b.out = (float*)(w + o_out);
     b.rb.logits = (float*)(w + o_lg);
@@ -634,6 +691,19 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     }
     ExpertTable et{a.tab->d_w};
     const int na_max = std::min(a.E, T * a.K);
+    if (b.use_tc) {
+        // tensor-core path: fp16 gather, gate/up GEMM + SwiGLU, down GEMM (gate/up phase times all)
+        PhaseScope ps(kGateUp, s);
+        CK(cudaMemsetAsync(b.tc_err, 0, sizeof(int), s));
+        const int rc = tc_run(*(const TcMaps*)a.tab->tc, a.tab->cg, a.tab->cd, a.E, a.inter, a.n_in, a.n_out, b.x,
+                              rb.ilist, a.K, T * a.K, rb.off, rb.active, rb.n_active, b.xs_h, b.act_h, b.y,
+                              b.items_gu, b.n_items, b.items_dn, b.n_items + 1, b.tc_err, s);
+        if (rc) {
+            set_err("tensor-core grouped GEMM launch failed (%d): %s", rc, cudaGetErrorString(cudaGetLastError()));
+            return -3;
+        }
+        g_launches += 5;
+    } else {
     {
         PhaseScope ps(kGateUp, s);
         if (g_act_mode == 1 && a.tab->cg == a.tab->cu &&
@@ -654,6 +724,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
                          a.tab->q6s);
         g_launches += 1;
     }
+    }
     CK(cudaGetLastError());
     if (a.sh) {
         if (int rc = dense_ffn(c, a.sh, T, b.x, a.sh_ff, a.n_in, a.n_out, b.act_sh, b.y_sh, s)) return rc;
@@ -668,9 +739,14 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
 }
 
 int check_route_err(Ctx* c, LayerBufs& b, cudaStream_t s) {
-    int h_err = 0;
+    int h_err = 0, h_tc = 0;
     CK(cudaMemcpyAsync(&h_err, b.rb.err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    if (b.use_tc) CK(cudaMemcpyAsync(&h_tc, b.tc_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
+    if (h_tc) {
+        set_err("tensor-core grouped GEMM stopped after a bounded wait ran out (code 0x%x)", h_tc);
+        return -5;
+    }
     if (h_err) {
         set_err("routing found fewer eligible experts than n_used (group limit or non-finite scores), code %d",
                 h_err);
@@ -894,7 +970,8 @@ static int moe_tok_impl(const float* X, const int* order, const float* wtop, con
     }
     if (int rc = run_layer(c, a, T, b, s)) return rc;
     if (!dev_io) CK(cudaMemcpyAsync(out, b.out, sizeof(float) * (size_t)T * n_out, cudaMemcpyDeviceToHost, s));
-    CK(cudaStreamSynchronize(s));
+    CK(cudaMemsetAsync(b.rb.err, 0, sizeof(int), s));   // routing was given: only the GEMM status counts
+    if (int rc = check_route_err(c, b, s)) return rc;
     m6_prof_t[23] += now_s() - t0;
     m6_prof_n[23]++;
     return 0;
@@ -1188,6 +1265,13 @@ int draco_b200_profile_read(double* ms, long* counts, int n) {
 long draco_b200_launch_count(void) {
     std::lock_guard<std::mutex> lk(g_mu);
     return g_launches;
+}
+
+int draco_b200_set_gemm_path(int mode) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int o = gemm_path();
+    if (mode >= 0 && mode <= 2) g_gemm_path = mode;
+    return o;
 }
 
 int draco_b200_set_act_mode(int mode) {

@@ -41,7 +41,7 @@ constexpr int kBStageBytes = 128 * 128;       // 128 tokens x 64 halves
 constexpr int kTmemCols = 512;
 constexpr int kAccCols = 128;                 // per accumulator (N <= 128)
 constexpr int kABase = 256;                   // A slots start here (after 2 accumulators)
-constexpr long kSpinLimit = 1L << 23;         // bounded waits (~seconds)
+constexpr long kSpinLimit = 1L << 21;         // bounded waits (a second or two)
 
 // error codes written to *err
 constexpr int kErrTimeout = 0x100;
@@ -81,6 +81,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     *abort_flag = 1;
     atomicOr(err, kErrTimeout | where);
     return false;
+}
+
+// The same for all 32 lanes of a warp, with a warp-uniform result (the caller goes on to
+// warp-collective tcgen05 instructions).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int where) {
+    for (long i = 0; i < kSpinLimit; i++) {
+        const bool done = mbar_try(bar, parity);
+        if (__all_sync(0xffffffffu, done)) return true;
+        if (__shfl_sync(0xffffffffu, *abort_flag, 0)) return false;
+    }
+    if ((threadIdx.x & 31) == 0) {
+        *abort_flag = 1;
+        atomicOr(err, kErrTimeout | where);
+    }
+    __syncwarp();
+    return false;
+}
+// Drain wait: bounded, does not give up early on the abort flag.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    for (long i = 0; i < kSpinLimit && !mbar_try(bar, parity); i++) {
+    }
 }
 
 // ---------------------------------------------------------------- TMA
@@ -337,15 +359,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // drain: wait (bounded) for the most recent fills to land before the CTA exits
                 for (uint32_t k = 0; k < kRawStages && k < rq; k++) {
                     const uint32_t q = rq - 1 - k;
-                    for (long i = 0; i < kSpinLimit / 16 && !mbar_try(&bars->raw_full[q % kRawStages],
-                                                                      (q / kRawStages) & 1); i++) {
-                    }
+                    mbar_drain(&bars->raw_full[q % kRawStages], (q / kRawStages) & 1);
                 }
                 for (uint32_t k = 0; k < kBStages && k < bq; k++) {
                     const uint32_t q = bq - 1 - k;
-                    for (long i = 0; i < kSpinLimit / 16 && !mbar_try(&bars->b_full[q % kBStages],
-                                                                      (q / kBStages) & 1); i++) {
-                    }
+                    mbar_drain(&bars->b_full[q % kBStages], (q / kBStages) & 1);
                 }
             }
         }
@@ -388,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // every issued MMA must finish before TMEM is released
             tc_commit(&bars->drain);
-            mbar_wait(&bars->drain, 0, abort_flag, err, 6);
+            mbar_drain(&bars->drain, 0);
         }
     } else {
         // ------------------------------------------------------------ dequant + epilogue
@@ -408,9 +426,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if ((int)(u & 3) != wg) continue;
                         const uint32_t q = rq0 + m;
                         const int rs = q % kRawStages;
-                        if (!(ok = mbar_wait(&bars->raw_full[rs], (q / kRawStages) & 1, abort_flag, err, 7))) break;
+                        if (!(ok = warp_wait(&bars->raw_full[rs], (q / kRawStages) & 1, abort_flag, err, 7))) break;
                         const int as = u % kASlots;
-                        if (!(ok = mbar_wait(&bars->a_empty[as], ((u / kASlots) & 1) ^ 1, abort_flag, err, 8))) break;
+                        if (!(ok = warp_wait(&bars->a_empty[as], ((u / kASlots) & 1) ^ 1, abort_flag, err, 8))) break;
                         tc_fence_after();
                         uint32_t v[32];
                         const uint8_t* blk = raw + rs * C::kRawStage + row * C::kBB;
@@ -432,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok) break;
             // epilogue: this warpgroup's 32-token column block of the accumulators
-            if (!(ok = mbar_wait(&bars->acc_full, n_done & 1, abort_flag, err, 9))) break;
+            if (!(ok = warp_wait(&bars->acc_full, n_done & 1, abort_flag, err, 9))) break;
             tc_fence_after();
             const int t0 = wg * 32;
             uint32_t g[32], up[32];
@@ -562,13 +580,9 @@ cudaError_t launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtens
                       const int* n_items, int grid, int rows_per_expert, int K, int out_ld, __half* act, float* y,
                       int* err, cudaStream_t s) {
     using C = tc::Cfg<MODE, CODE>;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(tc::moe_tc_kernel<MODE, CODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             C::kSmem);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    cudaError_t e = cudaFuncSetAttribute(tc::moe_tc_kernel<MODE, CODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmem);
+    if (e != cudaSuccess) return e;
     tc::moe_tc_kernel<MODE, CODE><<<grid, tc::kThreads, C::kSmem, s>>>(a0, a1, b, items, n_items, rows_per_expert, K,
                                                                        out_ld, act, y, err);
     return cudaGetLastError();

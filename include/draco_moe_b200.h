@@ -164,6 +164,12 @@ int draco_b200_moe_tok_noalloc(const float* X, const int* order, const float* wt
                                const uint64_t* ep_dev, const int* ec, int T, int n_used, int inter,
                                int n_in, int n_out, int n_exp, float* out, void* stream);
 
+/* Grouped expert GEMM path: 0 automatic (tensor cores from DRACO_B200_TC_MIN_P = 128
+ * token-expert assignments per call, when the formats and shapes allow), 1 CUDA cores,
+ * 2 tensor cores whenever supported.  DRACO_B200_GEMM sets the initial value.  Returns the
+ * previous mode. */
+int draco_b200_set_gemm_path(int mode);
+
 /* Activation mode for gate/up: 0 fp32 (reference semantics, default), 1 Q8_K (int8
  * activations, integer superblock dots).  Returns the previous mode. */
 int draco_b200_set_act_mode(int mode);

@@ -299,3 +299,54 @@ def test_q8k_quantize_and_dots_bitexact(dlib, port):
                                      d.ctypes.data_as(dm._f), bs.ctypes.data_as(dm._i16), y.ctypes.data_as(dm._f)) == 0
         y_ref = port.gemv_q8k(code, d, q, bs, W, rows, n_in)
         assert np.array_equal(bits(y), bits(y_ref))
+
+
+# ----------------------------------------------------------------------------- tensor-core path
+@pytest.fixture
+def gemm_path(dlib):
+    old = dlib.draco_b200_set_gemm_path(0)
+    yield dlib.draco_b200_set_gemm_path
+    dlib.draco_b200_set_gemm_path(old)
+
+
+@pytest.mark.parametrize("code_gu,code_d,T", [(5, 4, 64), (4, 5, 48), (5, 4, 3), (5, 5, 200)])
+def test_tensor_core_moe_tok(dlib, port, gemm_path, code_gu, code_d, T):
+    """tcgen05 grouped GEMM (fp16 operands, fp32 accumulation) vs the fp32 oracle."""
+    layer = synth.make_layer(hidden=2048, n_exp=16, n_used=8, inter=768, seed=80 + code_gu + T,
+                             code_gu=code_gu, code_d=code_d)
+    X = synth.make_tokens(layer, T, 80 + T)
+    order, wtop = port.route(layer, X)
+    ref = port.moe_tok(layer, X, order, wtop)
+    gemm_path(2)
+    got = dm.moe_tok(layer, X, order, wtop)
+    err = rel_l2(got, ref)
+    assert err <= REL_L2_TOL, err
+    gemm_path(1)
+    simt = dm.moe_tok(layer, X, order, wtop)
+    assert rel_l2(simt, ref) < 1e-5
+
+
+def test_tensor_core_hot_expert_many_tiles(dlib, port, gemm_path):
+    """One expert receives every token (several 128-token tiles) and the others none."""
+    layer = synth.make_layer(hidden=1024, n_exp=8, n_used=2, inter=512, seed=90)
+    T = 300
+    X = synth.make_tokens(layer, T, 90)
+    order = np.zeros((T, 2), np.int32)
+    order[:, 0] = 3
+    order[:, 1] = np.where(np.arange(T) % 2 == 0, 5, 3)
+    wtop = np.full((T, 2), 0.5, np.float32)
+    ref = port.moe_tok(layer, X, order, wtop)
+    gemm_path(2)
+    got = dm.moe_tok(layer, X, order, wtop)
+    assert rel_l2(got, ref) <= REL_L2_TOL
+
+
+def test_tensor_core_layer_k2_shape(dlib, port, gemm_path):
+    """K2 expert shape (H 7168, F 2048) with sigmoid routing, bias, scale and a shared expert."""
+    layer = synth.make_layer(hidden=7168, n_exp=16, n_used=8, inter=2048, scoring="sigmoid", w_scale=2.827,
+                             bias=True, shared_inter=2048, seed=91)
+    X = synth.make_tokens(layer, 40, 91)
+    ref = port.layer_forward(layer, X)
+    gemm_path(2)
+    got = dm.forward(layer, X)
+    assert rel_l2(got, ref) <= REL_L2_TOL
