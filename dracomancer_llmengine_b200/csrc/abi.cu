@@ -609,6 +609,7 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
     const size_t o_lg = cv.take<float>((size_t)T * a.E), o_ord = cv.take<int>(n), o_w = cv.take<float>(n);
     const size_t o_cnt = cv.take<int>(a.E), o_off = cv.take<int>(a.E + 1), o_il = cv.take<int>(n);
     const size_t o_pos = cv.take<int>(n), o_act = cv.take<int>(a.E), o_na = cv.take<int>(1), o_err = cv.take<int>(1);
+    const size_t o_cc = cv.take<int>(dispatch_chunk_ints((int)n, a.E));
     const size_t o_a = cv.take<float>(n * a.inter), o_y = cv.take<float>(n * a.n_out);
     const size_t o_ash = cv.take<float>(a.sh ? (size_t)T * a.sh_ff : 0);
     const size_t o_ysh = cv.take<float>(a.sh ? (size_t)T * a.n_out : 0);
@@ -643,6 +644,7 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
     b.rb.active = (int*)(w + o_act);
     b.rb.n_active = (int*)(w + o_na);
     b.rb.err = (int*)(w + o_err);
+    b.rb.chunk_counts = (int*)(w + o_cc);
     b.act = (float*)(w + o_a);
     b.y = (float*)(w + o_y);
     b.act_sh = (float*)(w + o_ash);
@@ -695,9 +697,26 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         // tensor-core path: fp16 gather, gate/up GEMM + SwiGLU, down GEMM (gate/up phase times all)
         PhaseScope ps(kGateUp, s);
         CK(cudaMemsetAsync(b.tc_err, 0, sizeof(int), s));
+        static unsigned long long* stats = nullptr;   // DRACO_B200_TC_STATS=1: per-site wait cycles
+        if (!stats && env_flag("DRACO_B200_TC_STATS")) {
+            cudaMallocManaged(&stats, sizeof(unsigned long long) * 2 * kTcStatSites);
+            cudaMemset(stats, 0, sizeof(unsigned long long) * 2 * kTcStatSites);
+        }
         const int rc = tc_run(*(const TcMaps*)a.tab->tc, a.tab->cg, a.tab->cd, a.E, a.inter, a.n_in, a.n_out, b.x,
                               rb.ilist, a.K, T * a.K, rb.off, rb.active, rb.n_active, b.xs_h, b.act_h, b.y,
-                              b.items_gu, b.n_items, b.items_dn, b.n_items + 1, b.tc_err, s);
+                              b.items_gu, b.n_items, b.items_dn, b.n_items + 1, b.tc_err, stats, s);
+        if (stats) {
+            cudaStreamSynchronize(s);
+            static const char* names[kTcStatSites] = {"prod_raw_empty", "prod_b_empty", "mma_acc_empty", "mma_b_full",
+                                                      "mma_a_full", "deq_raw_full", "deq_a_empty", "deq_acc_full",
+                                                      "deq_total", "mma_total", "deq_decode", "deq_store", "deq_epi"};
+            for (int k = 0; k < 2; k++) {
+                fprintf(stderr, "[tc stats %s]", k ? "down" : "gateup");
+                for (int i = 0; i < kTcStatSites; i++) fprintf(stderr, " %s=%.3g", names[i], (double)stats[k * kTcStatSites + i]);
+                fprintf(stderr, "\n");
+            }
+            memset(stats, 0, sizeof(unsigned long long) * 2 * kTcStatSites);
+        }
         if (rc) {
             set_err("tensor-core grouped GEMM launch failed (%d): %s", rc, cudaGetErrorString(cudaGetLastError()));
             return -3;
@@ -824,6 +843,10 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
     LayerBufs b;
     if (int rc = carve_layer(c, a, T, b)) return rc;
     const bool dev_io = dev_kind(x);
+    if (dev_io && ((uintptr_t)x & 15 || (uintptr_t)out & 15)) {
+        set_err("device activations and outputs must be 16-byte aligned");
+        return -1;
+    }
     cudaStream_t s = (dev_io && user_stream) ? user_stream : c->stream;
     float* d_out = b.out;
     if (dev_io) {
@@ -958,6 +981,10 @@ static int moe_tok_impl(const float* X, const int* order, const float* wtop, con
     cudaStream_t s = c->stream;
     const size_t n = (size_t)T * n_used;
     const bool dev_io = dev_kind(X);
+    if (dev_io && ((uintptr_t)X & 15 || (uintptr_t)out & 15)) {
+        set_err("device activations and outputs must be 16-byte aligned");
+        return -1;
+    }
     if (dev_io) {
         b.x = const_cast<float*>(X);
         b.out = out;

@@ -16,7 +16,11 @@ struct RouteBufs {
     int* active;        // [E]       experts with count > 0, ascending
     int* n_active;      // [1]
     int* err;           // [1]       nonzero: routing produced an invalid selection
+    int* chunk_counts;  // [ceil(T*K/1024)][E] dispatch scratch
 };
+
+// dispatch scratch ints for n assignments over E experts
+inline size_t dispatch_chunk_ints(int n, int E) { return (size_t)((n + 1023) / 1024 + 1) * (size_t)E; }
 
 // Router parameters (semantics of src/m6_layer.c:771-796 and :823-866).
 struct RouterParams {

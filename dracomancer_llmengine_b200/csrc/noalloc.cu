@@ -53,6 +53,7 @@ size_t scratch_bytes(int T, int n_used, int inter, int n_out, int n_exp) {
     off += up256(sizeof(int) * (n ? n : 1));                 // pos_of
     off += up256(sizeof(int) * (size_t)n_exp);               // active
     off += up256(sizeof(int));                               // n_active
+    off += up256(sizeof(int) * dispatch_chunk_ints((int)n, n_exp));   // dispatch chunk counts
     off += up256(sizeof(float) * (n ? n : 1) * (size_t)inter);   // act
     off += up256(sizeof(float) * (n ? n : 1) * (size_t)n_out);   // y
     return off;
@@ -70,6 +71,7 @@ extern "C" int draco_b200_moe_tok_noalloc(const float* X, const int* order, cons
         n_in <= 0 || n_out <= 0)
         return fail(-1, "unsupported shape");
     if (!X || !order || !wtop || !ep_dev || !ec || !out) return fail(-1, "null argument");
+    if (((uintptr_t)X & 15) || ((uintptr_t)out & 15)) return fail(-1, "X and out must be 16-byte aligned");
     const int cg = ec[0], cu = ec[1], cd = ec[2];
     for (int e = 0; e < n_exp; e++)
         if (ec[3 * e] != cg || ec[3 * e + 1] != cu || ec[3 * e + 2] != cd)
@@ -115,6 +117,7 @@ extern "C" int draco_b200_moe_tok_noalloc(const float* X, const int* order, cons
     rb.pos_of = (int*)take(sizeof(int) * n);
     rb.active = (int*)take(sizeof(int) * n_exp);
     rb.n_active = (int*)take(sizeof(int));
+    rb.chunk_counts = (int*)take(sizeof(int) * dispatch_chunk_ints((int)n, n_exp));
     float* act = (float*)take(sizeof(float) * n * inter);
     float* y = (float*)take(sizeof(float) * n * n_out);
     rb.order = const_cast<int*>(order);

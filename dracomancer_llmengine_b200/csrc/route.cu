@@ -59,14 +59,88 @@ __global__ void __launch_bounds__(32 * TY) router_logits_kernel(const float* __r
     }
 }
 
+// Many-warp variant: one output per thread, a 8-token x 32-expert tile per 256-thread block
+// (small shared footprint, so several blocks share an SM and hide each other's loads), k-chunks
+// of 64 staged in shared memory and read as float4 (4 consecutive k of one row); each thread
+// still walks k upward one rounded product at a time.  Rows are padded to 68 floats so the
+// expert rows a warp reads at one k fall in distinct bank groups.
+__global__ void __launch_bounds__(256) router_logits_v2(const float* __restrict__ X, const float* __restrict__ W,
+                                                        int T, int E, int H, float* __restrict__ logits) {
+    constexpr int KC = 64, LD = KC + 4, TT = 8, TE = 32;
+    constexpr int NV = (TT + TE) * (KC / 4);            // float4 slots per chunk
+    constexpr int PER = (NV + 255) / 256;               // per thread
+    __shared__ __align__(16) float xs[TT][LD];
+    __shared__ __align__(16) float ws[TE][LD];
+    const int tid = threadIdx.x, ty = tid >> 5, tx = tid & 31;
+    const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE;
+    // the next chunk is fetched into registers while the current one is consumed
+    float4 pre[PER];
+    auto fetch = [&](int k0) {
+        const int kn = min(KC, H - k0);
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int i = tid + 256 * j;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < NV) {
+                const int rr = i / (KC / 4), k4 = (i % (KC / 4)) * 4;
+                const bool is_x = rr < TT;
+                const int row = is_x ? t0 + rr : e0 + rr - TT;
+                if ((is_x ? row < T : row < E) && k4 < kn) {
+                    const float* src = (is_x ? X : W) + (size_t)row * H + k0 + k4;
+                    if (k4 + 4 <= kn) v = *reinterpret_cast<const float4*>(src);
+                    else {
+                        v.x = src[0];
+                        if (k4 + 1 < kn) v.y = src[1];
+                        if (k4 + 2 < kn) v.z = src[2];
+                    }
+                }
+            }
+            pre[j] = v;
+        }
+    };
+    auto stash = [&]() {
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int i = tid + 256 * j;
+            if (i < NV) {
+                const int rr = i / (KC / 4), k4 = (i % (KC / 4)) * 4;
+                float* dst = rr < TT ? &xs[rr][k4] : &ws[rr - TT][k4];
+                *reinterpret_cast<float4*>(dst) = pre[j];
+            }
+        }
+    };
+    float acc = 0.f;
+    fetch(0);
+    for (int k0 = 0; k0 < H; k0 += KC) {
+        const int kn = min(KC, H - k0);
+        stash();
+        __syncthreads();
+        if (k0 + KC < H) fetch(k0 + KC);
+        const int kq = kn / 4;
+        for (int q = 0; q < kq; q++) {
+            const float4 xv = *reinterpret_cast<const float4*>(&xs[ty][4 * q]);
+            const float4 wv = *reinterpret_cast<const float4*>(&ws[tx][4 * q]);
+            acc = __fadd_rn(acc, __fmul_rn(xv.x, wv.x));
+            acc = __fadd_rn(acc, __fmul_rn(xv.y, wv.y));
+            acc = __fadd_rn(acc, __fmul_rn(xv.z, wv.z));
+            acc = __fadd_rn(acc, __fmul_rn(xv.w, wv.w));
+        }
+        for (int k = 4 * kq; k < kn; k++) acc = __fadd_rn(acc, __fmul_rn(xs[ty][k], ws[tx][k]));
+        __syncthreads();
+    }
+    const int t = t0 + ty, e = e0 + tx;
+    if (t < T && e < E) logits[(size_t)t * E + e] = acc;
+}
+
 void launch_router_logits(const float* X, const float* W, int T, int E, int H, float* logits,
                           cudaStream_t s) {
-    if (T <= 4) {
+    const bool vec_ok = H % 4 == 0 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0;
+    if (T <= 4 || !vec_ok) {
         dim3 grid((E + 31) / 32, (T + 3) / 4);
         router_logits_kernel<4, 1><<<grid, dim3(32, 4), 0, s>>>(X, W, T, E, H, logits);
     } else {
-        dim3 grid((E + 31) / 32, (T + 31) / 32);
-        router_logits_kernel<8, 4><<<grid, dim3(32, 8), 0, s>>>(X, W, T, E, H, logits);
+        dim3 grid((T + 7) / 8, (E + 31) / 32);
+        router_logits_v2<<<grid, 256, 0, s>>>(X, W, T, E, H, logits);
     }
 }
 
@@ -230,33 +304,47 @@ void launch_router_select(const RouterParams& p, int T, RouteBufs& b, cudaStream
 
 // ------------------------------------------------------------------------------------------
 // Dispatch: stable counting sort of assignments i = t*K + k by expert (the order of
-// src/m6_moe_tok.c:53-70): counts, prefix, then per expert a warp walks i upward and places
-// its assignments with ballots, so each expert's list is in increasing i.
+// src/m6_moe_tok.c:53-70), in three passes over chunks of 1024 assignments: per-chunk expert
+// counts; per-expert prefix over chunks plus expert offsets; placement, where a chunk's warps
+// take turns and each ranks its lanes among equal experts with a match mask, so every
+// expert's list is in increasing i.
 // ------------------------------------------------------------------------------------------
-__global__ void dispatch_count_kernel(const int* __restrict__ order, int n, int E, int* counts) {
-    extern __shared__ int sc[];
+constexpr int kChunk = 1024;
+
+__global__ void __launch_bounds__(kChunk) dispatch_count_kernel(const int* __restrict__ order, int n, int E,
+                                                               int* __restrict__ chunk_counts) {
+    __shared__ int sc[kMaxExperts];
     for (int e = threadIdx.x; e < E; e += blockDim.x) sc[e] = 0;
     __syncthreads();
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int i = blockIdx.x * kChunk + threadIdx.x;
+    if (i < n) {
         const int e = order[i];
         if (e >= 0 && e < E) atomicAdd(&sc[e], 1);
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < E; e += blockDim.x)
-        if (sc[e]) atomicAdd(&counts[e], sc[e]);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_counts[(size_t)blockIdx.x * E + e] = sc[e];
 }
 
-__global__ void dispatch_scan_kernel(const int* __restrict__ counts, int E, int* off, int* active,
-                                     int* n_active) {
-    // E <= 512: one block of 512 threads, Hillis-Steele scan in shared memory
+__global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restrict__ chunk_counts, int n_chunks,
+                                                                   int E, int* __restrict__ counts,
+                                                                   int* __restrict__ off, int* __restrict__ active,
+                                                                   int* __restrict__ n_active) {
     __shared__ int sv[kMaxExperts];
     __shared__ int sa[kMaxExperts];
     const int e = threadIdx.x;
-    const int c = e < E ? counts[e] : 0;
+    // per expert: exclusive prefix over chunks (in place), total
+    int c = 0;
+    if (e < E)
+        for (int k = 0; k < n_chunks; k++) {
+            const int v = chunk_counts[(size_t)k * E + e];
+            chunk_counts[(size_t)k * E + e] = c;
+            c += v;
+        }
+    if (e < E) counts[e] = c;
     sv[e] = c;
     sa[e] = c > 0 ? 1 : 0;
     __syncthreads();
-    for (int o = 1; o < kMaxExperts; o <<= 1) {
+    for (int o = 1; o < kMaxExperts; o <<= 1) {   // inclusive scans over experts
         const int v = e >= o ? sv[e - o] : 0;
         const int a = e >= o ? sa[e - o] : 0;
         __syncthreads();
@@ -264,9 +352,11 @@ __global__ void dispatch_scan_kernel(const int* __restrict__ counts, int E, int*
         sa[e] += a;
         __syncthreads();
     }
+    const int base = sv[e] - c;   // exclusive offset of expert e
     if (e < E) {
         off[e + 1] = sv[e];
         if (c > 0) active[sa[e] - 1] = e;
+        for (int k = 0; k < n_chunks; k++) chunk_counts[(size_t)k * E + e] += base;
     }
     if (e == 0) {
         off[0] = 0;
@@ -274,36 +364,38 @@ __global__ void dispatch_scan_kernel(const int* __restrict__ counts, int E, int*
     }
 }
 
-__global__ void dispatch_place_kernel(const int* __restrict__ order, int n, int E,
-                                      const int* __restrict__ off, int* __restrict__ ilist,
-                                      int* __restrict__ pos_of) {
-    const int warps = blockDim.x >> 5;
-    const int e = blockIdx.x * warps + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (e >= E) return;
-    int base = off[e];
-    const int end = off[e + 1];
-    if (base == end) return;
-    for (int i0 = 0; i0 < n && base < end; i0 += 32) {
-        const int i = i0 + lane;
-        const bool hit = i < n && order[i] == e;
-        const unsigned m = __ballot_sync(0xffffffffu, hit);
-        if (hit) {
-            const int p = base + __popc(m & ((1u << lane) - 1u));
+__global__ void __launch_bounds__(kChunk) dispatch_place_kernel(const int* __restrict__ order, int n, int E,
+                                                               const int* __restrict__ chunk_base,
+                                                               int* __restrict__ ilist, int* __restrict__ pos_of) {
+    __shared__ int cursor[kMaxExperts];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cursor[e] = chunk_base[(size_t)blockIdx.x * E + e];
+    __syncthreads();
+    const int i = blockIdx.x * kChunk + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int e = i < n ? order[i] : -1;
+    if (e >= E) e = -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const bool leader = rank == 0;
+    for (int w = 0; w < kChunk / 32; w++) {
+        if (warp == w && e >= 0) {
+            const int p = cursor[e] + rank;
             ilist[p] = i;
             pos_of[i] = p;
         }
-        base += __popc(m);
+        __syncwarp();
+        if (warp == w && e >= 0 && leader) cursor[e] += __popc(peers);
+        __syncthreads();
     }
 }
 
 void launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s) {
     const int n = T * K;
-    cudaMemsetAsync(b.counts, 0, sizeof(int) * E, s);
-    const int blocks = min(148, max(1, (n + 1023) / 1024));
-    dispatch_count_kernel<<<blocks, 1024, sizeof(int) * E, s>>>(b.order, n, E, b.counts);
-    dispatch_scan_kernel<<<1, kMaxExperts, 0, s>>>(b.counts, E, b.off, b.active, b.n_active);
-    dispatch_place_kernel<<<(E + 7) / 8, 256, 0, s>>>(b.order, n, E, b.off, b.ilist, b.pos_of);
+    const int n_chunks = max(1, (n + kChunk - 1) / kChunk);
+    dispatch_count_kernel<<<n_chunks, kChunk, 0, s>>>(b.order, n, E, b.chunk_counts);
+    dispatch_scan_kernel<<<1, kMaxExperts, 0, s>>>(b.chunk_counts, n_chunks, E, b.counts, b.off, b.active,
+                                                   b.n_active);
+    dispatch_place_kernel<<<n_chunks, kChunk, 0, s>>>(b.order, n, E, b.chunk_counts, b.ilist, b.pos_of);
 }
 
 // host expf replica over an array (test hook)

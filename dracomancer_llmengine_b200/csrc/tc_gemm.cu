@@ -31,17 +31,19 @@ namespace draco {
 namespace tc {
 
 constexpr int kDeqWarps = 16;                 // 4 warpgroups
-constexpr int kProdWarp = 16;                 // TMA producer
+constexpr int kProdWarp = 16;                 // TMA producer of the weight superblocks
 constexpr int kMmaWarp = 17;                  // MMA issuer, TMEM owner
-constexpr int kThreads = 32 * 18;
-constexpr int kRawStages = 4;                 // raw superblock-column stages (one matrix each)
+constexpr int kBProdWarp = 18;                // TMA producer of the activation tiles
+constexpr int kThreads = 32 * 19;
+constexpr int kMaxRawStages = 8;              // raw superblock-column stages (one matrix each)
 constexpr int kBStages = 4;                   // k64 activation stages
 constexpr int kASlots = 8;                    // k64 A slots in TMEM
 constexpr int kBStageBytes = 128 * 128;       // 128 tokens x 64 halves
 constexpr int kTmemCols = 512;
 constexpr int kAccCols = 128;                 // per accumulator (N <= 128)
 constexpr int kABase = 256;                   // A slots start here (after 2 accumulators)
-constexpr long kSpinLimit = 1L << 21;         // bounded waits (a second or two)
+constexpr long kSpinLimit = 1L << 21;         // bounded waits: polls of at most kSuspendNs each
+constexpr uint32_t kSuspendNs = 1000;         // try_wait may suspend the thread up to this long
 
 // error codes written to *err
 constexpr int kErrTimeout = 0x100;
@@ -64,9 +66,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -104,6 +106,27 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
     for (long i = 0; i < kSpinLimit && !mbar_try(bar, parity); i++) {
     }
 }
+
+// Optional wait statistics: cycles a role spends in each wait site, summed over warps
+// (one lane per warp) into stats[site]; enabled when the kernel gets a stats pointer.
+enum StatSite {
+    kStProdRawEmpty = 0, kStProdBEmpty, kStMmaAccEmpty, kStMmaBFull, kStMmaAFull, kStDeqRawFull, kStDeqAEmpty,
+    kStDeqAccFull, kStDeqTotal, kStMmaTotal, kStDeqDecode, kStDeqStore, kStDeqEpi, kStSites
+};
+struct StatTimer {
+    unsigned long long acc[kStSites];
+    long long t;
+    __device__ void reset() {
+        for (int i = 0; i < kStSites; i++) acc[i] = 0;
+    }
+    __device__ __forceinline__ void start() { t = clock64(); }
+    __device__ __forceinline__ void stop(int site) { acc[site] += (unsigned long long)(clock64() - t); }
+    __device__ void flush(unsigned long long* stats) {
+        if (!stats) return;
+        for (int i = 0; i < kStSites; i++)
+            if (acc[i]) atomicAdd(stats + i, acc[i]);
+    }
+};
 
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -158,6 +181,16 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+
 // instruction descriptor: D fp32, A/B fp16, both K-major, M = 128, N = n
 __device__ __forceinline__ uint32_t idesc_f16(int n) {
     return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
@@ -183,35 +216,46 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// Q4_K 6-bit scale/min of sub-block j (0..7) from the 12 scale bytes held in three words
+// (s0 = bytes 0-3, s1 = 4-7, s2 = 8-11; src/m5_kern_scalar.c:39-46), without indexing memory
+__device__ __forceinline__ void q4k_sm_words(uint32_t s0, uint32_t s1, uint32_t s2, int j, int& sc, int& mn) {
+    if (j < 4) {
+        sc = (s0 >> (8 * j)) & 63;
+        mn = (s1 >> (8 * j)) & 63;
+    } else {
+        const int b = 8 * (j - 4);
+        const uint32_t e2 = (s2 >> b) & 0xff;
+        sc = (int)((e2 & 15) | (((s0 >> b) >> 6 & 3) << 4));
+        mn = (int)((e2 >> 4) | (((s1 >> b) >> 6 & 3) << 4));
+    }
+}
+
 // Q4_K: 64 values [64*kc, 64*kc+64) of one superblock row -> 32 packed fp16 pairs
 __device__ __forceinline__ void deq_q4k(const uint8_t* blk, int kc, uint32_t (&out)[32]) {
     const uint4 hd = *reinterpret_cast<const uint4*>(blk);
     const float d = h2f((uint16_t)(hd.x & 0xffff)), dmin = h2f((uint16_t)(hd.x >> 16));
-    uint8_t s12[12];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        s12[i] = (uint8_t)(hd.y >> (8 * i));
-        s12[4 + i] = (uint8_t)(hd.z >> (8 * i));
-        s12[8 + i] = (uint8_t)(hd.w >> (8 * i));
-    }
     int sc0, m0, sc1, m1;
-    q4k_sm(s12, 2 * kc, sc0, m0);
-    q4k_sm(s12, 2 * kc + 1, sc1, m1);
+    q4k_sm_words(hd.y, hd.z, hd.w, 2 * kc, sc0, m0);
+    q4k_sm_words(hd.y, hd.z, hd.w, 2 * kc + 1, sc1, m1);
     const float ds0 = d * (float)sc0, dm0 = dmin * (float)m0;
     const float ds1 = d * (float)sc1, dm1 = dmin * (float)m1;
     const float a0 = 64.f * ds0, b0 = -(128.f * ds0 + dm0);
     const float a1 = 64.f * ds1, b1 = -(128.f * ds1 + dm1);
     const uint4* qv = reinterpret_cast<const uint4*>(blk + 16 + 32 * kc);
-    const uint4 q0 = qv[0], q1 = qv[1];
-    const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-    for (int w = 0; w < 8; w++) {
-        const uint32_t lo = words[w] & 0x0F0F0F0Fu, hi = (words[w] >> 4) & 0x0F0F0F0Fu;
-        // low nibbles: values 4w..4w+3 of sub-block 2kc; high nibbles: of sub-block 2kc+1
-        out[2 * w] = pack2(fmaf(q_as_float(lo, 0), a0, b0), fmaf(q_as_float(lo, 1), a0, b0));
-        out[2 * w + 1] = pack2(fmaf(q_as_float(lo, 2), a0, b0), fmaf(q_as_float(lo, 3), a0, b0));
-        out[16 + 2 * w] = pack2(fmaf(q_as_float(hi, 0), a1, b1), fmaf(q_as_float(hi, 1), a1, b1));
-        out[16 + 2 * w + 1] = pack2(fmaf(q_as_float(hi, 2), a1, b1), fmaf(q_as_float(hi, 3), a1, b1));
+    for (int h = 0; h < 2; h++) {
+        const uint4 q = qv[h];
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint32_t word = c == 0 ? q.x : c == 1 ? q.y : c == 2 ? q.z : q.w;
+            const int w = 4 * h + c;
+            const uint32_t lo = word & 0x0F0F0F0Fu, hi = (word >> 4) & 0x0F0F0F0Fu;
+            // low nibbles: values 4w..4w+3 of sub-block 2kc; high nibbles: of sub-block 2kc+1
+            out[2 * w] = pack2(fmaf(q_as_float(lo, 0), a0, b0), fmaf(q_as_float(lo, 1), a0, b0));
+            out[2 * w + 1] = pack2(fmaf(q_as_float(lo, 2), a0, b0), fmaf(q_as_float(lo, 3), a0, b0));
+            out[16 + 2 * w] = pack2(fmaf(q_as_float(hi, 0), a1, b1), fmaf(q_as_float(hi, 1), a1, b1));
+            out[16 + 2 * w + 1] = pack2(fmaf(q_as_float(hi, 2), a1, b1), fmaf(q_as_float(hi, 3), a1, b1));
+        }
     }
 }
 
@@ -222,29 +266,23 @@ __device__ __forceinline__ void deq_q6k(const uint8_t* blk, int kc, uint32_t (&o
     const int h = kc >> 1, nhi = kc & 1;
     const uint4* qlv = reinterpret_cast<const uint4*>(blk + h * 64);
     const uint4* qhv = reinterpret_cast<const uint4*>(blk + 128 + h * 32);
-    const uint4 l0 = qlv[0], l1 = qlv[1], l2 = qlv[2], l3 = qlv[3];
-    const uint4 g0 = qhv[0], g1 = qhv[1];
-    const uint32_t ql[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w,
-                             l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
-    const uint32_t qh[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
     const uint32_t scw = *reinterpret_cast<const uint32_t*>(blk + 192 + 4 * kc);
     const float d = h2f(*reinterpret_cast<const uint16_t*>(blk + 208));
-    // 4 groups of 16 values: group g covers p = 64kc + 16g .. +16, scale sc[4kc + g]
+    const int nsh = 4 * nhi;
+    // 4 groups of 16 values: group g covers p = 64kc + 16g .. +16 with scale sc[4kc + g];
+    // ql byte 16g + i of this half, qh byte 16(g & 1) + i, 2-bit field at (2 nhi + g/2) * 2
 #pragma unroll
     for (int g = 0; g < 4; g++) {
         const float ds = d * (float)(int8_t)(scw >> (8 * g));
-        const float a = 64.f * ds, b = -(128.f * ds + 32.f * ds);
-        // p & 63 = 16g' with g' = g (within the 64-value half chosen by nhi) ... p = 64kc + 16g + i
-        // ql index (p & 63) = 16*(g) + i  (bytes 16g .. 16g+15 of this half's 64 ql bytes)
-        // qh index (p & 31) = 16*(g & 1) + i, shift = ((p >> 5) & 3) * 2 = (2*nhi + (g >> 1)) * 2
+        const float a = 64.f * ds, b = -(160.f * ds);
+        const uint4 l = qlv[g];
+        const uint4 q2 = qhv[g & 1];
         const int shift = (2 * nhi + (g >> 1)) * 2;
 #pragma unroll
         for (int w = 0; w < 4; w++) {
-            const uint32_t lw = ql[4 * g + w];
-            const uint32_t nib = nhi ? ((lw >> 4) & 0x0F0F0F0Fu) : (lw & 0x0F0F0F0Fu);
-            const uint32_t hw = qh[4 * (g & 1) + w];
-            const uint32_t two = (hw >> shift) & 0x03030303u;
-            const uint32_t q6 = nib | (two << 4);
+            const uint32_t lw = w == 0 ? l.x : w == 1 ? l.y : w == 2 ? l.z : l.w;
+            const uint32_t hw = w == 0 ? q2.x : w == 1 ? q2.y : w == 2 ? q2.z : q2.w;
+            const uint32_t q6 = ((lw >> nsh) & 0x0F0F0F0Fu) | (((hw >> shift) & 0x03030303u) << 4);
             out[8 * g + 2 * w] = pack2(fmaf(q_as_float(q6, 0), a, b), fmaf(q_as_float(q6, 1), a, b));
             out[8 * g + 2 * w + 1] = pack2(fmaf(q_as_float(q6, 2), a, b), fmaf(q_as_float(q6, 3), a, b));
         }
@@ -252,15 +290,13 @@ __device__ __forceinline__ void deq_q6k(const uint8_t* blk, int kc, uint32_t (&o
 }
 
 // ---------------------------------------------------------------- the kernel
-struct SmemLayout {
-    static constexpr int raw_bytes(int bb) { return kRawStages * 128 * bb; }
-};
-
 template <int MODE, int CODE>
 struct Cfg {
     static constexpr int kMats = MODE == 0 ? 2 : 1;
     static constexpr int kBB = CODE == DRACO_CODE_Q4_K ? 144 : kQ6Padded;   // raw bytes per row superblock
     static constexpr int kRawStage = 128 * kBB;
+    // as many weight stages as fit next to the activation ring (227 KB per block)
+    static constexpr int kRawStages = CODE == DRACO_CODE_Q4_K ? 8 : 5;
     // raw stage consumers: gate/up -> 2 warpgroups x 4 warps; down -> 4 x 4
     static constexpr int kRawConsumers = MODE == 0 ? 8 : 16;
     static constexpr int kBOff = kRawStages * kRawStage;                 // 1024-aligned below
@@ -270,7 +306,7 @@ struct Cfg {
 };
 
 struct Bars {
-    uint64_t raw_full[kRawStages], raw_empty[kRawStages];
+    uint64_t raw_full[kMaxRawStages], raw_empty[kMaxRawStages];
     uint64_t b_full[kBStages], b_empty[kBStages];
     uint64_t a_full[kASlots], a_empty[kASlots];
     uint64_t acc_full, acc_empty, drain;
@@ -283,11 +319,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     moe_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                   const __grid_constant__ CUtensorMap tmB, const int4* __restrict__ items,
                   const int* __restrict__ n_items_p, int rows_per_expert, int K, int out_ld,
-                  __half* __restrict__ act_out, float* __restrict__ y_out, int* __restrict__ err) {
+                  __half* __restrict__ act_out, float* __restrict__ y_out, int* __restrict__ err,
+                  unsigned long long* __restrict__ stats) {
     using C = Cfg<MODE, CODE>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    // 1024-align the dynamic shared memory base (swizzled tiles need it)
-    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // 1024-align the dynamic shared memory base (swizzled tiles need it) by pointer arithmetic
+    // on the shared array, so every access below stays a shared-memory access
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* raw = smem;
     uint8_t* bt = smem + C::kBOffAligned;
     Bars* bars = reinterpret_cast<Bars*>(smem + C::kBarOff);
@@ -298,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nb = K / 256;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kRawStages; i++) {
+        for (int i = 0; i < C::kRawStages; i++) {
             mbar_init(&bars->raw_full[i], 1);
             mbar_init(&bars->raw_empty[i], C::kRawConsumers);
         }
@@ -327,27 +365,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
+    StatTimer st;
+    st.reset();
+    const long long t_begin = clock64();
 
     if (warp == kProdWarp) {
-        // ------------------------------------------------------------ TMA producer
+        // ------------------------------------------------------------ weight producer
         if (lane == 0) {
-            uint32_t rq = 0, bq = 0;   // fills issued so far (raw, B)
+            uint32_t rq = 0;   // weight fills issued so far
             for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
                 const int4 item = items[it];
-                const int e = item.x, mt = item.y, p0 = item.z, ntok = item.w;
-                const int nbox = (ntok + 15) >> 4;
-                const int arow = e * rows_per_expert + mt * 128;
+                const int arow = item.x * rows_per_expert + item.y * 128;
                 for (int sb = 0; sb < nb && !*abort_flag; sb++) {
                     for (int m = 0; m < C::kMats; m++, rq++) {
-                        const int s = rq % kRawStages;
-                        if (!mbar_wait(&bars->raw_empty[s], ((rq / kRawStages) & 1) ^ 1, abort_flag, err, 1)) break;
+                        const int s = rq % C::kRawStages;
+                        st.start();
+                        const bool w_ok = mbar_wait(&bars->raw_empty[s], ((rq / C::kRawStages) & 1) ^ 1, abort_flag, err, 1);
+                        st.stop(kStProdRawEmpty);
+                        if (!w_ok) break;
                         mbar_expect_tx(&bars->raw_full[s], C::kRawStage);
                         tma_load_2d(raw + s * C::kRawStage, m == 0 ? &tmA0 : &tmA1, sb * (C::kBB / 4), arow,
                                     &bars->raw_full[s]);
                     }
+                }
+            }
+            if (*abort_flag)   // drain: the most recent fills land before the CTA exits
+                for (uint32_t k = 0; k < (uint32_t)C::kRawStages && k < rq; k++) {
+                    const uint32_t q = rq - 1 - k;
+                    mbar_drain(&bars->raw_full[q % C::kRawStages], (q / C::kRawStages) & 1);
+                }
+        }
+    } else if (warp == kBProdWarp) {
+        // ------------------------------------------------------------ activation producer
+        if (lane == 0) {
+            uint32_t bq = 0;
+            for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
+                const int4 item = items[it];
+                const int p0 = item.z, nbox = (item.w + 15) >> 4;
+                for (int sb = 0; sb < nb && !*abort_flag; sb++) {
                     for (int kc = 0; kc < 4; kc++, bq++) {
                         const int s = bq % kBStages;
-                        if (!mbar_wait(&bars->b_empty[s], ((bq / kBStages) & 1) ^ 1, abort_flag, err, 2)) break;
+                        st.start();
+                        const bool w_ok = mbar_wait(&bars->b_empty[s], ((bq / kBStages) & 1) ^ 1, abort_flag, err, 2);
+                        st.stop(kStProdBEmpty);
+                        if (!w_ok) break;
                         mbar_expect_tx(&bars->b_full[s], nbox * 16 * 128);
                         for (int j = 0; j < nbox; j++)
                             tma_load_2d(bt + s * kBStageBytes + j * 2048, &tmB, sb * 256 + kc * 64, p0 + 16 * j,
@@ -355,17 +416,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            if (*abort_flag) {
-                // drain: wait (bounded) for the most recent fills to land before the CTA exits
-                for (uint32_t k = 0; k < kRawStages && k < rq; k++) {
-                    const uint32_t q = rq - 1 - k;
-                    mbar_drain(&bars->raw_full[q % kRawStages], (q / kRawStages) & 1);
-                }
+            if (*abort_flag)
                 for (uint32_t k = 0; k < kBStages && k < bq; k++) {
                     const uint32_t q = bq - 1 - k;
                     mbar_drain(&bars->b_full[q % kBStages], (q / kBStages) & 1);
                 }
-            }
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
@@ -379,17 +434,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t idesc = idesc_f16(nmma);
                 if (n_done > 0) {
                     // the epilogue of the previous item must have read the accumulators
-                    if (!(ok = mbar_wait(&bars->acc_empty, (n_done - 1) & 1, abort_flag, err, 3))) break;
+                    st.start();
+                    ok = mbar_wait(&bars->acc_empty, (n_done - 1) & 1, abort_flag, err, 3);
+                    st.stop(kStMmaAccEmpty);
+                    if (!ok) break;
                     tc_fence_after();
                 }
                 for (int sb = 0; sb < nb && ok; sb++) {
                     for (int kc = 0; kc < 4 && ok; kc++, bq++) {
                         const int bs = bq % kBStages;
-                        if (!(ok = mbar_wait(&bars->b_full[bs], (bq / kBStages) & 1, abort_flag, err, 4))) break;
+                        st.start();
+                        ok = mbar_wait(&bars->b_full[bs], (bq / kBStages) & 1, abort_flag, err, 4);
+                        st.stop(kStMmaBFull);
+                        if (!ok) break;
                         const uint32_t b_addr = smem_u32(bt + bs * kBStageBytes);
                         for (int m = 0; m < C::kMats; m++, u++) {
                             const int as = u % kASlots;
-                            if (!(ok = mbar_wait(&bars->a_full[as], (u / kASlots) & 1, abort_flag, err, 5))) break;
+                            st.start();
+                            ok = mbar_wait(&bars->a_full[as], (u / kASlots) & 1, abort_flag, err, 5);
+                            st.stop(kStMmaAFull);
+                            if (!ok) break;
                             tc_fence_after();
                             const uint32_t a_tm = tmem + kABase + 32 * as;
                             const uint32_t d_tm = tmem + m * kAccCols;
@@ -425,58 +489,83 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int m = 0; m < C::kMats && ok; m++, u++) {
                         if ((int)(u & 3) != wg) continue;
                         const uint32_t q = rq0 + m;
-                        const int rs = q % kRawStages;
-                        if (!(ok = warp_wait(&bars->raw_full[rs], (q / kRawStages) & 1, abort_flag, err, 7))) break;
+                        const int rs = q % C::kRawStages;
+                        st.start();
+                        ok = warp_wait(&bars->raw_full[rs], (q / C::kRawStages) & 1, abort_flag, err, 7);
+                        st.stop(kStDeqRawFull);
+                        if (!ok) break;
                         const int as = u % kASlots;
-                        if (!(ok = warp_wait(&bars->a_empty[as], ((u / kASlots) & 1) ^ 1, abort_flag, err, 8))) break;
+                        st.start();
+                        ok = warp_wait(&bars->a_empty[as], ((u / kASlots) & 1) ^ 1, abort_flag, err, 8);
+                        st.stop(kStDeqAEmpty);
+                        if (!ok) break;
                         tc_fence_after();
                         uint32_t v[32];
                         const uint8_t* blk = raw + rs * C::kRawStage + row * C::kBB;
+                        st.start();
                         if (CODE == DRACO_CODE_Q4_K) deq_q4k(blk, kc, v);
                         else deq_q6k(blk, kc, v);
+                        st.stop(kStDeqDecode);
+                        // last read of this raw stage by this warpgroup: release it
+                        const bool last = MODE == 0 ? (kc >= 2) : true;
+                        __syncwarp();
+                        if (last && lane == 0) mbar_arrive(&bars->raw_empty[rs]);
+                        st.start();
                         tc_st32(tmem + lane_base + kABase + 32 * as, v);
                         tc_wait_st();
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&bars->a_full[as]);
-                        // last use of this raw stage by this warpgroup: release it
-                        const bool last = MODE == 0 ? (kc >= 2) : true;
-                        if (last) {
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&bars->raw_empty[rs]);
-                        }
+                        st.stop(kStDeqStore);
                     }
                 }
             }
             if (!ok) break;
             // epilogue: this warpgroup's 32-token column block of the accumulators
-            if (!(ok = warp_wait(&bars->acc_full, n_done & 1, abort_flag, err, 9))) break;
+            st.start();
+            ok = warp_wait(&bars->acc_full, n_done & 1, abort_flag, err, 9);
+            st.stop(kStDeqAccFull);
+            if (!ok) break;
+            st.start();
             tc_fence_after();
             const int t0 = wg * 32;
-            uint32_t g[32], up[32];
-            if (t0 < ntok) {
-                tc_ld32(tmem + lane_base + t0, g);
-                if (MODE == 0) tc_ld32(tmem + lane_base + kAccCols + t0, up);
-                tc_wait_ld();
+            const int orow = mt * 128 + row;
+            // two 16-column halves keep 32 accumulator registers live at a time
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const int tb = t0 + 16 * hh;
+                if (tb < ntok) {
+                    uint32_t g[16], up[16];
+                    tc_ld16(tmem + lane_base + tb, g);
+                    if (MODE == 0) tc_ld16(tmem + lane_base + kAccCols + tb, up);
+                    tc_wait_ld();
+                    const int nt = min(16, ntok - tb);
+                    if (MODE == 0) {
+                        __half* dst = act_out + (size_t)(p0 + tb) * out_ld + orow;
+#pragma unroll
+                        for (int t = 0; t < 16; t++) {
+                            if (t < nt) {
+                                const float gv = __uint_as_float(g[t]), uv = __uint_as_float(up[t]);
+                                dst[(size_t)t * out_ld] = __float2half_rn(gv / (1.f + __expf(-gv)) * uv);
+                            }
+                        }
+                    } else {
+                        float* dst = y_out + (size_t)(p0 + tb) * out_ld + orow;
+#pragma unroll
+                        for (int t = 0; t < 16; t++)
+                            if (t < nt) dst[(size_t)t * out_ld] = __uint_as_float(g[t]);
+                    }
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->acc_empty);
-            if (t0 < ntok) {
-                const int nt = min(32, ntok - t0);
-                const int orow = mt * 128 + row;
-                if (MODE == 0) {
-                    for (int t = 0; t < nt; t++) {
-                        const float gv = __uint_as_float(g[t]), uv = __uint_as_float(up[t]);
-                        const float a = gv / (1.f + __expf(-gv)) * uv;
-                        act_out[(size_t)(p0 + t0 + t) * out_ld + orow] = __float2half_rn(a);
-                    }
-                } else {
-                    for (int t = 0; t < nt; t++) y_out[(size_t)(p0 + t0 + t) * out_ld + orow] = __uint_as_float(g[t]);
-                }
-            }
+            st.stop(kStDeqEpi);
         }
+        st.acc[kStDeqTotal] = (unsigned long long)(clock64() - t_begin);
     }
+    if (warp == kMmaWarp) st.acc[kStMmaTotal] = (unsigned long long)(clock64() - t_begin);
+    if (lane == 0) st.flush(stats);
     tc_fence_before();
     __syncthreads();
     if (warp == kMmaWarp) {
@@ -578,13 +667,13 @@ bool map_acts(CUtensorMap* m, const void* base, size_t P, size_t K) {
 template <int MODE, int CODE>
 cudaError_t launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b, const int4* items,
                       const int* n_items, int grid, int rows_per_expert, int K, int out_ld, __half* act, float* y,
-                      int* err, cudaStream_t s) {
+                      int* err, unsigned long long* stats, cudaStream_t s) {
     using C = tc::Cfg<MODE, CODE>;
     cudaError_t e = cudaFuncSetAttribute(tc::moe_tc_kernel<MODE, CODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmem);
     if (e != cudaSuccess) return e;
     tc::moe_tc_kernel<MODE, CODE><<<grid, tc::kThreads, C::kSmem, s>>>(a0, a1, b, items, n_items, rows_per_expert, K,
-                                                                       out_ld, act, y, err);
+                                                                       out_ld, act, y, err, stats);
     return cudaGetLastError();
 }
 
@@ -610,7 +699,7 @@ int tc_make_weight_maps(TcMaps* maps, const uint8_t* gate, const uint8_t* up, co
 int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, int n_out, const float* X,
            const int* ilist, int tok_div, int P, const int* off, const int* active, const int* n_active,
            __half* Xs, __half* act_h, float* y, int4* items_gu, int* n_items_gu, int4* items_dn, int* n_items_dn,
-           int* err, cudaStream_t s) {
+           int* err, unsigned long long* stats, cudaStream_t s) {
     if (P <= 0) return 0;
     CUtensorMap mx, ma;
     if (!map_acts(&mx, Xs, (size_t)P, (size_t)n_in) || !map_acts(&ma, act_h, (size_t)P, (size_t)inter)) return -2;
@@ -620,17 +709,17 @@ int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, i
     cudaError_t e;
     if (cg == DRACO_CODE_Q4_K)
         e = launch_tc<0, DRACO_CODE_Q4_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, inter, n_in, inter, act_h,
-                                          nullptr, err, s);
+                                          nullptr, err, stats, s);
     else
         e = launch_tc<0, DRACO_CODE_Q6_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, inter, n_in, inter, act_h,
-                                          nullptr, err, s);
+                                          nullptr, err, stats, s);
     if (e != cudaSuccess) return -3;
     if (cd == DRACO_CODE_Q4_K)
         e = launch_tc<1, DRACO_CODE_Q4_K>(maps.down, maps.down, ma, items_dn, n_items_dn, 148, n_out, inter, n_out,
-                                          nullptr, y, err, s);
+                                          nullptr, y, err, stats ? stats + tc::kStSites : nullptr, s);
     else
         e = launch_tc<1, DRACO_CODE_Q6_K>(maps.down, maps.down, ma, items_dn, n_items_dn, 148, n_out, inter, n_out,
-                                          nullptr, y, err, s);
+                                          nullptr, y, err, stats ? stats + tc::kStSites : nullptr, s);
     return e == cudaSuccess ? 0 : -3;
 }
 

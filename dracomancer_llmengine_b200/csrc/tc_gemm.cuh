@@ -23,7 +23,9 @@ int tc_make_weight_maps(TcMaps* maps, const uint8_t* gate, const uint8_t* up, co
 int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, int n_out, const float* X,
            const int* ilist, int tok_div, int P, const int* off, const int* active, const int* n_active,
            __half* Xs, __half* act_h, float* y, int4* items_gu, int* n_items_gu, int4* items_dn, int* n_items_dn,
-           int* err, cudaStream_t s);
+           int* err, unsigned long long* stats, cudaStream_t s);
+// wait-statistics sites per kernel (stats holds 2 * kTcStatSites counters: gate/up, down)
+constexpr int kTcStatSites = 13;
 // item-list capacity for P assignments over at most n_active_max experts
 inline size_t tc_items_capacity(int P, int n_active_max, int row_tiles) {
     return ((size_t)P / 128 + (size_t)n_active_max + 1) * (size_t)row_tiles;
