@@ -24,7 +24,9 @@ __all__ = ["lib", "LIB_PATH", "DracoMoeLayer", "M6MoeP", "layer_desc", "forward"
            "bailing_moe", "moe_tok", "last_error", "DracoError"]
 
 PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG, "libdraco_moe_b200.so")
+# DRACO_B200_LIB selects another build of the library (same ABI), e.g. one made with
+# different compile-time tuning flags
+LIB_PATH = os.environ.get("DRACO_B200_LIB") or os.path.join(PKG, "libdraco_moe_b200.so")
 
 _f = ct.POINTER(ct.c_float)
 _i = ct.POINTER(ct.c_int)

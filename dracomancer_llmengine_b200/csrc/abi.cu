@@ -621,8 +621,8 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
     const int na_max = std::min(a.E, (int)n);
     const size_t o_xs = cv.take<__half>(b.use_tc ? n * a.n_in : 0);
     const size_t o_ah = cv.take<__half>(b.use_tc ? n * a.inter : 0);
-    const size_t o_igu = cv.take<int4>(b.use_tc ? tc_items_capacity((int)n, na_max, a.inter / 128) : 0);
-    const size_t o_idn = cv.take<int4>(b.use_tc ? tc_items_capacity((int)n, na_max, a.n_out / 128) : 0);
+    const size_t o_igu = cv.take<int4>(b.use_tc ? tc_items_capacity((int)n, na_max, tc_tiles_gateup(a.inter)) : 0);
+    const size_t o_idn = cv.take<int4>(b.use_tc ? tc_items_capacity((int)n, na_max, tc_tiles_down(a.n_out)) : 0);
     const size_t o_ni = cv.take<int>(2), o_terr = cv.take<int>(1);
     if (int rc = ensure_ws(c, cv.off)) return rc;
     char* w = c->ws;
@@ -708,8 +708,9 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         if (stats) {
             cudaStreamSynchronize(s);
             static const char* names[kTcStatSites] = {"prod_raw_empty", "prod_b_empty", "mma_acc_empty", "mma_b_full",
-                                                      "mma_a_full", "deq_raw_full", "deq_a_empty", "deq_acc_full",
-                                                      "deq_total", "mma_total", "deq_decode", "deq_store", "deq_epi"};
+                                                      "mma_a_full", "deq_raw_full", "deq_a_empty", "epi_acc_full",
+                                                      "deq_total", "mma_total", "deq_decode", "deq_store", "epi_work",
+                                                      "mma_test", "mma_issue"};
             for (int k = 0; k < 2; k++) {
                 fprintf(stderr, "[tc stats %s]", k ? "down" : "gateup");
                 for (int i = 0; i < kTcStatSites; i++) fprintf(stderr, " %s=%.3g", names[i], (double)stats[k * kTcStatSites + i]);

@@ -1,19 +1,26 @@
 // Grouped expert GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulators, TMA).
 //
-// One work item = (expert e, 128-row tile of its weight matrix, up to 128 of its tokens in
+// One work item = (expert e, 128-row tile of weight rows, up to 128 of its tokens in
 // expert-sorted order).  Per item the CTA computes D[row][tok] = sum_k W[row][k] * B[tok][k]
 // with K = the matrix row length:
-//   gate/up mode: two matrices (gate, up) share B = the tokens' activations; the epilogue writes
+//   gate/up mode: the 128 rows are 64 gate rows and the same 64 rows of up, interleaved so
+//                 that TMEM lanes i and i^8 of every warp quarter hold gate and up of one
+//                 intermediate row; B = the tokens' activations; the epilogue writes
 //                 act = silu(gate) * up as fp16, the B operand of the down GEMM;
-//   down mode:    one matrix, B = act; the epilogue writes y (fp32) for the combine.
+//   down mode:    128 rows of the down matrix, B = act; the epilogue writes y (fp32).
 //
-// Data path per 256-value superblock column of a matrix:
+// Data path per 256-value superblock column of the tile:
 //   TMA (no multicast) copies the 128 rows' raw superblocks (Q4_K 144 B, Q6_K 224 B padded)
-//   into a shared-memory ring -> 16 dequant warps (4 warpgroups, thread = weight row) decode
+//   into a shared-memory ring -> 16 dequant warps (4 warpgroups, thread = TMEM lane) decode
 //   64 values at a time to fp16 in registers and store them into TMEM (tcgen05.st), where
 //   they are the MMA's A operand -> one elected thread issues tcgen05.mma.kind::f16 with the
-//   activations' fp16 tile (TMA, 128-byte swizzle) as the B operand and fp32 accumulators in
-//   TMEM -> the dequant warps read the accumulators back (tcgen05.ld) for the epilogue.
+//   activations' fp16 tile (TMA, 128-byte swizzle) as the B operand into one of two fp32
+//   accumulators in TMEM -> an epilogue warpgroup reads the other accumulator back
+//   (tcgen05.ld) while the next item's MMAs run.
+// A K step is half a superblock column (8 MMAs of K = 16); four steps are in flight.  The
+// issuing thread tests the readiness of step q + 1 before it issues step q (an mbarrier wait
+// costs that thread a few hundred cycles during which it cannot issue), and one
+// tcgen05.commit per step releases both the step's A slot and its activation stage.
 // Every wait on an mbarrier is bounded; on a timeout the CTA records an error code, stops
 // issuing work, drains what it issued and frees its TMEM.
 //
@@ -26,6 +33,17 @@
 #include "tc_gemm.cuh"
 
 #include <cstdio>
+#include <mutex>
+
+#ifndef DRACO_TC_RAW_STAGES_Q4K
+#define DRACO_TC_RAW_STAGES_Q4K 5
+#endif
+#ifndef DRACO_TC_RAW_STAGES_Q6K
+#define DRACO_TC_RAW_STAGES_Q6K 3
+#endif
+#ifndef DRACO_TC_SUSPEND_NS
+#define DRACO_TC_SUSPEND_NS 1000
+#endif
 
 namespace draco {
 namespace tc {
@@ -34,16 +52,18 @@ constexpr int kDeqWarps = 16;                 // 4 warpgroups
 constexpr int kProdWarp = 16;                 // TMA producer of the weight superblocks
 constexpr int kMmaWarp = 17;                  // MMA issuer, TMEM owner
 constexpr int kBProdWarp = 18;                // TMA producer of the activation tiles
-constexpr int kThreads = 32 * 19;
-constexpr int kMaxRawStages = 8;              // raw superblock-column stages (one matrix each)
-constexpr int kBStages = 4;                   // k64 activation stages
-constexpr int kASlots = 8;                    // k64 A slots in TMEM
-constexpr int kBStageBytes = 128 * 128;       // 128 tokens x 64 halves
+constexpr int kEpiWarp0 = 19;                 // epilogue warpgroup: warps 19..22
+constexpr int kThreads = 32 * 23;
+constexpr int kMaxRawStages = 8;              // raw superblock-column stages
+constexpr int kSlots = 4;                     // K steps in flight: A slots in TMEM = activation stages
+constexpr int kBSubBytes = 128 * 128;         // activation tile of one 64-wide K chunk: 128 tokens x 64 halves
+constexpr int kBStageBytes = 2 * kBSubBytes;  // one K step = half a superblock column (128 values)
 constexpr int kTmemCols = 512;
-constexpr int kAccCols = 128;                 // per accumulator (N <= 128)
-constexpr int kABase = 256;                   // A slots start here (after 2 accumulators)
-constexpr long kSpinLimit = 1L << 21;         // bounded waits: polls of at most kSuspendNs each
-constexpr uint32_t kSuspendNs = 1000;         // try_wait may suspend the thread up to this long
+constexpr int kAccCols = 128;                 // per accumulator buffer (N <= 128)
+constexpr int kABase = 256;                   // A slots (64 columns each) start here
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // bounded waits give up after 2 s
+// try_wait may suspend the polling thread up to this long (0: poll with test_wait)
+constexpr uint32_t kSuspendNs = DRACO_TC_SUSPEND_NS;
 
 // error codes written to *err
 constexpr int kErrTimeout = 0x100;
@@ -65,20 +85,37 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 }
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
-        : "memory");
+    if (kSuspendNs == 0)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+            : "memory");
     return ok != 0;
 }
-// Bounded wait: returns false (and raises the CTA's abort flag) on timeout or when another
-// role already aborted.
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: returns false (and raises the CTA's abort flag) after kWaitLimitNs, or when
+// another role already aborted (checked every 64 polls).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
                                           int where) {
-    for (long i = 0; i < kSpinLimit; i++) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; i++) {
         if (mbar_try(bar, parity)) return true;
-        if (*abort_flag) return false;
+        if ((i & 63) == 0) {
+            if (*abort_flag) return false;
+            if (global_ns() - t0 > kWaitLimitNs) break;
+        }
     }
     *abort_flag = 1;
     atomicOr(err, kErrTimeout | where);
@@ -89,10 +126,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // warp-collective tcgen05 instructions).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
                                           int where) {
-    for (long i = 0; i < kSpinLimit; i++) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; i++) {
         const bool done = mbar_try(bar, parity);
         if (__all_sync(0xffffffffu, done)) return true;
-        if (__shfl_sync(0xffffffffu, *abort_flag, 0)) return false;
+        if ((i & 63) == 63) {
+            int stop = 0;
+            if ((threadIdx.x & 31) == 0) {
+                if (*abort_flag) stop = 1;
+                else if (t0 == 0) t0 = global_ns();
+                else if (global_ns() - t0 > kWaitLimitNs) stop = 2;
+            }
+            stop = __shfl_sync(0xffffffffu, stop, 0);
+            if (stop == 1) return false;
+            if (stop == 2) break;
+        }
     }
     if ((threadIdx.x & 31) == 0) {
         *abort_flag = 1;
@@ -101,30 +149,60 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     __syncwarp();
     return false;
 }
+// one lane of the (converged) warp
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(pred));
+    return pred != 0;
+}
+// Non-blocking test of two barriers' phases in one instruction group (one pass through the
+// shared-memory pipe instead of two)
+__device__ __forceinline__ bool mbar_test2(uint64_t* a, uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %3;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 q, [%2], %3;\n\tand.pred p, p, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(a)), "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // Drain wait: bounded, does not give up early on the abort flag.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-    for (long i = 0; i < kSpinLimit && !mbar_try(bar, parity); i++) {
-    }
+    if (mbar_try(bar, parity)) return;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1; !mbar_try(bar, parity); i++)
+        if ((i & 63) == 0 && global_ns() - t0 > kWaitLimitNs) return;
 }
 
-// Optional wait statistics: cycles a role spends in each wait site, summed over warps
-// (one lane per warp) into stats[site]; enabled when the kernel gets a stats pointer.
+// Optional wait statistics (kernels instantiated with STATS): cycles a role spends in each
+// wait site, summed over warps (one lane per warp) into stats[site].
 enum StatSite {
     kStProdRawEmpty = 0, kStProdBEmpty, kStMmaAccEmpty, kStMmaBFull, kStMmaAFull, kStDeqRawFull, kStDeqAEmpty,
-    kStDeqAccFull, kStDeqTotal, kStMmaTotal, kStDeqDecode, kStDeqStore, kStDeqEpi, kStSites
+    kStEpiAccFull, kStDeqTotal, kStMmaTotal, kStDeqDecode, kStDeqStore, kStEpiWork, kStMmaTest, kStMmaIssue,
+    kStSites
 };
+template <bool EN>
 struct StatTimer {
-    unsigned long long acc[kStSites];
+    unsigned long long acc[EN ? kStSites : 1];
     long long t;
-    __device__ void reset() {
-        for (int i = 0; i < kStSites; i++) acc[i] = 0;
+    __device__ __forceinline__ void reset() {
+        if (EN)
+            for (int i = 0; i < kStSites; i++) acc[i] = 0;
     }
-    __device__ __forceinline__ void start() { t = clock64(); }
-    __device__ __forceinline__ void stop(int site) { acc[site] += (unsigned long long)(clock64() - t); }
+    __device__ __forceinline__ void start() {
+        if (EN) t = clock64();
+    }
+    __device__ __forceinline__ void stop(int site) {
+        if (EN) acc[site] += (unsigned long long)(clock64() - t);
+    }
+    __device__ __forceinline__ void total(int site, long long t0) {
+        if (EN) acc[site] = (unsigned long long)(clock64() - t0);
+    }
     __device__ void flush(unsigned long long* stats) {
-        if (!stats) return;
-        for (int i = 0; i < kStSites; i++)
-            if (acc[i]) atomicAdd(stats + i, acc[i]);
+        if (EN && stats)
+            for (int i = 0; i < kStSites; i++)
+                if (acc[i]) atomicAdd(stats + i, acc[i]);
     }
 };
 
@@ -135,6 +213,28 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         "[%4];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+// the same with an L2 eviction-priority policy (createpolicy)
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
 }
 
 // ---------------------------------------------------------------- tcgen05
@@ -292,32 +392,43 @@ __device__ __forceinline__ void deq_q6k(const uint8_t* blk, int kc, uint32_t (&o
 // ---------------------------------------------------------------- the kernel
 template <int MODE, int CODE>
 struct Cfg {
-    static constexpr int kMats = MODE == 0 ? 2 : 1;
     static constexpr int kBB = CODE == DRACO_CODE_Q4_K ? 144 : kQ6Padded;   // raw bytes per row superblock
     static constexpr int kRawStage = 128 * kBB;
-    // as many weight stages as fit next to the activation ring (227 KB per block)
-    static constexpr int kRawStages = CODE == DRACO_CODE_Q4_K ? 8 : 5;
-    // raw stage consumers: gate/up -> 2 warpgroups x 4 warps; down -> 4 x 4
-    static constexpr int kRawConsumers = MODE == 0 ? 8 : 16;
+    // weight stages next to the four 32 KB activation stages (227 KB per block)
+    static constexpr int kRawStages = CODE == DRACO_CODE_Q4_K ? DRACO_TC_RAW_STAGES_Q4K : DRACO_TC_RAW_STAGES_Q6K;
     static constexpr int kBOff = kRawStages * kRawStage;                 // 1024-aligned below
     static constexpr int kBOffAligned = (kBOff + 1023) / 1024 * 1024;
-    static constexpr int kBarOff = kBOffAligned + kBStages * kBStageBytes;
+    static constexpr int kBarOff = kBOffAligned + kSlots * kBStageBytes;
     static constexpr int kSmem = kBarOff + 1024 + 1024;                    // barriers + alignment slack
+    static_assert(kRawStages <= kMaxRawStages && kSmem <= 232448, "shared memory");
+};
+
+// activation tensor maps, one per token-tile height R = 16 (i + 1): 3D view
+// {64 halves, rows, K / 64 chunks} with box {64, R, 2}, so that one copy brings a K step's two
+// 64-wide chunks for R tokens as two SW128 tiles of R rows (tile c at byte c * R * 128)
+struct ActMaps {
+    CUtensorMap m[8];
 };
 
 struct Bars {
     uint64_t raw_full[kMaxRawStages], raw_empty[kMaxRawStages];
-    uint64_t b_full[kBStages], b_empty[kBStages];
-    uint64_t a_full[kASlots], a_empty[kASlots];
-    uint64_t acc_full, acc_empty, drain;
+    uint64_t a_full[kSlots], b_full[kSlots];
+    uint64_t done[kSlots];                     // done[q % 4]: MMAs of K step q finished
+    uint64_t acc_full[2], acc_empty[2], drain;
     uint32_t tmem_base;
     int abort_flag;
 };
 
-template <int MODE, int CODE>
+// TMEM lane m (= 32 * quarter + i) of a gate/up tile holds raw row
+//   gate: 16*quarter + ((i & 16) >> 1) + (i & 7)         for (i & 8) == 0
+//   up:   64 + the same                                  for (i & 8) != 0
+// so lanes i and i^8 hold gate and up of one intermediate row; down tiles are unpermuted.
+__device__ __forceinline__ int gu_row(int quarter, int i) { return 16 * quarter + ((i & 16) >> 1) + (i & 7); }
+
+template <int MODE, int CODE, bool STATS>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
-                  const __grid_constant__ CUtensorMap tmB, const int4* __restrict__ items,
+                  const __grid_constant__ ActMaps tmB, const int4* __restrict__ items,
                   const int* __restrict__ n_items_p, int rows_per_expert, int K, int out_ld,
                   __half* __restrict__ act_out, float* __restrict__ y_out, int* __restrict__ err,
                   unsigned long long* __restrict__ stats) {
@@ -333,23 +444,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_items = *n_items_p;
-    const int nb = K / 256;
+    const int nb = K / 256;   // superblock columns per item; K steps per item = 2 * nb
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < C::kRawStages; i++) {
             mbar_init(&bars->raw_full[i], 1);
-            mbar_init(&bars->raw_empty[i], C::kRawConsumers);
+            mbar_init(&bars->raw_empty[i], kDeqWarps);
         }
-        for (int i = 0; i < kBStages; i++) {
+        for (int i = 0; i < kSlots; i++) {
+            mbar_init(&bars->a_full[i], kDeqWarps / 2);
             mbar_init(&bars->b_full[i], 1);
-            mbar_init(&bars->b_empty[i], 1);
+            mbar_init(&bars->done[i], 1);
         }
-        for (int i = 0; i < kASlots; i++) {
-            mbar_init(&bars->a_full[i], 4);
-            mbar_init(&bars->a_empty[i], 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&bars->acc_full[i], 1);
+            mbar_init(&bars->acc_empty[i], 4);
         }
-        mbar_init(&bars->acc_full, 1);
-        mbar_init(&bars->acc_empty, kDeqWarps);
         mbar_init(&bars->drain, 1);
         bars->abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -365,206 +475,231 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
-    StatTimer st;
+    StatTimer<STATS> st;
     st.reset();
-    const long long t_begin = clock64();
+    const long long t_begin = STATS ? clock64() : 0;
 
+    // The three issuing roles run warp-converged loops (every lane waits and computes the same
+    // values, so they stay in uniform registers) and one elected lane issues each TMA copy,
+    // MMA and commit.
     if (warp == kProdWarp) {
         // ------------------------------------------------------------ weight producer
-        if (lane == 0) {
-            uint32_t rq = 0;   // weight fills issued so far
-            for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
-                const int4 item = items[it];
-                const int arow = item.x * rows_per_expert + item.y * 128;
-                for (int sb = 0; sb < nb && !*abort_flag; sb++) {
-                    for (int m = 0; m < C::kMats; m++, rq++) {
-                        const int s = rq % C::kRawStages;
-                        st.start();
-                        const bool w_ok = mbar_wait(&bars->raw_empty[s], ((rq / C::kRawStages) & 1) ^ 1, abort_flag, err, 1);
-                        st.stop(kStProdRawEmpty);
-                        if (!w_ok) break;
-                        mbar_expect_tx(&bars->raw_full[s], C::kRawStage);
-                        tma_load_2d(raw + s * C::kRawStage, m == 0 ? &tmA0 : &tmA1, sb * (C::kBB / 4), arow,
-                                    &bars->raw_full[s]);
-                    }
+        const uint64_t pol = policy_evict_first();   // weights stream through L2 once
+        uint32_t sq = 0;   // superblock columns issued so far
+        bool ok = true;
+        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+            const int4 item = items[it];
+            const int row0 = item.x * rows_per_expert + item.y * (MODE == 0 ? 64 : 128);
+            for (int sb = 0; sb < nb; sb++, sq++) {
+                const int s = sq % C::kRawStages;
+                st.start();
+                ok = warp_wait(&bars->raw_empty[s], ((sq / C::kRawStages) & 1) ^ 1, abort_flag, err, 1);
+                st.stop(kStProdRawEmpty);
+                if (!ok) break;
+                if (elect_one()) {
+                    uint8_t* dst = raw + s * C::kRawStage;
+                    mbar_expect_tx(&bars->raw_full[s], C::kRawStage);
+                    tma_load_2d_hint(dst, &tmA0, sb * (C::kBB / 4), row0, &bars->raw_full[s], pol);
+                    tma_load_2d_hint(dst + 64 * C::kBB, MODE == 0 ? &tmA1 : &tmA0, sb * (C::kBB / 4),
+                                     MODE == 0 ? row0 : row0 + 64, &bars->raw_full[s], pol);
                 }
+                __syncwarp();
             }
-            if (*abort_flag)   // drain: the most recent fills land before the CTA exits
-                for (uint32_t k = 0; k < (uint32_t)C::kRawStages && k < rq; k++) {
-                    const uint32_t q = rq - 1 - k;
-                    mbar_drain(&bars->raw_full[q % C::kRawStages], (q / C::kRawStages) & 1);
-                }
         }
+        if (!ok)   // drain: the most recent fills land before the CTA exits
+            for (uint32_t k = 0; k < (uint32_t)C::kRawStages && k < sq; k++) {
+                const uint32_t q = sq - 1 - k;
+                mbar_drain(&bars->raw_full[q % C::kRawStages], (q / C::kRawStages) & 1);
+            }
     } else if (warp == kBProdWarp) {
         // ------------------------------------------------------------ activation producer
-        if (lane == 0) {
-            uint32_t bq = 0;
-            for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
-                const int4 item = items[it];
-                const int p0 = item.z, nbox = (item.w + 15) >> 4;
-                for (int sb = 0; sb < nb && !*abort_flag; sb++) {
-                    for (int kc = 0; kc < 4; kc++, bq++) {
-                        const int s = bq % kBStages;
-                        st.start();
-                        const bool w_ok = mbar_wait(&bars->b_empty[s], ((bq / kBStages) & 1) ^ 1, abort_flag, err, 2);
-                        st.stop(kStProdBEmpty);
-                        if (!w_ok) break;
-                        mbar_expect_tx(&bars->b_full[s], nbox * 16 * 128);
-                        for (int j = 0; j < nbox; j++)
-                            tma_load_2d(bt + s * kBStageBytes + j * 2048, &tmB, sb * 256 + kc * 64, p0 + 16 * j,
-                                        &bars->b_full[s]);
-                    }
+        uint32_t q = 0;   // K steps issued so far
+        bool ok = true;
+        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+            const int4 item = items[it];
+            const int p0 = item.z, nbox = (item.w + 15) >> 4;
+            const CUtensorMap* map = &tmB.m[nbox - 1];
+            for (int s2 = 0; s2 < 2 * nb; s2++, q++) {
+                const int bs = q % kSlots;
+                if (q >= (uint32_t)kSlots) {   // stage reused: step q - 4 finished
+                    st.start();
+                    ok = warp_wait(&bars->done[bs], ((q - kSlots) / kSlots) & 1, abort_flag, err, 2);
+                    st.stop(kStProdBEmpty);
+                    if (!ok) break;
                 }
+                if (elect_one()) {
+                    mbar_expect_tx(&bars->b_full[bs], 2 * nbox * 16 * 128);
+                    tma_load_3d(bt + bs * kBStageBytes, map, 0, p0, 2 * s2, &bars->b_full[bs]);
+                }
+                __syncwarp();
             }
-            if (*abort_flag)
-                for (uint32_t k = 0; k < kBStages && k < bq; k++) {
-                    const uint32_t q = bq - 1 - k;
-                    mbar_drain(&bars->b_full[q % kBStages], (q / kBStages) & 1);
-                }
         }
+        if (!ok)
+            for (uint32_t k = 0; k < (uint32_t)kSlots && k < q; k++) {
+                const uint32_t r = q - 1 - k;
+                mbar_drain(&bars->b_full[r % kSlots], (r / kSlots) & 1);
+            }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            uint32_t u = 0, bq = 0, n_done = 0;
-            bool ok = true;
-            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, n_done++) {
-                const int4 item = items[it];
-                const int ntok = item.w;
-                const int nmma = ((ntok + 15) >> 4) << 4;
-                const uint32_t idesc = idesc_f16(nmma);
-                if (n_done > 0) {
-                    // the epilogue of the previous item must have read the accumulators
-                    st.start();
-                    ok = mbar_wait(&bars->acc_empty, (n_done - 1) & 1, abort_flag, err, 3);
-                    st.stop(kStMmaAccEmpty);
-                    if (!ok) break;
-                    tc_fence_after();
-                }
-                for (int sb = 0; sb < nb && ok; sb++) {
-                    for (int kc = 0; kc < 4 && ok; kc++, bq++) {
-                        const int bs = bq % kBStages;
-                        st.start();
-                        ok = mbar_wait(&bars->b_full[bs], (bq / kBStages) & 1, abort_flag, err, 4);
-                        st.stop(kStMmaBFull);
-                        if (!ok) break;
-                        const uint32_t b_addr = smem_u32(bt + bs * kBStageBytes);
-                        for (int m = 0; m < C::kMats; m++, u++) {
-                            const int as = u % kASlots;
-                            st.start();
-                            ok = mbar_wait(&bars->a_full[as], (u / kASlots) & 1, abort_flag, err, 5);
-                            st.stop(kStMmaAFull);
-                            if (!ok) break;
-                            tc_fence_after();
-                            const uint32_t a_tm = tmem + kABase + 32 * as;
-                            const uint32_t d_tm = tmem + m * kAccCols;
-#pragma unroll
-                            for (int j = 0; j < 4; j++)
-                                tc_mma_ts(d_tm, a_tm + 8 * j, sdesc_sw128(b_addr + 32 * j), idesc,
-                                          (sb | kc | j) != 0 ? 1u : 0u);
-                            tc_commit(&bars->a_empty[as]);
-                        }
-                        if (ok) tc_commit(&bars->b_empty[bs]);
-                    }
-                }
-                if (ok) tc_commit(&bars->acc_full);
-            }
-            // every issued MMA must finish before TMEM is released
-            tc_commit(&bars->drain);
-            mbar_drain(&bars->drain, 0);
-        }
-    } else {
-        // ------------------------------------------------------------ dequant + epilogue
-        const int wg = warp >> 2, quarter = warp & 3;
-        const int row = quarter * 32 + lane;                         // tile row = TMEM lane
-        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        uint32_t u = 0, rq = 0, n_done = 0;
+        const uint64_t desc0 = sdesc_sw128(smem_u32(bt));
+        uint32_t q = 0, n_done = 0;
         bool ok = true;
         for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, n_done++) {
             const int4 item = items[it];
-            const int mt = item.y, p0 = item.z, ntok = item.w;
-            for (int sb = 0; sb < nb && ok; sb++) {
-                const uint32_t rq0 = rq;
-                rq += C::kMats;
-                for (int kc = 0; kc < 4 && ok; kc++) {
-                    for (int m = 0; m < C::kMats && ok; m++, u++) {
-                        if ((int)(u & 3) != wg) continue;
-                        const uint32_t q = rq0 + m;
-                        const int rs = q % C::kRawStages;
-                        st.start();
-                        ok = warp_wait(&bars->raw_full[rs], (q / C::kRawStages) & 1, abort_flag, err, 7);
-                        st.stop(kStDeqRawFull);
-                        if (!ok) break;
-                        const int as = u % kASlots;
-                        st.start();
-                        ok = warp_wait(&bars->a_empty[as], ((u / kASlots) & 1) ^ 1, abort_flag, err, 8);
-                        st.stop(kStDeqAEmpty);
-                        if (!ok) break;
-                        tc_fence_after();
-                        uint32_t v[32];
-                        const uint8_t* blk = raw + rs * C::kRawStage + row * C::kBB;
-                        st.start();
-                        if (CODE == DRACO_CODE_Q4_K) deq_q4k(blk, kc, v);
-                        else deq_q6k(blk, kc, v);
-                        st.stop(kStDeqDecode);
-                        // last read of this raw stage by this warpgroup: release it
-                        const bool last = MODE == 0 ? (kc >= 2) : true;
-                        __syncwarp();
-                        if (last && lane == 0) mbar_arrive(&bars->raw_empty[rs]);
-                        st.start();
-                        tc_st32(tmem + lane_base + kABase + 32 * as, v);
-                        tc_wait_st();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&bars->a_full[as]);
-                        st.stop(kStDeqStore);
-                    }
-                }
+            const int nbox = (item.w + 15) >> 4;
+            const uint32_t idesc = idesc_f16(nbox * 16);
+            const uint32_t sub = (uint32_t)nbox * (16 * 128 >> 4);   // second chunk's tile, 16-byte units
+            const int buf = n_done & 1;
+            if (n_done >= 2) {   // the epilogue of item n_done - 2 has read this buffer
+                st.start();
+                ok = warp_wait(&bars->acc_empty[buf], ((n_done >> 1) & 1) ^ 1, abort_flag, err, 3);
+                st.stop(kStMmaAccEmpty);
+                if (!ok) break;
+                tc_fence_after();
             }
-            if (!ok) break;
-            // epilogue: this warpgroup's 32-token column block of the accumulators
+            const uint32_t d_tm = tmem + buf * kAccCols;
+            bool rdy = __all_sync(0xffffffffu, mbar_test2(&bars->a_full[q % kSlots], &bars->b_full[q % kSlots],
+                                                          (q / kSlots) & 1));
+            for (int s2 = 0; s2 < 2 * nb; s2++, q++) {
+                const int sl = q % kSlots;
+                const uint32_t par = (q / kSlots) & 1;
+                if (!rdy) {
+                    st.start();
+                    ok = warp_wait(&bars->a_full[sl], par, abort_flag, err, 5);
+                    st.stop(kStMmaAFull);
+                    if (!ok) break;
+                    st.start();
+                    ok = warp_wait(&bars->b_full[sl], par, abort_flag, err, 4);
+                    st.stop(kStMmaBFull);
+                    if (!ok) break;
+                }
+                tc_fence_after();
+                // readiness of the next step, tested before this step's MMAs are issued
+                st.start();
+                if (s2 + 1 < 2 * nb)
+                    rdy = __all_sync(0xffffffffu, mbar_test2(&bars->a_full[(q + 1) % kSlots],
+                                                             &bars->b_full[(q + 1) % kSlots], ((q + 1) / kSlots) & 1));
+                st.stop(kStMmaTest);
+                st.start();
+                const uint32_t a_tm = tmem + kABase + 64 * sl;
+                const uint64_t bd = desc0 + (uint64_t)(sl * (kBStageBytes >> 4));
+                if (elect_one()) {
+#pragma unroll
+                    for (int c = 0; c < 2; c++) {
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            tc_mma_ts(d_tm, a_tm + 32 * c + 8 * j, bd + (uint64_t)(c * sub + 2 * j), idesc,
+                                      (s2 | c | j) != 0 ? 1u : 0u);
+                    }
+                    tc_commit(&bars->done[sl]);
+                }
+                __syncwarp();
+                st.stop(kStMmaIssue);
+            }
+            if (ok && elect_one()) tc_commit(&bars->acc_full[buf]);
+            __syncwarp();
+        }
+        // every issued MMA must finish before TMEM is released
+        if (elect_one()) {
+            tc_commit(&bars->drain);
+            mbar_drain(&bars->drain, 0);
+        }
+        __syncwarp();
+    } else if (warp < kDeqWarps) {
+        // ------------------------------------------------------------ dequant
+        // warpgroup wg decodes the 64-value chunk wg of every superblock column, i.e. half
+        // (wg & 1) of K step 2 * column + (wg >> 1)
+        const int wg = warp >> 2, quarter = warp & 3;
+        const int row = MODE == 0 ? ((lane >> 3) & 1) * 64 + gu_row(quarter, lane) : quarter * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        uint32_t sq = 0;   // superblock columns consumed
+        bool ok = true;
+        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+            for (int sb = 0; sb < nb; sb++, sq++) {
+                const uint32_t q = 2 * sq + (wg >> 1);   // this warpgroup's K step
+                const int rs = sq % C::kRawStages, sl = q % kSlots;
+                st.start();
+                ok = warp_wait(&bars->raw_full[rs], (sq / C::kRawStages) & 1, abort_flag, err, 7);
+                st.stop(kStDeqRawFull);
+                if (!ok) break;
+                st.start();
+                ok = warp_wait(&bars->done[sl], ((q / kSlots) & 1) ^ 1, abort_flag, err, 8);
+                st.stop(kStDeqAEmpty);
+                if (!ok) break;
+                tc_fence_after();
+                uint32_t v[32];
+                const uint8_t* blk = raw + rs * C::kRawStage + row * C::kBB;
+                st.start();
+                if (CODE == DRACO_CODE_Q4_K) deq_q4k(blk, wg, v);
+                else deq_q6k(blk, wg, v);
+                st.stop(kStDeqDecode);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->raw_empty[rs]);
+                st.start();
+                tc_st32(tmem + lane_base + kABase + 64 * sl + 32 * (wg & 1), v);
+                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->a_full[sl]);
+                st.stop(kStDeqStore);
+            }
+        }
+        st.total(kStDeqTotal, t_begin);
+    } else if (warp >= kEpiWarp0) {
+        // ------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        uint32_t n_done = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x, n_done++) {
+            const int4 item = items[it];
+            const int mt = item.y, p0 = item.z, ntok = item.w;
+            const int buf = n_done & 1;
             st.start();
-            ok = warp_wait(&bars->acc_full, n_done & 1, abort_flag, err, 9);
-            st.stop(kStDeqAccFull);
+            const bool ok = warp_wait(&bars->acc_full[buf], (n_done >> 1) & 1, abort_flag, err, 9);
+            st.stop(kStEpiAccFull);
             if (!ok) break;
             st.start();
             tc_fence_after();
-            const int t0 = wg * 32;
-            const int orow = mt * 128 + row;
-            // two 16-column halves keep 32 accumulator registers live at a time
-#pragma unroll
-            for (int hh = 0; hh < 2; hh++) {
-                const int tb = t0 + 16 * hh;
-                if (tb < ntok) {
-                    uint32_t g[16], up[16];
-                    tc_ld16(tmem + lane_base + tb, g);
-                    if (MODE == 0) tc_ld16(tmem + lane_base + kAccCols + tb, up);
+            const uint32_t acc = tmem + lane_base + buf * kAccCols;
+            if (MODE == 0) {
+                // lanes i (gate) and i ^ 8 (up) share an intermediate row; per column pair the
+                // gate lane finishes the even column and the up lane the odd one
+                const bool is_up = (lane & 8) != 0;
+                const int orow = mt * 64 + gu_row(quarter, lane);
+                for (int tb = 0; tb < ntok; tb += 16) {
+                    uint32_t v[16];
+                    tc_ld16(acc + tb, v);
                     tc_wait_ld();
-                    const int nt = min(16, ntok - tb);
-                    if (MODE == 0) {
-                        __half* dst = act_out + (size_t)(p0 + tb) * out_ld + orow;
 #pragma unroll
-                        for (int t = 0; t < 16; t++) {
-                            if (t < nt) {
-                                const float gv = __uint_as_float(g[t]), uv = __uint_as_float(up[t]);
-                                dst[(size_t)t * out_ld] = __float2half_rn(gv / (1.f + __expf(-gv)) * uv);
-                            }
-                        }
-                    } else {
-                        float* dst = y_out + (size_t)(p0 + tb) * out_ld + orow;
-#pragma unroll
-                        for (int t = 0; t < 16; t++)
-                            if (t < nt) dst[(size_t)t * out_ld] = __uint_as_float(g[t]);
+                    for (int c = 0; c < 16; c += 2) {
+                        const float mine_e = __uint_as_float(v[c]), mine_o = __uint_as_float(v[c + 1]);
+                        const float other = __shfl_xor_sync(0xffffffffu, is_up ? mine_e : mine_o, 8);
+                        const float g = is_up ? other : mine_e, u = is_up ? mine_o : other;
+                        const int col = tb + c + (is_up ? 1 : 0);
+                        if (col < ntok)
+                            act_out[(size_t)(p0 + col) * out_ld + orow] = __float2half_rn(g / (1.f + __expf(-g)) * u);
                     }
+                }
+            } else {
+                const int orow = mt * 128 + quarter * 32 + lane;
+                for (int tb = 0; tb < ntok; tb += 16) {
+                    uint32_t v[16];
+                    tc_ld16(acc + tb, v);
+                    tc_wait_ld();
+                    float* dst = y_out + (size_t)(p0 + tb) * out_ld + orow;
+                    const int nt = min(16, ntok - tb);
+#pragma unroll
+                    for (int t = 0; t < 16; t++)
+                        if (t < nt) dst[(size_t)t * out_ld] = __uint_as_float(v[t]);
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->acc_empty);
-            st.stop(kStDeqEpi);
+            if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+            st.stop(kStEpiWork);
         }
-        st.acc[kStDeqTotal] = (unsigned long long)(clock64() - t_begin);
     }
-    if (warp == kMmaWarp) st.acc[kStMmaTotal] = (unsigned long long)(clock64() - t_begin);
+    if (warp == kMmaWarp) st.total(kStMmaTotal, t_begin);
     if (lane == 0) st.flush(stats);
     tc_fence_before();
     __syncthreads();
@@ -642,39 +777,82 @@ bool get_encode() {
     return true;
 }
 
-// weights [rows_total][row_bytes] viewed as uint32 elements, box = one superblock column x 128 rows
+// weights [rows_total][row_bytes] viewed as uint32 elements, box = one superblock column x 64 rows
 bool map_weights(CUtensorMap* m, const void* base, size_t rows_total, size_t row_bytes_, int bb) {
     const cuuint64_t dims[2] = {row_bytes_ / 4, rows_total};
     const cuuint64_t strides[1] = {row_bytes_};
-    const cuuint32_t box[2] = {(cuuint32_t)(bb / 4), 128};
+    const cuuint32_t box[2] = {(cuuint32_t)(bb / 4), 64};
     const cuuint32_t es[2] = {1, 1};
     return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, es,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// activations [P][K] fp16, box 64 x 16 rows, 128-byte swizzle (the UMMA K-major SW128 layout)
-bool map_acts(CUtensorMap* m, const void* base, size_t P, size_t K) {
-    const cuuint64_t dims[2] = {K, P};
-    const cuuint64_t strides[1] = {K * 2};
-    const cuuint32_t box[2] = {64, 16};
-    const cuuint32_t es[2] = {1, 1};
-    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+// activations [P][K] fp16 as {64 halves, P rows, K/64 chunks}; box {64, 16 (i + 1), 2},
+// 128-byte swizzle (the UMMA K-major SW128 layout)
+bool map_acts(tc::ActMaps* m, const void* base, size_t P, size_t K) {
+    const cuuint64_t dims[3] = {64, P, K / 64};
+    const cuuint64_t strides[2] = {K * 2, 128};
+    const cuuint32_t es[3] = {1, 1, 1};
+    for (int i = 0; i < 8; i++) {
+        const cuuint32_t box[3] = {64, (cuuint32_t)(16 * (i + 1)), 2};
+        if (g_encode(&m->m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    return true;
+}
+// encoded maps of the last few (buffer, rows, K), shared by all calls of the process
+bool cached_act_maps(tc::ActMaps* out, const void* base, size_t P, size_t K) {
+    struct Entry {
+        const void* base;
+        size_t P, K;
+        tc::ActMaps maps;
+    };
+    static std::mutex mu;
+    static Entry cache[4];
+    static int next = 0;
+    std::lock_guard<std::mutex> lk(mu);
+    for (const Entry& e : cache)
+        if (e.base == base && e.P == P && e.K == K) {
+            *out = e.maps;
+            return true;
+        }
+    Entry& e = cache[next];
+    if (!map_acts(&e.maps, base, P, K)) {
+        e.base = nullptr;
+        return false;
+    }
+    e.base = base;
+    e.P = P;
+    e.K = K;
+    next = (next + 1) % 4;
+    *out = e.maps;
+    return true;
 }
 
+template <int MODE, int CODE, bool STATS>
+cudaError_t launch_tc_k(const CUtensorMap& a0, const CUtensorMap& a1, const tc::ActMaps& b, const int4* items,
+                        const int* n_items, int grid, int rows_per_expert, int K, int out_ld, __half* act, float* y,
+                        int* err, unsigned long long* stats, cudaStream_t s) {
+    using C = tc::Cfg<MODE, CODE>;
+    auto kern = tc::moe_tc_kernel<MODE, CODE, STATS>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, tc::kThreads, C::kSmem, s>>>(a0, a1, b, items, n_items, rows_per_expert, K, out_ld, act, y, err,
+                                              stats);
+    return cudaGetLastError();
+}
 template <int MODE, int CODE>
-cudaError_t launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b, const int4* items,
+cudaError_t launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const tc::ActMaps& b, const int4* items,
                       const int* n_items, int grid, int rows_per_expert, int K, int out_ld, __half* act, float* y,
                       int* err, unsigned long long* stats, cudaStream_t s) {
-    using C = tc::Cfg<MODE, CODE>;
-    cudaError_t e = cudaFuncSetAttribute(tc::moe_tc_kernel<MODE, CODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmem);
-    if (e != cudaSuccess) return e;
-    tc::moe_tc_kernel<MODE, CODE><<<grid, tc::kThreads, C::kSmem, s>>>(a0, a1, b, items, n_items, rows_per_expert, K,
-                                                                       out_ld, act, y, err, stats);
-    return cudaGetLastError();
+    if (stats)
+        return launch_tc_k<MODE, CODE, true>(a0, a1, b, items, n_items, grid, rows_per_expert, K, out_ld, act, y, err,
+                                             stats, s);
+    return launch_tc_k<MODE, CODE, false>(a0, a1, b, items, n_items, grid, rows_per_expert, K, out_ld, act, y, err,
+                                          nullptr, s);
 }
 
 }  // namespace
@@ -701,11 +879,12 @@ int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, i
            __half* Xs, __half* act_h, float* y, int4* items_gu, int* n_items_gu, int4* items_dn, int* n_items_dn,
            int* err, unsigned long long* stats, cudaStream_t s) {
     if (P <= 0) return 0;
-    CUtensorMap mx, ma;
-    if (!map_acts(&mx, Xs, (size_t)P, (size_t)n_in) || !map_acts(&ma, act_h, (size_t)P, (size_t)inter)) return -2;
+    tc::ActMaps mx, ma;
+    if (!cached_act_maps(&mx, Xs, (size_t)P, (size_t)n_in) || !cached_act_maps(&ma, act_h, (size_t)P, (size_t)inter))
+        return -2;
     tc::gather_half_kernel<<<148 * 8, 256, 0, s>>>(X, ilist, tok_div, P, n_in, Xs);
-    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, inter / 128, items_gu, n_items_gu);
-    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, n_out / 128, items_dn, n_items_dn);
+    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, tc_tiles_gateup(inter), items_gu, n_items_gu);
+    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, tc_tiles_down(n_out), items_dn, n_items_dn);
     cudaError_t e;
     if (cg == DRACO_CODE_Q4_K)
         e = launch_tc<0, DRACO_CODE_Q4_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, inter, n_in, inter, act_h,

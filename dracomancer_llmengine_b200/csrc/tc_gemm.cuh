@@ -25,7 +25,10 @@ int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, i
            __half* Xs, __half* act_h, float* y, int4* items_gu, int* n_items_gu, int4* items_dn, int* n_items_dn,
            int* err, unsigned long long* stats, cudaStream_t s);
 // wait-statistics sites per kernel (stats holds 2 * kTcStatSites counters: gate/up, down)
-constexpr int kTcStatSites = 13;
+constexpr int kTcStatSites = 15;
+// weight-row tiles per expert: gate/up tiles hold 64 rows of each matrix, down tiles 128 rows
+inline int tc_tiles_gateup(int inter) { return inter / 64; }
+inline int tc_tiles_down(int n_out) { return n_out / 128; }
 // item-list capacity for P assignments over at most n_active_max experts
 inline size_t tc_items_capacity(int P, int n_active_max, int row_tiles) {
     return ((size_t)P / 128 + (size_t)n_active_max + 1) * (size_t)row_tiles;
