@@ -59,77 +59,96 @@ __global__ void __launch_bounds__(32 * TY) router_logits_kernel(const float* __r
     }
 }
 
-// Many-warp variant: one output per thread, a 8-token x 32-expert tile per 256-thread block
-// (small shared footprint, so several blocks share an SM and hide each other's loads), k-chunks
-// of 64 staged in shared memory and read as float4 (4 consecutive k of one row); each thread
-// still walks k upward one rounded product at a time.  Rows are padded to 68 floats so the
-// expert rows a warp reads at one k fall in distinct bank groups.
-__global__ void __launch_bounds__(256) router_logits_v2(const float* __restrict__ X, const float* __restrict__ W,
-                                                        int T, int E, int H, float* __restrict__ logits) {
-    constexpr int KC = 64, LD = KC + 4, TT = 8, TE = 32;
-    constexpr int NV = (TT + TE) * (KC / 4);            // float4 slots per chunk
-    constexpr int PER = (NV + 255) / 256;               // per thread
-    __shared__ __align__(16) float xs[TT][LD];
-    __shared__ __align__(16) float ws[TE][LD];
-    const int tid = threadIdx.x, ty = tid >> 5, tx = tid & 31;
+// Tiled variant: an 8-token x 32-expert block of 4 warps; warp w owns experts 8w..8w+7 and
+// lane l the token l & 7 with the expert pair 2 (l >> 3), +1, so one float4 of a token row
+// serves two dot products and shared-memory reads stay near one wavefront per operand row
+// group.  k-chunks of 128 stream into a 3-stage shared-memory ring with cp.async (two chunks in
+// flight while one is consumed), read as float4 (4 consecutive k of one row) with the next
+// float4s fetched ahead; each dot product still walks k upward one rounded product at a time.
+// Rows are padded to 132 floats so the rows a warp reads at one k fall in distinct bank
+// groups.  Needs H % 4 == 0 and 16-byte aligned X and W.
+namespace rl {
+constexpr int KC = 128, LD = KC + 4, TT = 8, TE = 32, NS = 3, NTH = 128;
+constexpr int NV = (TT + TE) * (KC / 4);   // 16-byte copies per chunk
+constexpr int PER = NV / NTH;
+constexpr int kSmem = NS * (TT + TE) * LD * 4;
+static_assert(NV % NTH == 0, "copies per thread");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__global__ void __launch_bounds__(rl::NTH) router_logits_v2(const float* __restrict__ X, const float* __restrict__ W,
+                                                            int T, int E, int H, float* __restrict__ logits) {
+    using namespace rl;
+    extern __shared__ __align__(16) float rl_smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ti = lane & 7, ep = 8 * warp + 2 * (lane >> 3);   // token row, first expert row (tile-relative)
     const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE;
-    // the next chunk is fetched into registers while the current one is consumed
-    float4 pre[PER];
-    auto fetch = [&](int k0) {
-        const int kn = min(KC, H - k0);
+    const int nc = (H + KC - 1) / KC;
+    // this thread's copies: chunk-relative source rows and stage offsets, fixed for all chunks
+    const float* src[PER];
+    int dst[PER];
+    bool valid[PER];
 #pragma unroll
-        for (int j = 0; j < PER; j++) {
-            const int i = tid + 256 * j;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (i < NV) {
-                const int rr = i / (KC / 4), k4 = (i % (KC / 4)) * 4;
-                const bool is_x = rr < TT;
-                const int row = is_x ? t0 + rr : e0 + rr - TT;
-                if ((is_x ? row < T : row < E) && k4 < kn) {
-                    const float* src = (is_x ? X : W) + (size_t)row * H + k0 + k4;
-                    if (k4 + 4 <= kn) v = *reinterpret_cast<const float4*>(src);
-                    else {
-                        v.x = src[0];
-                        if (k4 + 1 < kn) v.y = src[1];
-                        if (k4 + 2 < kn) v.z = src[2];
-                    }
-                }
-            }
-            pre[j] = v;
-        }
-    };
-    auto stash = [&]() {
-#pragma unroll
-        for (int j = 0; j < PER; j++) {
-            const int i = tid + 256 * j;
-            if (i < NV) {
-                const int rr = i / (KC / 4), k4 = (i % (KC / 4)) * 4;
-                float* dst = rr < TT ? &xs[rr][k4] : &ws[rr - TT][k4];
-                *reinterpret_cast<float4*>(dst) = pre[j];
-            }
-        }
-    };
-    float acc = 0.f;
-    fetch(0);
-    for (int k0 = 0; k0 < H; k0 += KC) {
-        const int kn = min(KC, H - k0);
-        stash();
-        __syncthreads();
-        if (k0 + KC < H) fetch(k0 + KC);
-        const int kq = kn / 4;
-        for (int q = 0; q < kq; q++) {
-            const float4 xv = *reinterpret_cast<const float4*>(&xs[ty][4 * q]);
-            const float4 wv = *reinterpret_cast<const float4*>(&ws[tx][4 * q]);
-            acc = __fadd_rn(acc, __fmul_rn(xv.x, wv.x));
-            acc = __fadd_rn(acc, __fmul_rn(xv.y, wv.y));
-            acc = __fadd_rn(acc, __fmul_rn(xv.z, wv.z));
-            acc = __fadd_rn(acc, __fmul_rn(xv.w, wv.w));
-        }
-        for (int k = 4 * kq; k < kn; k++) acc = __fadd_rn(acc, __fmul_rn(xs[ty][k], ws[tx][k]));
-        __syncthreads();
+    for (int j = 0; j < PER; j++) {
+        const int i = tid + NTH * j;
+        const int rr = i / (KC / 4), k4 = (i % (KC / 4)) * 4;
+        const bool is_x = rr < TT;
+        const int row = is_x ? t0 + rr : e0 + rr - TT;
+        valid[j] = is_x ? row < T : row < E;
+        src[j] = valid[j] ? (is_x ? X : W) + (size_t)row * H + k4 : X;
+        dst[j] = rr * LD + k4;
     }
-    const int t = t0 + ty, e = e0 + tx;
-    if (t < T && e < E) logits[(size_t)t * E + e] = acc;
+    auto issue = [&](int c) {
+        if (c < nc) {
+            float* st = rl_smem + (c % NS) * (TT + TE) * LD;
+            const int k0 = c * KC;
+#pragma unroll
+            for (int j = 0; j < PER; j++) {
+                const bool in = valid[j] && k0 + dst[j] % LD < H;
+                cp_async16(st + dst[j], in ? src[j] + k0 : X, in ? 16 : 0);   // zero-fill outside
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    issue(0);
+    issue(1);
+    float a0 = 0.f, a1 = 0.f;
+    for (int c = 0; c < nc; c++) {
+        issue(c + 2);
+        asm volatile("cp.async.wait_group 2;" ::: "memory");
+        __syncthreads();
+        const float* st = rl_smem + (c % NS) * (TT + TE) * LD;
+        const float4* xr = reinterpret_cast<const float4*>(st + ti * LD);
+        const float4* w0r = reinterpret_cast<const float4*>(st + (TT + ep) * LD);
+        const float4* w1r = reinterpret_cast<const float4*>(st + (TT + ep + 1) * LD);
+        const int kq = min(KC, H - c * KC) / 4;   // H is a multiple of 4
+        auto step = [&](const float4& xv, const float4& u, const float4& v) {
+            a0 = __fadd_rn(a0, __fmul_rn(xv.x, u.x));
+            a1 = __fadd_rn(a1, __fmul_rn(xv.x, v.x));
+            a0 = __fadd_rn(a0, __fmul_rn(xv.y, u.y));
+            a1 = __fadd_rn(a1, __fmul_rn(xv.y, v.y));
+            a0 = __fadd_rn(a0, __fmul_rn(xv.z, u.z));
+            a1 = __fadd_rn(a1, __fmul_rn(xv.z, v.z));
+            a0 = __fadd_rn(a0, __fmul_rn(xv.w, u.w));
+            a1 = __fadd_rn(a1, __fmul_rn(xv.w, v.w));
+        };
+        if (kq == KC / 4) {
+            // full chunk, fully unrolled: the loads run ahead of the two add chains
+#pragma unroll
+            for (int q = 0; q < KC / 4; q++) step(xr[q], w0r[q], w1r[q]);
+        } else {
+            for (int q = 0; q < kq; q++) step(xr[q], w0r[q], w1r[q]);
+        }
+        __syncthreads();   // stage c % NS is refilled by the next iteration's issue(c + 3)
+    }
+    const int t = t0 + ti, e = e0 + ep;
+    if (t < T) {
+        if (e < E) logits[(size_t)t * E + e] = a0;
+        if (e + 1 < E) logits[(size_t)t * E + e + 1] = a1;
+    }
 }
 
 void launch_router_logits(const float* X, const float* W, int T, int E, int H, float* logits,
@@ -139,8 +158,9 @@ void launch_router_logits(const float* X, const float* W, int T, int E, int H, f
         dim3 grid((E + 31) / 32, (T + 3) / 4);
         router_logits_kernel<4, 1><<<grid, dim3(32, 4), 0, s>>>(X, W, T, E, H, logits);
     } else {
+        cudaFuncSetAttribute(router_logits_v2, cudaFuncAttributeMaxDynamicSharedMemorySize, rl::kSmem);
         dim3 grid((T + 7) / 8, (E + 31) / 32);
-        router_logits_v2<<<grid, 256, 0, s>>>(X, W, T, E, H, logits);
+        router_logits_v2<<<grid, rl::NTH, rl::kSmem, s>>>(X, W, T, E, H, logits);
     }
 }
 
@@ -160,87 +180,85 @@ __device__ __forceinline__ bool beats(float v2, int i2, float v1, int i1) {
     return v2 > v1 || (v2 == v1 && i2 < i1);
 }
 
-// strict-greater argmax over unused entries with the reference's -1e30 floor
-__device__ int warp_argmax(const float* v, const unsigned char* used, int n, int lane) {
-    float bv = -1e30f;
-    int bi = -1;
-    for (int i = lane; i < n; i += 32)
-        if (!used[i] && v[i] > bv) {
-            bv = v[i];
-            bi = i;
-        }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (beats(ov, oi, bv, bi)) {
-            bv = ov;
-            bi = oi;
-        }
-    }
-    return bi;
-}
-
+// One warp per token.  Lane l holds experts l + 32 j (j < NS) in registers with a bitmask of
+// those still selectable; each of the K rounds takes every lane's best candidate and a 5-step
+// shuffle argmax over (score, expert, prob).  The order of comparisons gives exactly the
+// reference's scan (src/m6_layer.c:860-870): the largest score wins, the lowest expert index
+// among equal scores, and only scores above the -1e30 floor count (NaN never does).  The softmax
+// denominator and the weight sum are taken sequentially in the reference's order.
+template <int NS>
 __global__ void __launch_bounds__(32 * kSelWarps) router_select_kernel(RouterParams p, int T,
                                                                       const float* __restrict__ logits,
                                                                       int* __restrict__ order,
                                                                       float* __restrict__ wtop,
                                                                       int* __restrict__ err) {
-    __shared__ float s_p[kSelWarps][kMaxExperts];
-    __shared__ float s_sel[kSelWarps][kMaxExperts];
-    __shared__ unsigned char s_used[kSelWarps][kMaxExperts];
+    __shared__ __align__(16) float s_v[kSelWarps][kMaxExperts];
     __shared__ float s_gs[kSelWarps][kMaxGroups];
-    __shared__ unsigned char s_gused[kSelWarps][kMaxGroups];
-    __shared__ int s_idx[kSelWarps][kMaxUsed];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * kSelWarps + w;
     if (t >= T) return;
     const int E = p.n_exp, K = p.n_used;
     const float* lg = logits + (size_t)t * E;
-    float* P = s_p[w];
-    float* S = s_sel[w];
-    unsigned char* used = s_used[w];
+    float* V = s_v[w];
+    float S[NS], P[NS];
     if (p.scoring == 0) {
         // max-subtracted softmax (src/m6_layer.c:784-789)
         float mx = -1e30f;
-        for (int e = lane; e < E; e += 32) {
-            const float v = lg[e];
-            P[e] = v;
-            mx = v > mx ? v : mx;
+#pragma unroll
+        for (int j = 0; j < NS; j++) {
+            const int e = lane + 32 * j;
+            S[j] = e < E ? lg[e] : 0.f;
+            if (e < E && S[j] > mx) mx = S[j];
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, mx, o);
             mx = ov > mx ? ov : mx;
         }
-        for (int e = lane; e < E; e += 32) P[e] = host_expf(__fsub_rn(P[e], mx));
+#pragma unroll
+        for (int j = 0; j < NS; j++) {
+            const int e = lane + 32 * j;
+            P[j] = host_expf(__fsub_rn(S[j], mx));
+            if (e < E) V[e] = P[j];
+        }
         __syncwarp();
         float s = 0.f;
-        if (lane == 0)
-            for (int e = 0; e < E; e++) s = __fadd_rn(s, P[e]);
+        if (lane == 0) {
+            int e = 0;
+            for (; e + 4 <= E; e += 4) {
+                const float4 q = *reinterpret_cast<const float4*>(V + e);
+                s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, q.x), q.y), q.z), q.w);
+            }
+            for (; e < E; e++) s = __fadd_rn(s, V[e]);
+        }
         s = __shfl_sync(0xffffffffu, s, 0);
         const float inv = __fdiv_rn(1.0f, s);
-        for (int e = lane; e < E; e += 32) {
-            P[e] = __fmul_rn(P[e], inv);
-            S[e] = P[e];
-            used[e] = 0;
+#pragma unroll
+        for (int j = 0; j < NS; j++) {
+            P[j] = __fmul_rn(P[j], inv);
+            S[j] = P[j];
         }
     } else {
         // sigmoid scores; bias only steers the selection (src/m6_layer.c:833-840)
-        for (int e = lane; e < E; e += 32) {
-            const float pe = __fdiv_rn(1.0f, __fadd_rn(1.0f, host_expf(-lg[e])));
-            P[e] = pe;
-            S[e] = __fadd_rn(pe, p.probs_b ? p.probs_b[e] : 0.0f);
-            used[e] = 0;
+#pragma unroll
+        for (int j = 0; j < NS; j++) {
+            const int e = lane + 32 * j;
+            const float l = e < E ? lg[e] : 0.f;
+            P[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, host_expf(-l)));
+            S[j] = __fadd_rn(P[j], p.probs_b && e < E ? p.probs_b[e] : 0.0f);
         }
-        __syncwarp();
         if (p.n_group > 1) {
-            // group score = sum of the group's two largest (src/m6_layer.c:841-859)
+            // group score = sum of the group's two largest (src/m6_layer.c:841-859), then the
+            // n_group_used best groups by the same strict-greater scan
+#pragma unroll
+            for (int j = 0; j < NS; j++)
+                if (lane + 32 * j < E) V[lane + 32 * j] = S[j];
+            __syncwarp();
             const int per = E / p.n_group;
             for (int g = lane; g < p.n_group; g += 32) {
                 float m1 = -1e30f, m2 = -1e30f;
                 for (int i = 0; i < per; i++) {
-                    const float v = S[g * per + i];
+                    const float v = V[g * per + i];
                     if (v > m1) {
                         m2 = m1;
                         m1 = v;
@@ -249,57 +267,125 @@ __global__ void __launch_bounds__(32 * kSelWarps) router_select_kernel(RouterPar
                     }
                 }
                 s_gs[w][g] = __fadd_rn(m1, m2);
-                s_gused[w][g] = 0;
             }
             __syncwarp();
-            for (int j = 0; j < p.n_group_used; j++) {
-                const int bg = warp_argmax(s_gs[w], s_gused[w], p.n_group, lane);
-                if (bg < 0) {
+            uint32_t gavail = 0, gsel = 0;   // groups lane, lane + 32
+            float G[2];
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int g = lane + 32 * j;
+                G[j] = g < p.n_group ? s_gs[w][g] : 0.f;
+                if (g < p.n_group) gavail |= 1u << j;
+            }
+            for (int r = 0; r < p.n_group_used; r++) {
+                float bv = -1e30f;
+                int bi = -1;
+#pragma unroll
+                for (int j = 0; j < 2; j++)
+                    if ((gavail >> j & 1) && G[j] > bv) {
+                        bv = G[j];
+                        bi = lane + 32 * j;
+                    }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (beats(ov, oi, bv, bi)) {
+                        bv = ov;
+                        bi = oi;
+                    }
+                }
+                if (bi < 0) {
                     if (lane == 0) atomicOr(err, 1);
                     break;
                 }
-                if (lane == 0) s_gused[w][bg] = 1;
-                __syncwarp();
+                if ((bi & 31) == lane) {
+                    gavail &= ~(1u << (bi >> 5));
+                    gsel |= 1u << (bi >> 5);
+                }
             }
-            __syncwarp();
-            for (int e = lane; e < E; e += 32)
-                if (!s_gused[w][e / per]) S[e] = -1e30f;
+            // every lane learns the chosen groups
+            const unsigned long long chosen =
+                (unsigned long long)__ballot_sync(0xffffffffu, gsel & 1) |
+                ((unsigned long long)__ballot_sync(0xffffffffu, gsel >> 1 & 1) << 32);
+#pragma unroll
+            for (int j = 0; j < NS; j++) {
+                const int e = lane + 32 * j;
+                if (e < E && !(chosen >> (e / per) & 1)) S[j] = -1e30f;
+            }
         }
     }
-    __syncwarp();
-    for (int j = 0; j < K; j++) {
-        const int bi = warp_argmax(S, used, E, lane);
-        if (lane == 0) {
-            s_idx[w][j] = bi;
-            if (bi >= 0) used[bi] = 1;
-            else atomicOr(err, 2);
+    uint32_t avail = 0;
+#pragma unroll
+    for (int j = 0; j < NS; j++)
+        if (lane + 32 * j < E) avail |= 1u << j;
+    // lane l keeps result l (and l + 32 when K > 32)
+    static_assert(kMaxUsed <= 64, "two results per lane");
+    int my_i0 = -1, my_i1 = -1;
+    float my_p0 = 0.f, my_p1 = 0.f;
+    for (int r = 0; r < K; r++) {
+        float bv = -1e30f, bp = 0.f;
+        int bi = -1;
+#pragma unroll
+        for (int j = 0; j < NS; j++)
+            if ((avail >> j & 1) && S[j] > bv) {
+                bv = S[j];
+                bp = P[j];
+                bi = lane + 32 * j;
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+            if (beats(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+                bp = op;
+            }
         }
-        __syncwarp();
+        if (bi < 0) {
+            if (lane == 0) atomicOr(err, 2);
+        } else if ((bi & 31) == lane) {
+            avail &= ~(1u << (bi >> 5));
+        }
+        if ((r & 31) == lane) {
+            if (r < 32) {
+                my_i0 = bi;
+                my_p0 = bi >= 0 ? bp : 0.f;
+            } else {
+                my_i1 = bi;
+                my_p1 = bi >= 0 ? bp : 0.f;
+            }
+        }
     }
-    if (lane == 0) {
-        float wl[kMaxUsed];
-        float s = 0.f;
-        for (int j = 0; j < K; j++) {
-            const int i = s_idx[w][j];
-            wl[j] = i >= 0 ? P[i] : 0.f;
-            s = __fadd_rn(s, wl[j]);
-        }
-        if (p.scoring == 0 || p.norm_w) {
-            if (s < 6.103515625e-5f) s = 6.103515625e-5f;
-            for (int j = 0; j < K; j++) wl[j] = __fdiv_rn(wl[j], s);
-        }
-        if (p.scoring != 0 && p.w_scale != 0.f && p.w_scale != 1.f)
-            for (int j = 0; j < K; j++) wl[j] = __fmul_rn(wl[j], p.w_scale);
-        for (int j = 0; j < K; j++) {
-            order[(size_t)t * K + j] = s_idx[w][j];
-            wtop[(size_t)t * K + j] = wl[j];
+    // weights (src/m6_layer.c:871-880): sum in selection order, then per-lane division
+    float s = 0.f;
+    for (int j = 0; j < K; j++) s = __fadd_rn(s, __shfl_sync(0xffffffffu, j < 32 ? my_p0 : my_p1, j & 31));
+    const bool renorm = p.scoring == 0 || p.norm_w;
+    if (s < 6.103515625e-5f) s = 6.103515625e-5f;
+    const bool scale = p.scoring != 0 && p.w_scale != 0.f && p.w_scale != 1.f;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int j = lane + 32 * h;
+        if (j < K) {
+            float wl = h ? my_p1 : my_p0;
+            if (renorm) wl = __fdiv_rn(wl, s);
+            if (scale) wl = __fmul_rn(wl, p.w_scale);
+            order[(size_t)t * K + j] = h ? my_i1 : my_i0;
+            wtop[(size_t)t * K + j] = wl;
         }
     }
 }
 
 void launch_router_select(const RouterParams& p, int T, RouteBufs& b, cudaStream_t s) {
-    router_select_kernel<<<(T + kSelWarps - 1) / kSelWarps, 32 * kSelWarps, 0, s>>>(
-        p, T, b.logits, b.order, b.wtop, b.err);
+    const int grid = (T + kSelWarps - 1) / kSelWarps, nth = 32 * kSelWarps;
+    const int ns = (p.n_exp + 31) / 32;
+    if (ns <= 1) router_select_kernel<1><<<grid, nth, 0, s>>>(p, T, b.logits, b.order, b.wtop, b.err);
+    else if (ns <= 2) router_select_kernel<2><<<grid, nth, 0, s>>>(p, T, b.logits, b.order, b.wtop, b.err);
+    else if (ns <= 4) router_select_kernel<4><<<grid, nth, 0, s>>>(p, T, b.logits, b.order, b.wtop, b.err);
+    else if (ns <= 8) router_select_kernel<8><<<grid, nth, 0, s>>>(p, T, b.logits, b.order, b.wtop, b.err);
+    else router_select_kernel<16><<<grid, nth, 0, s>>>(p, T, b.logits, b.order, b.wtop, b.err);
 }
 
 // ------------------------------------------------------------------------------------------

@@ -17,7 +17,8 @@
 //   activations' fp16 tile (TMA, 128-byte swizzle) as the B operand into one of two fp32
 //   accumulators in TMEM -> an epilogue warpgroup reads the other accumulator back
 //   (tcgen05.ld) while the next item's MMAs run.
-// A K step is half a superblock column (8 MMAs of K = 16); four steps are in flight.  The
+// A K step is half a superblock column (8 MMAs of K = 16); four A slots are in flight and four
+// or eight activation stages (token tiles of <= 128 or <= 64 tokens).  The
 // issuing thread tests the readiness of step q + 1 before it issues step q (an mbarrier wait
 // costs that thread a few hundred cycles during which it cannot issue), and one
 // tcgen05.commit per step releases both the step's A slot and its activation stage.
@@ -55,9 +56,9 @@ constexpr int kBProdWarp = 18;                // TMA producer of the activation 
 constexpr int kEpiWarp0 = 19;                 // epilogue warpgroup: warps 19..22
 constexpr int kThreads = 32 * 23;
 constexpr int kMaxRawStages = 8;              // raw superblock-column stages
-constexpr int kSlots = 4;                     // K steps in flight: A slots in TMEM = activation stages
-constexpr int kBSubBytes = 128 * 128;         // activation tile of one 64-wide K chunk: 128 tokens x 64 halves
-constexpr int kBStageBytes = 2 * kBSubBytes;  // one K step = half a superblock column (128 values)
+constexpr int kSlots = 4;                     // A slots in TMEM (K steps decoded ahead of the MMAs)
+constexpr int kDone = 8;                      // ring of per-step completion barriers (>= every stage count)
+constexpr int kMaxBStages = 8;                // activation stages
 constexpr int kTmemCols = 512;
 constexpr int kAccCols = 128;                 // per accumulator buffer (N <= 128)
 constexpr int kABase = 256;                   // A slots (64 columns each) start here
@@ -157,13 +158,13 @@ __device__ __forceinline__ bool elect_one() {
 }
 // Non-blocking test of two barriers' phases in one instruction group (one pass through the
 // shared-memory pipe instead of two)
-__device__ __forceinline__ bool mbar_test2(uint64_t* a, uint64_t* b, uint32_t parity) {
+__device__ __forceinline__ bool mbar_test2(uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %3;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 q, [%2], %3;\n\tand.pred p, p, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        "mbarrier.test_wait.parity.shared::cta.b64 q, [%2], %4;\n\tand.pred p, p, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(a)), "r"(smem_u32(b)), "r"(parity)
+        : "r"(smem_u32(a)), "r"(smem_u32(b)), "r"(pa), "r"(pb)
         : "memory");
     return ok != 0;
 }
@@ -390,17 +391,23 @@ __device__ __forceinline__ void deq_q6k(const uint8_t* blk, int kc, uint32_t (&o
 }
 
 // ---------------------------------------------------------------- the kernel
-template <int MODE, int CODE>
+// NT = most tokens per item (64 or 128)
+template <int MODE, int CODE, int NT>
 struct Cfg {
     static constexpr int kBB = CODE == DRACO_CODE_Q4_K ? 144 : kQ6Padded;   // raw bytes per row superblock
     static constexpr int kRawStage = 128 * kBB;
-    // weight stages next to the four 32 KB activation stages (227 KB per block)
+    // activation stages: one K step = two 64-wide chunks x NT tokens x 128 B; 128 KB in all
+    static constexpr int kBStage = NT * 256;
+    static constexpr int kBStages = NT == 64 ? 8 : 4;
+    // weight stages next to them (227 KB per block)
     static constexpr int kRawStages = CODE == DRACO_CODE_Q4_K ? DRACO_TC_RAW_STAGES_Q4K : DRACO_TC_RAW_STAGES_Q6K;
     static constexpr int kBOff = kRawStages * kRawStage;                 // 1024-aligned below
     static constexpr int kBOffAligned = (kBOff + 1023) / 1024 * 1024;
-    static constexpr int kBarOff = kBOffAligned + kSlots * kBStageBytes;
+    static constexpr int kBarOff = kBOffAligned + kBStages * kBStage;
     static constexpr int kSmem = kBarOff + 1024 + 1024;                    // barriers + alignment slack
-    static_assert(kRawStages <= kMaxRawStages && kSmem <= 232448, "shared memory");
+    static_assert(kRawStages <= kMaxRawStages && kBStages <= kMaxBStages && kBStages <= kDone &&
+                      kSlots <= kDone && kSmem <= 232448,
+                  "rings and shared memory");
 };
 
 // activation tensor maps, one per token-tile height R = 16 (i + 1): 3D view
@@ -412,8 +419,8 @@ struct ActMaps {
 
 struct Bars {
     uint64_t raw_full[kMaxRawStages], raw_empty[kMaxRawStages];
-    uint64_t a_full[kSlots], b_full[kSlots];
-    uint64_t done[kSlots];                     // done[q % 4]: MMAs of K step q finished
+    uint64_t a_full[kSlots], b_full[kMaxBStages];
+    uint64_t done[kDone];                      // done[q % 8]: MMAs of K step q finished
     uint64_t acc_full[2], acc_empty[2], drain;
     uint32_t tmem_base;
     int abort_flag;
@@ -425,14 +432,14 @@ struct Bars {
 // so lanes i and i^8 hold gate and up of one intermediate row; down tiles are unpermuted.
 __device__ __forceinline__ int gu_row(int quarter, int i) { return 16 * quarter + ((i & 16) >> 1) + (i & 7); }
 
-template <int MODE, int CODE, bool STATS>
+template <int MODE, int CODE, int NT, bool STATS>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                   const __grid_constant__ ActMaps tmB, const int4* __restrict__ items,
                   const int* __restrict__ n_items_p, int rows_per_expert, int K, int out_ld,
                   __half* __restrict__ act_out, float* __restrict__ y_out, int* __restrict__ err,
                   unsigned long long* __restrict__ stats) {
-    using C = Cfg<MODE, CODE>;
+    using C = Cfg<MODE, CODE, NT>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-align the dynamic shared memory base (swizzled tiles need it) by pointer arithmetic
     // on the shared array, so every access below stays a shared-memory access
@@ -451,11 +458,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars->raw_full[i], 1);
             mbar_init(&bars->raw_empty[i], kDeqWarps);
         }
-        for (int i = 0; i < kSlots; i++) {
-            mbar_init(&bars->a_full[i], kDeqWarps / 2);
-            mbar_init(&bars->b_full[i], 1);
-            mbar_init(&bars->done[i], 1);
-        }
+        for (int i = 0; i < kSlots; i++) mbar_init(&bars->a_full[i], kDeqWarps / 2);
+        for (int i = 0; i < C::kBStages; i++) mbar_init(&bars->b_full[i], 1);
+        for (int i = 0; i < kDone; i++) mbar_init(&bars->done[i], 1);
         for (int i = 0; i < 2; i++) {
             mbar_init(&bars->acc_full[i], 1);
             mbar_init(&bars->acc_empty[i], 4);
@@ -520,24 +525,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int p0 = item.z, nbox = (item.w + 15) >> 4;
             const CUtensorMap* map = &tmB.m[nbox - 1];
             for (int s2 = 0; s2 < 2 * nb; s2++, q++) {
-                const int bs = q % kSlots;
-                if (q >= (uint32_t)kSlots) {   // stage reused: step q - 4 finished
+                const int bs = q % C::kBStages;
+                if (q >= (uint32_t)C::kBStages) {   // stage reused: step q - kBStages finished
+                    const uint32_t r = q - C::kBStages;
                     st.start();
-                    ok = warp_wait(&bars->done[bs], ((q - kSlots) / kSlots) & 1, abort_flag, err, 2);
+                    ok = warp_wait(&bars->done[r % kDone], (r / kDone) & 1, abort_flag, err, 2);
                     st.stop(kStProdBEmpty);
                     if (!ok) break;
                 }
                 if (elect_one()) {
                     mbar_expect_tx(&bars->b_full[bs], 2 * nbox * 16 * 128);
-                    tma_load_3d(bt + bs * kBStageBytes, map, 0, p0, 2 * s2, &bars->b_full[bs]);
+                    tma_load_3d(bt + bs * C::kBStage, map, 0, p0, 2 * s2, &bars->b_full[bs]);
                 }
                 __syncwarp();
             }
         }
         if (!ok)
-            for (uint32_t k = 0; k < (uint32_t)kSlots && k < q; k++) {
+            for (uint32_t k = 0; k < (uint32_t)C::kBStages && k < q; k++) {
                 const uint32_t r = q - 1 - k;
-                mbar_drain(&bars->b_full[r % kSlots], (r / kSlots) & 1);
+                mbar_drain(&bars->b_full[r % C::kBStages], (r / C::kBStages) & 1);
             }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
@@ -558,18 +564,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
             }
             const uint32_t d_tm = tmem + buf * kAccCols;
-            bool rdy = __all_sync(0xffffffffu, mbar_test2(&bars->a_full[q % kSlots], &bars->b_full[q % kSlots],
-                                                          (q / kSlots) & 1));
+            bool rdy = __all_sync(0xffffffffu, mbar_test2(&bars->a_full[q % kSlots], (q / kSlots) & 1,
+                                                          &bars->b_full[q % C::kBStages], (q / C::kBStages) & 1));
             for (int s2 = 0; s2 < 2 * nb; s2++, q++) {
-                const int sl = q % kSlots;
-                const uint32_t par = (q / kSlots) & 1;
+                const int sl = q % kSlots, bs = q % C::kBStages;
                 if (!rdy) {
                     st.start();
-                    ok = warp_wait(&bars->a_full[sl], par, abort_flag, err, 5);
+                    ok = warp_wait(&bars->a_full[sl], (q / kSlots) & 1, abort_flag, err, 5);
                     st.stop(kStMmaAFull);
                     if (!ok) break;
                     st.start();
-                    ok = warp_wait(&bars->b_full[sl], par, abort_flag, err, 4);
+                    ok = warp_wait(&bars->b_full[bs], (q / C::kBStages) & 1, abort_flag, err, 4);
                     st.stop(kStMmaBFull);
                     if (!ok) break;
                 }
@@ -577,12 +582,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // readiness of the next step, tested before this step's MMAs are issued
                 st.start();
                 if (s2 + 1 < 2 * nb)
-                    rdy = __all_sync(0xffffffffu, mbar_test2(&bars->a_full[(q + 1) % kSlots],
-                                                             &bars->b_full[(q + 1) % kSlots], ((q + 1) / kSlots) & 1));
+                    rdy = __all_sync(0xffffffffu,
+                                     mbar_test2(&bars->a_full[(q + 1) % kSlots], ((q + 1) / kSlots) & 1,
+                                                &bars->b_full[(q + 1) % C::kBStages], ((q + 1) / C::kBStages) & 1));
                 st.stop(kStMmaTest);
                 st.start();
                 const uint32_t a_tm = tmem + kABase + 64 * sl;
-                const uint64_t bd = desc0 + (uint64_t)(sl * (kBStageBytes >> 4));
+                const uint64_t bd = desc0 + (uint64_t)(bs * (C::kBStage >> 4));
                 if (elect_one()) {
 #pragma unroll
                     for (int c = 0; c < 2; c++) {
@@ -591,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tc_mma_ts(d_tm, a_tm + 32 * c + 8 * j, bd + (uint64_t)(c * sub + 2 * j), idesc,
                                       (s2 | c | j) != 0 ? 1u : 0u);
                     }
-                    tc_commit(&bars->done[sl]);
+                    tc_commit(&bars->done[q % kDone]);
                 }
                 __syncwarp();
                 st.stop(kStMmaIssue);
@@ -622,10 +628,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = warp_wait(&bars->raw_full[rs], (sq / C::kRawStages) & 1, abort_flag, err, 7);
                 st.stop(kStDeqRawFull);
                 if (!ok) break;
-                st.start();
-                ok = warp_wait(&bars->done[sl], ((q / kSlots) & 1) ^ 1, abort_flag, err, 8);
-                st.stop(kStDeqAEmpty);
-                if (!ok) break;
+                if (q >= (uint32_t)kSlots) {   // slot reused: step q - 4 finished
+                    const uint32_t r = q - kSlots;
+                    st.start();
+                    ok = warp_wait(&bars->done[r % kDone], (r / kDone) & 1, abort_flag, err, 8);
+                    st.stop(kStDeqAEmpty);
+                    if (!ok) break;
+                }
                 tc_fence_after();
                 uint32_t v[32];
                 const uint8_t* blk = raw + rs * C::kRawStage + row * C::kBB;
@@ -712,8 +721,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------- helpers
 // work items: per active expert, token tiles of <= 128 sorted positions x 128-row weight tiles
 __global__ void build_items_kernel(const int* __restrict__ off, const int* __restrict__ active,
-                                   const int* __restrict__ n_active_p, int mtiles, int4* __restrict__ items,
-                                   int* __restrict__ n_items) {
+                                   const int* __restrict__ n_active_p, int mtiles, int nt_max,
+                                   int4* __restrict__ items, int* __restrict__ n_items) {
     __shared__ int cnt[512];
     const int n_active = *n_active_p;
     const int a = threadIdx.x;
@@ -721,7 +730,7 @@ __global__ void build_items_kernel(const int* __restrict__ off, const int* __res
     if (a < n_active) {
         e = active[a];
         c = off[e + 1] - off[e];
-        cnt[a] = ((c + 127) / 128) * mtiles;
+        cnt[a] = ((c + nt_max - 1) / nt_max) * mtiles;
     } else {
         cnt[a] = 0;
     }
@@ -733,9 +742,9 @@ __global__ void build_items_kernel(const int* __restrict__ off, const int* __res
         __syncthreads();
     }
     if (a < n_active) {
-        int k = cnt[a] - ((c + 127) / 128) * mtiles;
-        for (int nt = 0; nt * 128 < c; nt++)
-            for (int mt = 0; mt < mtiles; mt++) items[k++] = make_int4(e, mt, off[e] + nt * 128, min(128, c - nt * 128));
+        int k = cnt[a] - ((c + nt_max - 1) / nt_max) * mtiles;
+        for (int t0 = 0; t0 < c; t0 += nt_max)
+            for (int mt = 0; mt < mtiles; mt++) items[k++] = make_int4(e, mt, off[e] + t0, min(nt_max, c - t0));
     }
     if (a == 511) *n_items = cnt[511];
 }
@@ -832,12 +841,12 @@ bool cached_act_maps(tc::ActMaps* out, const void* base, size_t P, size_t K) {
     return true;
 }
 
-template <int MODE, int CODE, bool STATS>
+template <int MODE, int CODE, int NT, bool STATS>
 cudaError_t launch_tc_k(const CUtensorMap& a0, const CUtensorMap& a1, const tc::ActMaps& b, const int4* items,
                         const int* n_items, int grid, int rows_per_expert, int K, int out_ld, __half* act, float* y,
                         int* err, unsigned long long* stats, cudaStream_t s) {
-    using C = tc::Cfg<MODE, CODE>;
-    auto kern = tc::moe_tc_kernel<MODE, CODE, STATS>;
+    using C = tc::Cfg<MODE, CODE, NT>;
+    auto kern = tc::moe_tc_kernel<MODE, CODE, NT, STATS>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) return e;
     kern<<<grid, tc::kThreads, C::kSmem, s>>>(a0, a1, b, items, n_items, rows_per_expert, K, out_ld, act, y, err,
@@ -846,13 +855,17 @@ cudaError_t launch_tc_k(const CUtensorMap& a0, const CUtensorMap& a1, const tc::
 }
 template <int MODE, int CODE>
 cudaError_t launch_tc(const CUtensorMap& a0, const CUtensorMap& a1, const tc::ActMaps& b, const int4* items,
-                      const int* n_items, int grid, int rows_per_expert, int K, int out_ld, __half* act, float* y,
-                      int* err, unsigned long long* stats, cudaStream_t s) {
-    if (stats)
-        return launch_tc_k<MODE, CODE, true>(a0, a1, b, items, n_items, grid, rows_per_expert, K, out_ld, act, y, err,
-                                             stats, s);
-    return launch_tc_k<MODE, CODE, false>(a0, a1, b, items, n_items, grid, rows_per_expert, K, out_ld, act, y, err,
-                                          nullptr, s);
+                      const int* n_items, int grid, int nt, int rows_per_expert, int K, int out_ld, __half* act,
+                      float* y, int* err, unsigned long long* stats, cudaStream_t s) {
+    if (nt == 64)
+        return stats ? launch_tc_k<MODE, CODE, 64, true>(a0, a1, b, items, n_items, grid, rows_per_expert, K, out_ld,
+                                                         act, y, err, stats, s)
+                     : launch_tc_k<MODE, CODE, 64, false>(a0, a1, b, items, n_items, grid, rows_per_expert, K, out_ld,
+                                                          act, y, err, nullptr, s);
+    return stats ? launch_tc_k<MODE, CODE, 128, true>(a0, a1, b, items, n_items, grid, rows_per_expert, K, out_ld, act,
+                                                      y, err, stats, s)
+                 : launch_tc_k<MODE, CODE, 128, false>(a0, a1, b, items, n_items, grid, rows_per_expert, K, out_ld,
+                                                       act, y, err, nullptr, s);
 }
 
 }  // namespace
@@ -883,21 +896,24 @@ int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, i
     if (!cached_act_maps(&mx, Xs, (size_t)P, (size_t)n_in) || !cached_act_maps(&ma, act_h, (size_t)P, (size_t)inter))
         return -2;
     tc::gather_half_kernel<<<148 * 8, 256, 0, s>>>(X, ilist, tok_div, P, n_in, Xs);
-    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, tc_tiles_gateup(inter), items_gu, n_items_gu);
-    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, tc_tiles_down(n_out), items_dn, n_items_dn);
+    // token tiles of <= 64 with eight activation stages for sparse loads (<= 16 tokens per
+    // expert on average), else <= 128 with four
+    const int nt = P <= 16 * n_exp ? 64 : 128;
+    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, tc_tiles_gateup(inter), nt, items_gu, n_items_gu);
+    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, tc_tiles_down(n_out), nt, items_dn, n_items_dn);
     cudaError_t e;
     if (cg == DRACO_CODE_Q4_K)
-        e = launch_tc<0, DRACO_CODE_Q4_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, inter, n_in, inter, act_h,
-                                          nullptr, err, stats, s);
+        e = launch_tc<0, DRACO_CODE_Q4_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, nt, inter, n_in, inter,
+                                          act_h, nullptr, err, stats, s);
     else
-        e = launch_tc<0, DRACO_CODE_Q6_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, inter, n_in, inter, act_h,
-                                          nullptr, err, stats, s);
+        e = launch_tc<0, DRACO_CODE_Q6_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, nt, inter, n_in, inter,
+                                          act_h, nullptr, err, stats, s);
     if (e != cudaSuccess) return -3;
     if (cd == DRACO_CODE_Q4_K)
-        e = launch_tc<1, DRACO_CODE_Q4_K>(maps.down, maps.down, ma, items_dn, n_items_dn, 148, n_out, inter, n_out,
+        e = launch_tc<1, DRACO_CODE_Q4_K>(maps.down, maps.down, ma, items_dn, n_items_dn, 148, nt, n_out, inter, n_out,
                                           nullptr, y, err, stats ? stats + tc::kStSites : nullptr, s);
     else
-        e = launch_tc<1, DRACO_CODE_Q6_K>(maps.down, maps.down, ma, items_dn, n_items_dn, 148, n_out, inter, n_out,
+        e = launch_tc<1, DRACO_CODE_Q6_K>(maps.down, maps.down, ma, items_dn, n_items_dn, 148, nt, n_out, inter, n_out,
                                           nullptr, y, err, stats ? stats + tc::kStSites : nullptr, s);
     return e == cudaSuccess ? 0 : -3;
 }

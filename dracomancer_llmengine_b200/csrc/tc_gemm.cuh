@@ -29,9 +29,10 @@ constexpr int kTcStatSites = 15;
 // weight-row tiles per expert: gate/up tiles hold 64 rows of each matrix, down tiles 128 rows
 inline int tc_tiles_gateup(int inter) { return inter / 64; }
 inline int tc_tiles_down(int n_out) { return n_out / 128; }
-// item-list capacity for P assignments over at most n_active_max experts
+// item-list capacity for P assignments over at most n_active_max experts (token tiles of 64 or
+// more tokens)
 inline size_t tc_items_capacity(int P, int n_active_max, int row_tiles) {
-    return ((size_t)P / 128 + (size_t)n_active_max + 1) * (size_t)row_tiles;
+    return ((size_t)P / 64 + (size_t)n_active_max + 1) * (size_t)row_tiles;
 }
 
 }  // namespace draco
