@@ -213,8 +213,24 @@ struct Ctx {
     char* ws = nullptr;
     size_t ws_cap = 0;
     int* d_consts = nullptr;     // [0] = 0, [1] = 1, [2..3] = {0, T} (dense single-expert lists)
-    int* h_consts = nullptr;     // pinned mirror of d_consts[2..3]
     unsigned long gen = 0;       // bumped whenever cached tables are dropped
+    // the workspace is shared by all calls: each call's stream waits for the previous call's
+    // last use of it (recorded on its stream) before its first use
+    cudaEvent_t ws_event = nullptr;
+    bool ws_event_set = false;
+    // set once a call was captured into an application's CUDA graph: that graph keeps the
+    // workspace addresses, so a workspace that is outgrown is retired instead of freed
+    bool ws_captured = false;
+    std::vector<char*> ws_retired;
+    // captured launch sequences of asynchronous device-pointer layer calls
+    struct Graph {
+        std::vector<uint64_t> key;
+        cudaGraphExec_t exec = nullptr;
+        long launches = 0;
+        unsigned long last_use = 0;
+    };
+    std::vector<Graph> graphs;
+    unsigned long graph_clock = 0;
 };
 
 Ctx* g_ctx[64];
@@ -245,7 +261,7 @@ Ctx* get_ctx() {
         c->dev = dev;
         if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
             cudaMalloc(&c->d_consts, 4 * sizeof(int)) != cudaSuccess ||
-            cudaMallocHost(&c->h_consts, 4 * sizeof(int)) != cudaSuccess) {
+            cudaEventCreateWithFlags(&c->ws_event, cudaEventDisableTiming) != cudaSuccess) {
             set_err("CUDA context set-up failed: %s", cudaGetErrorString(cudaGetLastError()));
             delete c;
             return nullptr;
@@ -263,10 +279,13 @@ void free_table(Table& t) {
     t.tc = nullptr;
 }
 
+void drop_graphs(Ctx* c);
+
 void drop_tables(Ctx* c) {
     for (auto& kv : c->tables) free_table(kv.second);
     c->tables.clear();
     c->gen++;
+    drop_graphs(c);   // they launch kernels on the dropped tables' device data
 }
 
 void drop_region(Ctx* c, std::map<uintptr_t, Region>::iterator it) {
@@ -562,10 +581,28 @@ struct Carver {
     }
 };
 
+void drop_graphs(Ctx* c) {
+    for (auto& g : c->graphs) cudaGraphExecDestroy(g.exec);
+    c->graphs.clear();
+}
+
+// order stream s after the previous call's use of the workspace / record this call's use
+void ws_acquire(Ctx* c, cudaStream_t s) {
+    if (c->ws_event_set) cudaStreamWaitEvent(s, c->ws_event, 0);
+}
+void ws_release(Ctx* c, cudaStream_t s) {
+    cudaEventRecord(c->ws_event, s);
+    c->ws_event_set = true;
+}
+
 int ensure_ws(Ctx* c, size_t bytes) {
+    ws_acquire(c, c->stream);
     if (bytes <= c->ws_cap) return 0;
     CK(cudaStreamSynchronize(c->stream));
-    if (c->ws) cudaFree(c->ws);
+    if (c->ws_event_set) CK(cudaEventSynchronize(c->ws_event));   // asynchronous calls are done with it
+    drop_graphs(c);
+    if (c->ws && c->ws_captured) c->ws_retired.push_back(c->ws);
+    else if (c->ws) cudaFree(c->ws);
     c->ws = nullptr;
     c->ws_cap = 0;
     const size_t cap = align_up(bytes + bytes / 2, 1 << 20);
@@ -658,9 +695,7 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
 // dense one-expert FFN over T token rows: act = silu(G x) * (U x), y = D act
 int dense_ffn(Ctx* c, Table* t, int T, const float* x, int ff, int n_in, int n_out, float* act, float* y,
               cudaStream_t s) {
-    c->h_consts[2] = 0;
-    c->h_consts[3] = T;
-    CK(cudaMemcpyAsync(c->d_consts + 2, c->h_consts + 2, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
+    launch_set_pair(c->d_consts + 2, 0, T, s);   // the one expert's token list [0, T)
     ExpertTable et{t->d_w};
     {
         PhaseScope ps(kShared, s);
@@ -668,10 +703,8 @@ int dense_ffn(Ctx* c, Table* t, int T, const float* x, int ff, int n_in, int n_o
                             n_in, act, s, t->q6s);
         launch_down_code(et, t->cd, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, act, ff, n_out, y, s, t->q6s);
     }
-    g_launches += 2;
+    g_launches += 3;
     CK(cudaGetLastError());
-    // the pinned mirror is rewritten by the next call: finish this copy first
-    CK(cudaStreamSynchronize(s));
     return 0;
 }
 
@@ -791,6 +824,65 @@ int validate_shape(int n_exp, int n_used, int inter, int n_in, int n_out, int n_
     return 0;
 }
 
+uint32_t __float_as_uint_host(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return u;
+}
+
+// Run `body` (launches on stream s) through a cached CUDA graph keyed by `key`: capture it on
+// the first call, replay it afterwards.  Falls back to direct launches while profiling, when
+// the caller is itself capturing the stream, or when capture fails.
+template <class F>
+int graph_call(Ctx* c, const std::vector<uint64_t>& key, cudaStream_t s, F&& body) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (g_prof || env_flag("DRACO_B200_TC_STATS") || env_flag("DRACO_B200_NO_GRAPH") ||
+        cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return body();
+    }
+    for (auto& g : c->graphs)
+        if (g.key == key) {
+            g.last_use = ++c->graph_clock;
+            CK(cudaGraphLaunch(g.exec, s));
+            g_launches += g.launches;
+            return 0;
+        }
+    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return body();
+    }
+    const long l0 = g_launches;
+    const int rc = body();
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(s, &graph);
+    cudaGraphExec_t exec = nullptr;
+    if (rc == 0 && ec == cudaSuccess && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess) {
+        cudaGraphDestroy(graph);
+        Ctx::Graph g;
+        g.key = key;
+        g.exec = exec;
+        g.launches = g_launches - l0;
+        g.last_use = ++c->graph_clock;
+        if (c->graphs.size() >= 16) {   // evict the least recently used
+            auto lru = std::min_element(c->graphs.begin(), c->graphs.end(),
+                                        [](const Ctx::Graph& x, const Ctx::Graph& y) { return x.last_use < y.last_use; });
+            cudaGraphExecDestroy(lru->exec);
+            c->graphs.erase(lru);
+        }
+        c->graphs.push_back(std::move(g));
+        g_launches = l0;
+        CK(cudaGraphLaunch(exec, s));
+        g_launches += c->graphs.back().launches;
+        return 0;
+    }
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    g_launches = l0;
+    if (rc) return rc;
+    return body();   // capture failed: launch directly
+}
+
 // Synchronous single-call layer on host or device x/out (the reference entry points).
 int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, const float* gate_inp,
                const float* probs_b, int scoring, int n_exp, int n_used, int n_group, int n_group_used, int norm_w,
@@ -849,6 +941,12 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
         return -1;
     }
     cudaStream_t s = (dev_io && user_stream) ? user_stream : c->stream;
+    // a stream being captured by the caller: no ordering against work outside the capture
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cap) != cudaSuccess) cudaGetLastError();
+    const bool captured = cap != cudaStreamCaptureStatusNone;
+    if (captured) c->ws_captured = true;
+    else ws_acquire(c, s);
     float* d_out = b.out;
     if (dev_io) {
         b.x = const_cast<float*>(x);
@@ -857,10 +955,32 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
     } else {
         CK(cudaMemcpyAsync(b.x, x, sizeof(float) * (size_t)T * n_in, cudaMemcpyHostToDevice, s));
     }
-    if (int rc = run_layer(c, a, T, b, s)) return rc;
+    auto body = [&]() -> int {
+        if (int rc = run_layer(c, a, T, b, s)) return rc;
+        if (dev_io) {
+            if (order_out)
+                CK(cudaMemcpyAsync(order_out, b.rb.order, sizeof(int) * T * n_used, cudaMemcpyDeviceToDevice, s));
+            if (wtop_out)
+                CK(cudaMemcpyAsync(wtop_out, b.rb.wtop, sizeof(float) * T * n_used, cudaMemcpyDeviceToDevice, s));
+        }
+        return 0;
+    };
+    if (dev_io && user_stream) {
+        // asynchronous call: replay the captured launch sequence of an identical earlier call
+        const std::vector<uint64_t> key = {
+            (uintptr_t)a.tab, (uintptr_t)a.sh, c->gen, (uintptr_t)c->ws, c->ws_cap, (uintptr_t)a.d_gi,
+            (uintptr_t)a.rp.probs_b, (uintptr_t)x, (uintptr_t)out, (uintptr_t)order_out, (uintptr_t)wtop_out,
+            (uint64_t)T, (uintptr_t)s, (uint64_t)n_exp, (uint64_t)n_used, (uint64_t)inter, (uint64_t)n_in,
+            (uint64_t)n_out, (uint64_t)a.sh_ff, (uint64_t)a.rp.scoring, (uint64_t)a.rp.n_group,
+            (uint64_t)a.rp.n_group_used, (uint64_t)a.rp.norm_w, (uint64_t)__float_as_uint_host(a.rp.w_scale),
+            (uint64_t)gemm_path(), (uint64_t)g_act_mode, (uint64_t)b.use_tc};
+        const int rc = captured ? body() : graph_call(c, key, s, body);
+        if (!captured) ws_release(c, s);
+        return rc;
+    }
+    if (int rc = body()) return rc;
     if (dev_io) {
-        if (order_out) CK(cudaMemcpyAsync(order_out, b.rb.order, sizeof(int) * T * n_used, cudaMemcpyDeviceToDevice, s));
-        if (wtop_out) CK(cudaMemcpyAsync(wtop_out, b.rb.wtop, sizeof(float) * T * n_used, cudaMemcpyDeviceToDevice, s));
+        if (!captured) ws_release(c, s);
         if (user_stream) return 0;
     } else {
         CK(cudaMemcpyAsync(out, d_out, sizeof(float) * (size_t)T * n_out, cudaMemcpyDeviceToHost, s));
@@ -1330,15 +1450,18 @@ void draco_b200_reset(void) {
     std::lock_guard<std::mutex> lk(g_mu);
     Ctx* c = get_ctx();
     if (!c) return;
-    cudaStreamSynchronize(c->stream);
-    for (auto& kv : c->tables) cudaFree((void*)kv.second.d_w);
-    c->tables.clear();
+    cudaDeviceSynchronize();   // asynchronous calls on any stream are done with the buffers
+    drop_tables(c);            // tables, their tensor maps and the captured graphs
     for (auto& kv : c->regions) cudaFree(kv.second.dev);
     c->regions.clear();
     c->reg_bytes = 0;
     if (c->ws) cudaFree(c->ws);
+    for (char* w : c->ws_retired) cudaFree(w);
+    c->ws_retired.clear();
     c->ws = nullptr;
     c->ws_cap = 0;
+    c->ws_captured = false;
+    c->ws_event_set = false;
 }
 
 size_t draco_b200_registered_bytes(void) {

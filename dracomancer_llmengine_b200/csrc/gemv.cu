@@ -431,6 +431,12 @@ __global__ void combine_kernel(const float* __restrict__ y, const int* __restric
     }
 }
 
+__global__ void set_pair_kernel(int* d, int a, int b) {
+    d[0] = a;
+    d[1] = b;
+}
+void launch_set_pair(int* d, int a, int b, cudaStream_t s) { set_pair_kernel<<<1, 1, 0, s>>>(d, a, b); }
+
 void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T, int K, int E,
                     int n_out, const float* shared, float* out, cudaStream_t s) {
     dim3 grid((n_out + 255) / 256, T);

@@ -40,6 +40,8 @@ void launch_router_logits(const float* X, const float* gate_inp, int T, int E, i
                           cudaStream_t s);
 void launch_router_select(const RouterParams& p, int T, RouteBufs& b, cudaStream_t s);
 void launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s);
+// d[0] = a, d[1] = b (small device-side constants, stream ordered and graph capturable)
+void launch_set_pair(int* d, int a, int b, cudaStream_t s);
 
 // gate/up (+SwiGLU) over grouped assignments.  Token of sorted position p is
 // ilist[p] / tok_div (ilist == nullptr: identity).  act is [positions][inter] in sorted order.
