@@ -712,16 +712,28 @@ int dense_ffn(Ctx* c, Table* t, int T, const float* x, int ff, int n_in, int n_o
 // otherwise b.rb.order / b.rb.wtop already hold it.
 int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     RouteBufs& rb = b.rb;
-    CK(cudaMemsetAsync(rb.err, 0, sizeof(int), s));
     if (a.d_gi) {
         PhaseScope ps(kRoute, s);
-        launch_router_logits(b.x, a.d_gi, T, a.E, a.n_in, rb.logits, s);
+        launch_router_logits(b.x, a.d_gi, T, a.E, a.n_in, rb.logits, s, rb.err);   // also zeroes err
         launch_router_select(a.rp, T, rb, s);
         g_launches += 2;
+    } else {
+        CK(cudaMemsetAsync(rb.err, 0, sizeof(int), s));
     }
     {
         PhaseScope ps(kDispatch, s);
-        launch_dispatch(T, a.K, a.E, rb, s);
+        ItemLists il;
+        if (b.use_tc) {
+            il.gu = b.items_gu;
+            il.n_gu = b.n_items;
+            il.mt_gu = tc_tiles_gateup(a.inter);
+            il.dn = b.items_dn;
+            il.n_dn = b.n_items + 1;
+            il.mt_dn = tc_tiles_down(a.n_out);
+            il.nt = tc_token_tile(T * a.K, a.E);
+            il.zero = b.tc_err;
+        }
+        launch_dispatch(T, a.K, a.E, rb, s, il);
         g_launches += 3;
     }
     ExpertTable et{a.tab->d_w};
@@ -729,7 +741,6 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     if (b.use_tc) {
         // tensor-core path: fp16 gather, gate/up GEMM + SwiGLU, down GEMM (gate/up phase times all)
         PhaseScope ps(kGateUp, s);
-        CK(cudaMemsetAsync(b.tc_err, 0, sizeof(int), s));
         static unsigned long long* stats = nullptr;   // DRACO_B200_TC_STATS=1: per-site wait cycles
         if (!stats && env_flag("DRACO_B200_TC_STATS")) {
             cudaMallocManaged(&stats, sizeof(unsigned long long) * 2 * kTcStatSites);
@@ -755,7 +766,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
             set_err("tensor-core grouped GEMM launch failed (%d): %s", rc, cudaGetErrorString(cudaGetLastError()));
             return -3;
         }
-        g_launches += 5;
+        g_launches += 3;
     } else {
     {
         PhaseScope ps(kGateUp, s);

@@ -36,10 +36,26 @@ struct ExpertTable {
     const uint8_t* const* w;   // device array [3 * n_exp] of device pointers (gate, up, down)
 };
 
+// logits[t][e] = sum_k X[t][k] * gate_inp[e][k] (k ascending, rounded products); also sets
+// *zero_err = 0 when given (the routing status word the select kernel then raises)
 void launch_router_logits(const float* X, const float* gate_inp, int T, int E, int H, float* logits,
-                          cudaStream_t s);
+                          cudaStream_t s, int* zero_err = nullptr);
 void launch_router_select(const RouterParams& p, int T, RouteBufs& b, cudaStream_t s);
-void launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s);
+// Work items of the tensor-core grouped GEMM (int4 {expert, row tile, first sorted position,
+// tokens}): per active expert in increasing order, its token tiles of <= nt, each times the
+// row tiles of the matrix.  Built by the dispatch scan when `gu` is set, which also zeroes
+// *zero (the GEMM's status word).
+struct ItemLists {
+    int4* gu = nullptr;
+    int* n_gu = nullptr;
+    int mt_gu = 0;
+    int4* dn = nullptr;
+    int* n_dn = nullptr;
+    int mt_dn = 0;
+    int nt = 128;
+    int* zero = nullptr;
+};
+void launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s, const ItemLists& items = ItemLists());
 // d[0] = a, d[1] = b (small device-side constants, stream ordered and graph capturable)
 void launch_set_pair(int* d, int a, int b, cudaStream_t s);
 

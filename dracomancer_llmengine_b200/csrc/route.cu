@@ -18,7 +18,9 @@ template <int TY, int RT>
 __global__ void __launch_bounds__(32 * TY) router_logits_kernel(const float* __restrict__ X,
                                                                const float* __restrict__ W, int T,
                                                                int E, int H,
-                                                               float* __restrict__ logits) {
+                                                               float* __restrict__ logits,
+                                                               int* __restrict__ zero_err) {
+    if (zero_err && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && threadIdx.y == 0) *zero_err = 0;
     constexpr int KC = 32;
     __shared__ float ws[32][KC + 1];
     __shared__ float xs[TY * RT][KC + 1];
@@ -80,8 +82,10 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_b
                  : "memory");
 }
 __global__ void __launch_bounds__(rl::NTH) router_logits_v2(const float* __restrict__ X, const float* __restrict__ W,
-                                                            int T, int E, int H, float* __restrict__ logits) {
+                                                            int T, int E, int H, float* __restrict__ logits,
+                                                            int* __restrict__ zero_err) {
     using namespace rl;
+    if (zero_err && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *zero_err = 0;
     extern __shared__ __align__(16) float rl_smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ti = lane & 7, ep = 8 * warp + 2 * (lane >> 3);   // token row, first expert row (tile-relative)
@@ -152,15 +156,15 @@ __global__ void __launch_bounds__(rl::NTH) router_logits_v2(const float* __restr
 }
 
 void launch_router_logits(const float* X, const float* W, int T, int E, int H, float* logits,
-                          cudaStream_t s) {
+                          cudaStream_t s, int* zero_err) {
     const bool vec_ok = H % 4 == 0 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0;
     if (T <= 4 || !vec_ok) {
         dim3 grid((E + 31) / 32, (T + 3) / 4);
-        router_logits_kernel<4, 1><<<grid, dim3(32, 4), 0, s>>>(X, W, T, E, H, logits);
+        router_logits_kernel<4, 1><<<grid, dim3(32, 4), 0, s>>>(X, W, T, E, H, logits, zero_err);
     } else {
         cudaFuncSetAttribute(router_logits_v2, cudaFuncAttributeMaxDynamicSharedMemorySize, rl::kSmem);
         dim3 grid((T + 7) / 8, (E + 31) / 32);
-        router_logits_v2<<<grid, rl::NTH, rl::kSmem, s>>>(X, W, T, E, H, logits);
+        router_logits_v2<<<grid, rl::NTH, rl::kSmem, s>>>(X, W, T, E, H, logits, zero_err);
     }
 }
 
@@ -414,9 +418,10 @@ __global__ void __launch_bounds__(kChunk) dispatch_count_kernel(const int* __res
 __global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restrict__ chunk_counts, int n_chunks,
                                                                    int E, int* __restrict__ counts,
                                                                    int* __restrict__ off, int* __restrict__ active,
-                                                                   int* __restrict__ n_active) {
+                                                                   int* __restrict__ n_active, ItemLists il) {
     __shared__ int sv[kMaxExperts];
     __shared__ int sa[kMaxExperts];
+    __shared__ int st[kMaxExperts];
     const int e = threadIdx.x;
     // per expert: exclusive prefix over chunks (in place), total
     int c = 0;
@@ -427,15 +432,19 @@ __global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restr
             c += v;
         }
     if (e < E) counts[e] = c;
+    const int tiles = (c + il.nt - 1) / il.nt;
     sv[e] = c;
     sa[e] = c > 0 ? 1 : 0;
+    st[e] = tiles;
     __syncthreads();
     for (int o = 1; o < kMaxExperts; o <<= 1) {   // inclusive scans over experts
         const int v = e >= o ? sv[e - o] : 0;
         const int a = e >= o ? sa[e - o] : 0;
+        const int u = e >= o ? st[e - o] : 0;
         __syncthreads();
         sv[e] += v;
         sa[e] += a;
+        st[e] += u;
         __syncthreads();
     }
     const int base = sv[e] - c;   // exclusive offset of expert e
@@ -447,6 +456,32 @@ __global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restr
     if (e == 0) {
         off[0] = 0;
         *n_active = sa[kMaxExperts - 1];
+    }
+    if (!il.gu) return;
+    // tensor-core items, one per (token tile, row tile): tile j belongs to the expert whose
+    // inclusive tile prefix first exceeds j
+    const int n_tiles = st[kMaxExperts - 1];
+    if (e == 0) {
+        *il.n_gu = n_tiles * il.mt_gu;
+        *il.n_dn = n_tiles * il.mt_dn;
+        *il.zero = 0;
+    }
+    const int mt_sum = il.mt_gu + il.mt_dn;
+    for (int j = e; j < n_tiles * mt_sum; j += kMaxExperts) {
+        const int tile = j / mt_sum, r = j % mt_sum;
+        int lo = 0, hi = kMaxExperts - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (st[mid] > tile) hi = mid;
+            else lo = mid + 1;
+        }
+        const int x = lo;
+        const int cx = sv[x] - (x ? sv[x - 1] : 0);
+        const int first_tile = st[x] - (cx + il.nt - 1) / il.nt;
+        const int t0 = (tile - first_tile) * il.nt;
+        const int4 item = make_int4(x, r < il.mt_gu ? r : r - il.mt_gu, sv[x] - cx + t0, min(il.nt, cx - t0));
+        if (r < il.mt_gu) il.gu[tile * il.mt_gu + r] = item;
+        else il.dn[tile * il.mt_dn + r - il.mt_gu] = item;
     }
 }
 
@@ -475,12 +510,12 @@ __global__ void __launch_bounds__(kChunk) dispatch_place_kernel(const int* __res
     }
 }
 
-void launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s) {
+void launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s, const ItemLists& items) {
     const int n = T * K;
     const int n_chunks = max(1, (n + kChunk - 1) / kChunk);
     dispatch_count_kernel<<<n_chunks, kChunk, 0, s>>>(b.order, n, E, b.chunk_counts);
     dispatch_scan_kernel<<<1, kMaxExperts, 0, s>>>(b.chunk_counts, n_chunks, E, b.counts, b.off, b.active,
-                                                   b.n_active);
+                                                   b.n_active, items);
     dispatch_place_kernel<<<n_chunks, kChunk, 0, s>>>(b.order, n, E, b.chunk_counts, b.ilist, b.pos_of);
 }
 

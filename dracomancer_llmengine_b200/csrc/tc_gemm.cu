@@ -719,36 +719,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- helpers
-// work items: per active expert, token tiles of <= 128 sorted positions x 128-row weight tiles
-__global__ void build_items_kernel(const int* __restrict__ off, const int* __restrict__ active,
-                                   const int* __restrict__ n_active_p, int mtiles, int nt_max,
-                                   int4* __restrict__ items, int* __restrict__ n_items) {
-    __shared__ int cnt[512];
-    const int n_active = *n_active_p;
-    const int a = threadIdx.x;
-    int c = 0, e = 0;
-    if (a < n_active) {
-        e = active[a];
-        c = off[e + 1] - off[e];
-        cnt[a] = ((c + nt_max - 1) / nt_max) * mtiles;
-    } else {
-        cnt[a] = 0;
-    }
-    __syncthreads();
-    for (int o = 1; o < 512; o <<= 1) {   // inclusive scan
-        const int v = a >= o ? cnt[a - o] : 0;
-        __syncthreads();
-        cnt[a] += v;
-        __syncthreads();
-    }
-    if (a < n_active) {
-        int k = cnt[a] - ((c + nt_max - 1) / nt_max) * mtiles;
-        for (int t0 = 0; t0 < c; t0 += nt_max)
-            for (int mt = 0; mt < mtiles; mt++) items[k++] = make_int4(e, mt, off[e] + t0, min(nt_max, c - t0));
-    }
-    if (a == 511) *n_items = cnt[511];
-}
-
 // fp16 copy of the token rows in expert-sorted order: Xs[p] = X[ilist[p] / tok_div]
 __global__ void gather_half_kernel(const float* __restrict__ X, const int* __restrict__ ilist, int tok_div, int P,
                                    int H, __half* __restrict__ Xs) {
@@ -896,11 +866,7 @@ int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, i
     if (!cached_act_maps(&mx, Xs, (size_t)P, (size_t)n_in) || !cached_act_maps(&ma, act_h, (size_t)P, (size_t)inter))
         return -2;
     tc::gather_half_kernel<<<148 * 8, 256, 0, s>>>(X, ilist, tok_div, P, n_in, Xs);
-    // token tiles of <= 64 with eight activation stages for sparse loads (<= 16 tokens per
-    // expert on average), else <= 128 with four
-    const int nt = P <= 16 * n_exp ? 64 : 128;
-    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, tc_tiles_gateup(inter), nt, items_gu, n_items_gu);
-    tc::build_items_kernel<<<1, 512, 0, s>>>(off, active, n_active, tc_tiles_down(n_out), nt, items_dn, n_items_dn);
+    const int nt = tc_token_tile(P, n_exp);
     cudaError_t e;
     if (cg == DRACO_CODE_Q4_K)
         e = launch_tc<0, DRACO_CODE_Q4_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, nt, inter, n_in, inter,

@@ -18,7 +18,8 @@ bool tc_supported(int cg, int cu, int cd, int inter, int n_in, int n_out);
 int tc_make_weight_maps(TcMaps* maps, const uint8_t* gate, const uint8_t* up, const uint8_t* down, int n_exp,
                         int cg, int cd, int inter, int n_in, int n_out);
 // gather (fp16) -> gate/up GEMM (+SwiGLU, fp16 act) -> down GEMM (fp32 y), for the sorted
-// assignments described by off/active/ilist.  Scratch: Xs [P][n_in] and act_h [P][inter]
+// assignments described by off/active/ilist; the item lists were built by the dispatch scan
+// (ItemLists with tc_token_tile / tc_tiles_*).  Scratch: Xs [P][n_in] and act_h [P][inter]
 // fp16, items buffers (see tc_items_capacity), err (device int, nonzero after a timeout).
 int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, int n_out, const float* X,
            const int* ilist, int tok_div, int P, const int* off, const int* active, const int* n_active,
@@ -29,6 +30,9 @@ constexpr int kTcStatSites = 15;
 // weight-row tiles per expert: gate/up tiles hold 64 rows of each matrix, down tiles 128 rows
 inline int tc_tiles_gateup(int inter) { return inter / 64; }
 inline int tc_tiles_down(int n_out) { return n_out / 128; }
+// tokens per item for P assignments over n_exp experts: tiles of <= 64 with eight activation
+// stages for sparse loads (<= 16 tokens per expert on average), else <= 128 with four
+inline int tc_token_tile(int P, int n_exp) { return P <= 16 * n_exp ? 64 : 128; }
 // item-list capacity for P assignments over at most n_active_max experts (token tiles of 64 or
 // more tokens)
 inline size_t tc_items_capacity(int P, int n_active_max, int row_tiles) {
