@@ -54,13 +54,13 @@ constexpr int kProdWarp = 16;                 // TMA producer of the weight supe
 constexpr int kMmaWarp = 17;                  // MMA issuer, TMEM owner
 constexpr int kBProdWarp = 18;                // TMA producer of the activation tiles
 constexpr int kEpiWarp0 = 19;                 // epilogue warpgroup: warps 19..22
-constexpr int kThreads = 32 * 23;
+constexpr int kMmaWarp2 = 23;                 // second MMA issuer (odd K steps; 64-token tiles)
 constexpr int kMaxRawStages = 8;              // raw superblock-column stages
 constexpr int kSlots = 4;                     // A slots in TMEM (K steps decoded ahead of the MMAs)
 constexpr int kDone = 8;                      // ring of per-step completion barriers (>= every stage count)
 constexpr int kMaxBStages = 8;                // activation stages
 constexpr int kTmemCols = 512;
-constexpr int kAccCols = 128;                 // per accumulator buffer (N <= 128)
+constexpr int kAccCols = 128;                 // per accumulator buffer
 constexpr int kABase = 256;                   // A slots (64 columns each) start here
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // bounded waits give up after 2 s
 // try_wait may suspend the polling thread up to this long (0: poll with test_wait)
@@ -391,9 +391,15 @@ __device__ __forceinline__ void deq_q6k(const uint8_t* blk, int kc, uint32_t (&o
 }
 
 // ---------------------------------------------------------------- the kernel
-// NT = most tokens per item (64 or 128)
+// NT = most tokens per item (64 or 128).  With 64-token tiles two warps issue the MMAs (even
+// and odd K steps) into separate accumulators that the epilogue adds: both issuers' per-step
+// overheads (readiness test, commit) then overlap.
 template <int MODE, int CODE, int NT>
 struct Cfg {
+    static constexpr int kIssuers = NT == 64 ? 2 : 1;
+    static constexpr int kThreads = 32 * (NT == 64 ? 24 : 23);
+    // TMEM columns of accumulator (buffer b, issuer i): b * kAccStride + i * NT
+    static constexpr int kAccStride = kIssuers * NT;
     static constexpr int kBB = CODE == DRACO_CODE_Q4_K ? 144 : kQ6Padded;   // raw bytes per row superblock
     static constexpr int kRawStage = 128 * kBB;
     // activation stages: one K step = two 64-wide chunks x NT tokens x 128 B; 128 KB in all
@@ -421,7 +427,7 @@ struct Bars {
     uint64_t raw_full[kMaxRawStages], raw_empty[kMaxRawStages];
     uint64_t a_full[kSlots], b_full[kMaxBStages];
     uint64_t done[kDone];                      // done[q % 8]: MMAs of K step q finished
-    uint64_t acc_full[2], acc_empty[2], drain;
+    uint64_t acc_full[2], acc_empty[2], drain[2];
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -433,7 +439,7 @@ struct Bars {
 __device__ __forceinline__ int gu_row(int quarter, int i) { return 16 * quarter + ((i & 16) >> 1) + (i & 7); }
 
 template <int MODE, int CODE, int NT, bool STATS>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
     moe_tc_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                   const __grid_constant__ ActMaps tmB, const int4* __restrict__ items,
                   const int* __restrict__ n_items_p, int rows_per_expert, int K, int out_ld,
@@ -462,10 +468,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < C::kBStages; i++) mbar_init(&bars->b_full[i], 1);
         for (int i = 0; i < kDone; i++) mbar_init(&bars->done[i], 1);
         for (int i = 0; i < 2; i++) {
-            mbar_init(&bars->acc_full[i], 1);
+            mbar_init(&bars->acc_full[i], C::kIssuers);
             mbar_init(&bars->acc_empty[i], 4);
+            mbar_init(&bars->drain[i], 1);
         }
-        mbar_init(&bars->drain, 1);
         bars->abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -545,8 +551,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t r = q - 1 - k;
                 mbar_drain(&bars->b_full[r % C::kBStages], (r / C::kBStages) & 1);
             }
-    } else if (warp == kMmaWarp) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == kMmaWarp || (C::kIssuers == 2 && warp == kMmaWarp2)) {
+        // ------------------------------------------------------------ MMA issuer(s)
+        const int iss = warp == kMmaWarp ? 0 : 1;   // issues the K steps with (step & 1) == iss
         const uint64_t desc0 = sdesc_sw128(smem_u32(bt));
         uint32_t q = 0, n_done = 0;
         bool ok = true;
@@ -563,52 +570,57 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 tc_fence_after();
             }
-            const uint32_t d_tm = tmem + buf * kAccCols;
-            bool rdy = __all_sync(0xffffffffu, mbar_test2(&bars->a_full[q % kSlots], (q / kSlots) & 1,
-                                                          &bars->b_full[q % C::kBStages], (q / C::kBStages) & 1));
-            for (int s2 = 0; s2 < 2 * nb; s2++, q++) {
-                const int sl = q % kSlots, bs = q % C::kBStages;
+            const uint32_t d_tm = tmem + buf * C::kAccStride + iss * NT;
+            const int nsteps = 2 * nb;   // even, so a step's parity is the same in every item
+            uint32_t qi = q + (C::kIssuers == 2 ? iss : 0);   // this issuer's first step
+            bool rdy = __all_sync(0xffffffffu, mbar_test2(&bars->a_full[qi % kSlots], (qi / kSlots) & 1,
+                                                          &bars->b_full[qi % C::kBStages], (qi / C::kBStages) & 1));
+            for (int s2 = qi - q; s2 < nsteps; s2 += C::kIssuers, qi += C::kIssuers) {
+                const int sl = qi % kSlots, bs = qi % C::kBStages;
                 if (!rdy) {
                     st.start();
-                    ok = warp_wait(&bars->a_full[sl], (q / kSlots) & 1, abort_flag, err, 5);
+                    ok = warp_wait(&bars->a_full[sl], (qi / kSlots) & 1, abort_flag, err, 5);
                     st.stop(kStMmaAFull);
                     if (!ok) break;
                     st.start();
-                    ok = warp_wait(&bars->b_full[bs], (q / C::kBStages) & 1, abort_flag, err, 4);
+                    ok = warp_wait(&bars->b_full[bs], (qi / C::kBStages) & 1, abort_flag, err, 4);
                     st.stop(kStMmaBFull);
                     if (!ok) break;
                 }
                 tc_fence_after();
-                // readiness of the next step, tested before this step's MMAs are issued
+                // readiness of this issuer's next step, tested before this step's MMAs are issued
                 st.start();
-                if (s2 + 1 < 2 * nb)
+                const uint32_t qn = qi + C::kIssuers;
+                if (s2 + C::kIssuers < nsteps)
                     rdy = __all_sync(0xffffffffu,
-                                     mbar_test2(&bars->a_full[(q + 1) % kSlots], ((q + 1) / kSlots) & 1,
-                                                &bars->b_full[(q + 1) % C::kBStages], ((q + 1) / C::kBStages) & 1));
+                                     mbar_test2(&bars->a_full[qn % kSlots], (qn / kSlots) & 1,
+                                                &bars->b_full[qn % C::kBStages], (qn / C::kBStages) & 1));
                 st.stop(kStMmaTest);
                 st.start();
                 const uint32_t a_tm = tmem + kABase + 64 * sl;
                 const uint64_t bd = desc0 + (uint64_t)(bs * (C::kBStage >> 4));
+                const bool first = s2 < C::kIssuers;   // this accumulator's first step of the item
                 if (elect_one()) {
 #pragma unroll
                     for (int c = 0; c < 2; c++) {
 #pragma unroll
                         for (int j = 0; j < 4; j++)
                             tc_mma_ts(d_tm, a_tm + 32 * c + 8 * j, bd + (uint64_t)(c * sub + 2 * j), idesc,
-                                      (s2 | c | j) != 0 ? 1u : 0u);
+                                      (!first || c || j) ? 1u : 0u);
                     }
-                    tc_commit(&bars->done[q % kDone]);
+                    tc_commit(&bars->done[qi % kDone]);
                 }
                 __syncwarp();
                 st.stop(kStMmaIssue);
             }
+            q += nsteps;
             if (ok && elect_one()) tc_commit(&bars->acc_full[buf]);
             __syncwarp();
         }
         // every issued MMA must finish before TMEM is released
         if (elect_one()) {
-            tc_commit(&bars->drain);
-            mbar_drain(&bars->drain, 0);
+            tc_commit(&bars->drain[iss]);
+            mbar_drain(&bars->drain[iss], 0);
         }
         __syncwarp();
     } else if (warp < kDeqWarps) {
@@ -658,6 +670,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ epilogue
         const int quarter = warp & 3;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        // 16 accumulator columns, the two issuers' partial sums added (even steps first)
+        auto ld_acc = [&](uint32_t addr, uint32_t (&v)[16]) {
+            tc_ld16(addr, v);
+            if (C::kIssuers == 2) {
+                uint32_t w[16];
+                tc_ld16(addr + NT, w);
+                tc_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; i++) v[i] = __float_as_uint(__fadd_rn(__uint_as_float(v[i]), __uint_as_float(w[i])));
+            } else {
+                tc_wait_ld();
+            }
+        };
         uint32_t n_done = 0;
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, n_done++) {
             const int4 item = items[it];
@@ -669,7 +694,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             st.start();
             tc_fence_after();
-            const uint32_t acc = tmem + lane_base + buf * kAccCols;
+            const uint32_t acc = tmem + lane_base + buf * C::kAccStride;
             if (MODE == 0) {
                 // lanes i (gate) and i ^ 8 (up) share an intermediate row; per column pair the
                 // gate lane finishes the even column and the up lane the odd one
@@ -677,8 +702,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int orow = mt * 64 + gu_row(quarter, lane);
                 for (int tb = 0; tb < ntok; tb += 16) {
                     uint32_t v[16];
-                    tc_ld16(acc + tb, v);
-                    tc_wait_ld();
+                    ld_acc(acc + tb, v);
 #pragma unroll
                     for (int c = 0; c < 16; c += 2) {
                         const float mine_e = __uint_as_float(v[c]), mine_o = __uint_as_float(v[c + 1]);
@@ -693,8 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int orow = mt * 128 + quarter * 32 + lane;
                 for (int tb = 0; tb < ntok; tb += 16) {
                     uint32_t v[16];
-                    tc_ld16(acc + tb, v);
-                    tc_wait_ld();
+                    ld_acc(acc + tb, v);
                     float* dst = y_out + (size_t)(p0 + tb) * out_ld + orow;
                     const int nt = min(16, ntok - tb);
 #pragma unroll
@@ -708,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             st.stop(kStEpiWork);
         }
     }
-    if (warp == kMmaWarp) st.total(kStMmaTotal, t_begin);
+    if (warp == kMmaWarp) st.total(kStMmaTotal, t_begin);   // the first issuer only
     if (lane == 0) st.flush(stats);
     tc_fence_before();
     __syncthreads();
@@ -819,7 +842,7 @@ cudaError_t launch_tc_k(const CUtensorMap& a0, const CUtensorMap& a1, const tc::
     auto kern = tc::moe_tc_kernel<MODE, CODE, NT, STATS>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) return e;
-    kern<<<grid, tc::kThreads, C::kSmem, s>>>(a0, a1, b, items, n_items, rows_per_expert, K, out_ld, act, y, err,
+    kern<<<grid, C::kThreads, C::kSmem, s>>>(a0, a1, b, items, n_items, rows_per_expert, K, out_ld, act, y, err,
                                               stats);
     return cudaGetLastError();
 }

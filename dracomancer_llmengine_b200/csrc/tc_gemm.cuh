@@ -30,9 +30,10 @@ constexpr int kTcStatSites = 15;
 // weight-row tiles per expert: gate/up tiles hold 64 rows of each matrix, down tiles 128 rows
 inline int tc_tiles_gateup(int inter) { return inter / 64; }
 inline int tc_tiles_down(int n_out) { return n_out / 128; }
-// tokens per item for P assignments over n_exp experts: tiles of <= 64 with eight activation
-// stages for sparse loads (<= 16 tokens per expert on average), else <= 128 with four
-inline int tc_token_tile(int P, int n_exp) { return P <= 16 * n_exp ? 64 : 128; }
+// tokens per item for P assignments over n_exp experts: tiles of <= 64 (eight activation
+// stages, two MMA issuers) when experts average <= 40 tokens, else <= 128 (four stages, one
+// issuer)
+inline int tc_token_tile(int P, int n_exp) { return P <= 40 * n_exp ? 64 : 128; }
 // item-list capacity for P assignments over at most n_active_max experts (token tiles of 64 or
 // more tokens)
 inline size_t tc_items_capacity(int P, int n_active_max, int row_tiles) {
