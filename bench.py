@@ -66,9 +66,26 @@ def layer_work(layer, order, T):
     assign = int(((order >= 0) & (order < layer.n_exp)).sum())
     flops = 2 * 3 * H * F * assign + (2 * 3 * H * layer.shared_inter * T if layer.shared_inter else 0) \
         + 2 * T * layer.n_exp * H
-    gateup_bytes = distinct * gu + T * H * 4
+    # the gate/up grouped GEMM kernel: gate+up weights of the distinct experts, the fp16 token
+    # row of every assignment in, the fp16 SwiGLU activation of every assignment out
+    gateup_bytes = distinct * gu + assign * H * 2 + assign * F * 2
     return dict(distinct=distinct, bytes=total_bytes, flops=flops, gateup_bytes=gateup_bytes,
                 gateup_flops=2 * 2 * H * F * assign)
+
+
+def profiled_traffic(config: str):
+    """DRAM bytes per launch of the gate/up GEMM kernel from the committed ncu summary of this
+    workload (profiles/tc_gemm_<config>.md, line `traffic_bytes_per_launch: N`), else None."""
+    p = os.path.join(ROOT, "profiles", f"tc_gemm_{config}.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
 
 
 class ClockSampler:
@@ -322,7 +339,8 @@ def main():
     gu_ms = prof["gateup"][0] / max(prof["gateup"][1], 1)
     gu_gbs = work["gateup_bytes"] / (gu_ms / 1e3) / 1e9
     roof = {"kernel": "gateup (grouped dequant GEMM, gate+up+SwiGLU)", "bound": "hbm", "achieved": gu_gbs,
-            "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm, "traffic": None,
+            "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm, "traffic": profiled_traffic(args.config),
+            "algorithmic_bytes": work["gateup_bytes"],
             "peak_source": src, "kernel_ms": gu_ms,
             "layer_gbs": work["bytes"] / (ms_per_step / 1e3) / 1e9,
             "layer_tflops": work["flops"] / (ms_per_step / 1e3) / 1e12,

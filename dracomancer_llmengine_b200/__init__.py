@@ -123,7 +123,7 @@ def lib() -> ct.CDLL:
     return _LIB
 
 
-PHASES = ("route", "dispatch", "gateup", "down", "shared", "combine")
+PHASES = ("route", "dispatch", "gateup", "down", "shared", "combine", "gather")
 
 
 def profile(enable: bool) -> None:

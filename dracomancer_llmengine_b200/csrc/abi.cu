@@ -57,7 +57,7 @@ long g_launches = 0;          // kernels this library launched (all devices)
 
 // Optional per-phase device timing: CUDA events recorded around each phase on the launching
 // stream, resolved when read.
-enum Phase { kRoute = 0, kDispatch, kGateUp, kDown, kShared, kCombine, kPhases };
+enum Phase { kRoute = 0, kDispatch, kGateUp, kDown, kShared, kCombine, kGather, kPhases };
 bool g_prof = false;
 struct PendingEv {
     int phase;
@@ -739,16 +739,27 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     ExpertTable et{a.tab->d_w};
     const int na_max = std::min(a.E, T * a.K);
     if (b.use_tc) {
-        // tensor-core path: fp16 gather, gate/up GEMM + SwiGLU, down GEMM (gate/up phase times all)
-        PhaseScope ps(kGateUp, s);
+        // tensor-core path: fp16 gather, gate/up GEMM + SwiGLU, down GEMM
         static unsigned long long* stats = nullptr;   // DRACO_B200_TC_STATS=1: per-site wait cycles
         if (!stats && env_flag("DRACO_B200_TC_STATS")) {
             cudaMallocManaged(&stats, sizeof(unsigned long long) * 2 * kTcStatSites);
             cudaMemset(stats, 0, sizeof(unsigned long long) * 2 * kTcStatSites);
         }
-        const int rc = tc_run(*(const TcMaps*)a.tab->tc, a.tab->cg, a.tab->cd, a.E, a.inter, a.n_in, a.n_out, b.x,
-                              rb.ilist, a.K, T * a.K, rb.off, rb.active, rb.n_active, b.xs_h, b.act_h, b.y,
-                              b.items_gu, b.n_items, b.items_dn, b.n_items + 1, b.tc_err, stats, s);
+        TcCall call;
+        int rc = tc_prepare(&call, a.tab->cg, a.tab->cd, a.E, a.inter, a.n_in, a.n_out, T * a.K, b.xs_h, b.act_h);
+        const TcMaps& maps = *(const TcMaps*)a.tab->tc;
+        if (rc == 0) {
+            PhaseScope ps(kGather, s);
+            tc_gather(call, b.x, rb.ilist, a.K, b.xs_h, s);
+        }
+        if (rc == 0) {
+            PhaseScope ps(kGateUp, s);
+            rc = tc_gateup(call, maps, b.items_gu, b.n_items, b.act_h, b.tc_err, stats, s);
+        }
+        if (rc == 0) {
+            PhaseScope ps(kDown, s);
+            rc = tc_down(call, maps, b.items_dn, b.n_items + 1, b.y, b.tc_err, stats ? stats + kTcStatSites : nullptr, s);
+        }
         if (stats) {
             cudaStreamSynchronize(s);
             static const char* names[kTcStatSites] = {"prod_raw_empty", "prod_b_empty", "mma_acc_empty", "mma_b_full",

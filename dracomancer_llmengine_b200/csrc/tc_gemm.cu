@@ -416,12 +416,9 @@ struct Cfg {
                   "rings and shared memory");
 };
 
-// activation tensor maps, one per token-tile height R = 16 (i + 1): 3D view
-// {64 halves, rows, K / 64 chunks} with box {64, R, 2}, so that one copy brings a K step's two
-// 64-wide chunks for R tokens as two SW128 tiles of R rows (tile c at byte c * R * 128)
-struct ActMaps {
-    CUtensorMap m[8];
-};
+// one copy of a map brings a K step's two 64-wide chunks for R tokens as two SW128 tiles of R
+// rows (tile c at byte c * R * 128)
+using ActMaps = TcActMaps;
 
 struct Bars {
     uint64_t raw_full[kMaxRawStages], raw_empty[kMaxRawStages];
@@ -880,30 +877,50 @@ int tc_make_weight_maps(TcMaps* maps, const uint8_t* gate, const uint8_t* up, co
     return 0;
 }
 
-int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, int n_out, const float* X,
-           const int* ilist, int tok_div, int P, const int* off, const int* active, const int* n_active,
-           __half* Xs, __half* act_h, float* y, int4* items_gu, int* n_items_gu, int4* items_dn, int* n_items_dn,
-           int* err, unsigned long long* stats, cudaStream_t s) {
+int tc_prepare(TcCall* call, int cg, int cd, int n_exp, int inter, int n_in, int n_out, int P, __half* Xs,
+               __half* act_h) {
+    call->cg = cg;
+    call->cd = cd;
+    call->n_exp = n_exp;
+    call->inter = inter;
+    call->n_in = n_in;
+    call->n_out = n_out;
+    call->P = P;
+    call->nt = tc_token_tile(P, n_exp);
     if (P <= 0) return 0;
-    tc::ActMaps mx, ma;
-    if (!cached_act_maps(&mx, Xs, (size_t)P, (size_t)n_in) || !cached_act_maps(&ma, act_h, (size_t)P, (size_t)inter))
+    if (!cached_act_maps(&call->mx, Xs, (size_t)P, (size_t)n_in) ||
+        !cached_act_maps(&call->ma, act_h, (size_t)P, (size_t)inter))
         return -2;
-    tc::gather_half_kernel<<<148 * 8, 256, 0, s>>>(X, ilist, tok_div, P, n_in, Xs);
-    const int nt = tc_token_tile(P, n_exp);
+    return 0;
+}
+
+void tc_gather(const TcCall& c, const float* X, const int* ilist, int tok_div, __half* Xs, cudaStream_t s) {
+    if (c.P > 0) tc::gather_half_kernel<<<148 * 8, 256, 0, s>>>(X, ilist, tok_div, c.P, c.n_in, Xs);
+}
+
+int tc_gateup(const TcCall& c, const TcMaps& maps, const int4* items, const int* n_items, __half* act_h, int* err,
+              unsigned long long* stats, cudaStream_t s) {
+    if (c.P <= 0) return 0;
     cudaError_t e;
-    if (cg == DRACO_CODE_Q4_K)
-        e = launch_tc<0, DRACO_CODE_Q4_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, nt, inter, n_in, inter,
+    if (c.cg == DRACO_CODE_Q4_K)
+        e = launch_tc<0, DRACO_CODE_Q4_K>(maps.gate, maps.up, c.mx, items, n_items, 148, c.nt, c.inter, c.n_in, c.inter,
                                           act_h, nullptr, err, stats, s);
     else
-        e = launch_tc<0, DRACO_CODE_Q6_K>(maps.gate, maps.up, mx, items_gu, n_items_gu, 148, nt, inter, n_in, inter,
+        e = launch_tc<0, DRACO_CODE_Q6_K>(maps.gate, maps.up, c.mx, items, n_items, 148, c.nt, c.inter, c.n_in, c.inter,
                                           act_h, nullptr, err, stats, s);
-    if (e != cudaSuccess) return -3;
-    if (cd == DRACO_CODE_Q4_K)
-        e = launch_tc<1, DRACO_CODE_Q4_K>(maps.down, maps.down, ma, items_dn, n_items_dn, 148, nt, n_out, inter, n_out,
-                                          nullptr, y, err, stats ? stats + tc::kStSites : nullptr, s);
+    return e == cudaSuccess ? 0 : -3;
+}
+
+int tc_down(const TcCall& c, const TcMaps& maps, const int4* items, const int* n_items, float* y, int* err,
+            unsigned long long* stats, cudaStream_t s) {
+    if (c.P <= 0) return 0;
+    cudaError_t e;
+    if (c.cd == DRACO_CODE_Q4_K)
+        e = launch_tc<1, DRACO_CODE_Q4_K>(maps.down, maps.down, c.ma, items, n_items, 148, c.nt, c.n_out, c.inter,
+                                          c.n_out, nullptr, y, err, stats, s);
     else
-        e = launch_tc<1, DRACO_CODE_Q6_K>(maps.down, maps.down, ma, items_dn, n_items_dn, 148, nt, n_out, inter, n_out,
-                                          nullptr, y, err, stats ? stats + tc::kStSites : nullptr, s);
+        e = launch_tc<1, DRACO_CODE_Q6_K>(maps.down, maps.down, c.ma, items, n_items, 148, c.nt, c.n_out, c.inter,
+                                          c.n_out, nullptr, y, err, stats, s);
     return e == cudaSuccess ? 0 : -3;
 }
 

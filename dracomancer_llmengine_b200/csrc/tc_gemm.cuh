@@ -12,19 +12,37 @@ struct TcMaps {
     CUtensorMap gate, up, down;
 };
 
+// activation tensor maps, one per token-tile height R = 16 (i + 1): 3D view
+// {64 halves, rows, K / 64 chunks} with box {64, R, 2}
+struct TcActMaps {
+    CUtensorMap m[8];
+};
+
+// one call's operands: the fp16 activation maps of Xs and act_h and the sizes
+struct TcCall {
+    TcActMaps mx, ma;
+    int cg = 0, cd = 0, n_exp = 0, inter = 0, n_in = 0, n_out = 0, P = 0, nt = 128;
+};
+
 // formats/shapes the tensor-core path handles
 bool tc_supported(int cg, int cu, int cd, int inter, int n_in, int n_out);
 // describe stacked weights: gate/up [n_exp*inter rows][n_in values], down [n_exp*n_out][inter]
 int tc_make_weight_maps(TcMaps* maps, const uint8_t* gate, const uint8_t* up, const uint8_t* down, int n_exp,
                         int cg, int cd, int inter, int n_in, int n_out);
-// gather (fp16) -> gate/up GEMM (+SwiGLU, fp16 act) -> down GEMM (fp32 y), for the sorted
-// assignments described by off/active/ilist; the item lists were built by the dispatch scan
-// (ItemLists with tc_token_tile / tc_tiles_*).  Scratch: Xs [P][n_in] and act_h [P][inter]
-// fp16, items buffers (see tc_items_capacity), err (device int, nonzero after a timeout).
-int tc_run(const TcMaps& maps, int cg, int cd, int n_exp, int inter, int n_in, int n_out, const float* X,
-           const int* ilist, int tok_div, int P, const int* off, const int* active, const int* n_active,
-           __half* Xs, __half* act_h, float* y, int4* items_gu, int* n_items_gu, int4* items_dn, int* n_items_dn,
-           int* err, unsigned long long* stats, cudaStream_t s);
+// The three launches of one call, for P sorted assignments (the item lists were built by the
+// dispatch scan with tc_token_tile / tc_tiles_*):
+//   tc_gather: Xs[p] = fp16(X[ilist[p] / tok_div])
+//   tc_gateup: act_h = fp16(silu(gate . Xs) * (up . Xs)) per item
+//   tc_down:   y = down . act_h per item (fp32)
+// err (device int) is nonzero after a bounded wait ran out; stats optionally collects wait
+// cycles (kTcStatSites per kernel).
+int tc_prepare(TcCall* call, int cg, int cd, int n_exp, int inter, int n_in, int n_out, int P, __half* Xs,
+               __half* act_h);
+void tc_gather(const TcCall& call, const float* X, const int* ilist, int tok_div, __half* Xs, cudaStream_t s);
+int tc_gateup(const TcCall& call, const TcMaps& maps, const int4* items, const int* n_items, __half* act_h, int* err,
+              unsigned long long* stats, cudaStream_t s);
+int tc_down(const TcCall& call, const TcMaps& maps, const int4* items, const int* n_items, float* y, int* err,
+            unsigned long long* stats, cudaStream_t s);
 // wait-statistics sites per kernel (stats holds 2 * kTcStatSites counters: gate/up, down)
 constexpr int kTcStatSites = 15;
 // weight-row tiles per expert: gate/up tiles hold 64 rows of each matrix, down tiles 128 rows

@@ -176,8 +176,8 @@ int draco_b200_set_act_mode(int mode);
 
 /* Per-phase device timing with CUDA events on the launching stream (enable != 0 turns it on
  * and clears the totals).  profile_read fills ms[i] (total milliseconds) and counts[i] for
- * phases 0 route, 1 dispatch, 2 gate/up, 3 down, 4 shared expert, 5 combine; returns the
- * number of phases. */
+ * phases 0 route, 1 dispatch, 2 gate/up, 3 down, 4 shared expert, 5 combine, 6 gather of the
+ * fp16 token rows (tensor-core path); returns the number of phases. */
 int draco_b200_profile(int enable);
 int draco_b200_profile_read(double* ms, long* counts, int n);
 /* Number of kernels this library has launched since it was loaded. */
