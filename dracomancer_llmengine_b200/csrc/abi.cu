@@ -202,6 +202,7 @@ struct Table {
     size_t dev_per[3] = {0, 0, 0};
     int inter = 0, n_in = 0, n_out = 0;
     void* tc = nullptr;              // tensor-core path state (tensor maps), owned by tc_gemm.cu
+    bool aligned16 = false;          // every matrix starts on a 16-byte boundary (bulk copies)
 };
 
 struct Ctx {
@@ -538,11 +539,15 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
             }
         }
     }
-    for (int e = 0; e < 3 * n; e++)
-        if (dptr[e] % 2 || ((e % 3 != 2 ? t.cg : t.cd) == DRACO_CODE_Q4_K && dptr[e] % 16)) {
+    t.aligned16 = true;
+    for (int e = 0; e < 3 * n; e++) {
+        const int code = e % 3 == 0 ? t.cg : e % 3 == 1 ? t.cu : t.cd;
+        if (dptr[e] % 2 || (code == DRACO_CODE_Q4_K && dptr[e] % 16)) {
             set_err("weight address 0x%llx misaligned for its format", (unsigned long long)dptr[e]);
             return nullptr;
         }
+        if (dptr[e] % 16) t.aligned16 = false;
+    }
     // an upload made while building this table may have dropped cached tables; the matrices
     // resolved above must still resolve to the same device bytes
     for (auto& m : t.mats) {
@@ -636,7 +641,9 @@ bool want_tc(const LayerArgs& a, int T) {
     const int mode = gemm_path();
     if (mode == 1 || !a.tab || !a.tab->tc || g_act_mode == 1) return false;
     if (mode == 2) return true;
-    return T * a.K >= tc_min_assignments();
+    // the tensor-core path decodes every weight once per token tile; with fewer than ~4 tokens
+    // per expert the CUDA-core GEMV over staged tiles reads the weights at HBM speed instead
+    return T * a.K >= tc_min_assignments() && T * a.K >= 4 * a.E;
 }
 
 int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
@@ -723,6 +730,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     {
         PhaseScope ps(kDispatch, s);
         ItemLists il;
+        il.zero = b.tc_err;   // status word of the expert GEMMs (both paths)
         if (b.use_tc) {
             il.gu = b.items_gu;
             il.n_gu = b.n_items;
@@ -731,10 +739,8 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
             il.n_dn = b.n_items + 1;
             il.mt_dn = tc_tiles_down(a.n_out);
             il.nt = tc_token_tile(T * a.K, a.E);
-            il.zero = b.tc_err;
         }
-        launch_dispatch(T, a.K, a.E, rb, s, il);
-        g_launches += 3;
+        g_launches += launch_dispatch(T, a.K, a.E, rb, s, il);
     }
     ExpertTable et{a.tab->d_w};
     const int na_max = std::min(a.E, T * a.K);
@@ -778,6 +784,25 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
             return -3;
         }
         g_launches += 3;
+    } else if (g_act_mode == 0 && a.tab->aligned16 &&
+               dec_supported(a.tab->cg, a.tab->cu, a.tab->cd, a.inter, a.n_in, a.n_out, a.tab->q6s)) {
+        // few tokens per expert: CUDA-core GEMV over staged weight tiles
+        int rc;
+        {
+            PhaseScope ps(kGateUp, s);
+            rc = launch_dec_gateup(et, a.tab->cg, a.tab->cu, rb.active, rb.n_active, na_max, rb.off, rb.ilist, a.K,
+                                   b.x, a.inter, a.n_in, b.act, a.tab->q6s, b.tc_err, s);
+        }
+        if (rc == 0) {
+            PhaseScope ps(kDown, s);
+            rc = launch_dec_down(et, a.tab->cd, rb.active, rb.n_active, na_max, rb.off, b.act, a.inter, a.n_out, b.y,
+                                 a.tab->q6s, b.tc_err, s);
+        }
+        if (rc) {
+            set_err("decode GEMV launch failed (%d): %s", rc, cudaGetErrorString(cudaGetLastError()));
+            return -3;
+        }
+        g_launches += 2;
     } else {
     {
         PhaseScope ps(kGateUp, s);
@@ -816,10 +841,10 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
 int check_route_err(Ctx* c, LayerBufs& b, cudaStream_t s) {
     int h_err = 0, h_tc = 0;
     CK(cudaMemcpyAsync(&h_err, b.rb.err, sizeof(int), cudaMemcpyDeviceToHost, s));
-    if (b.use_tc) CK(cudaMemcpyAsync(&h_tc, b.tc_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(&h_tc, b.tc_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
     if (h_tc) {
-        set_err("tensor-core grouped GEMM stopped after a bounded wait ran out (code 0x%x)", h_tc);
+        set_err("expert GEMM stopped after a bounded wait ran out (code 0x%x)", h_tc);
         return -5;
     }
     if (h_err) {

@@ -43,8 +43,8 @@ void launch_router_logits(const float* X, const float* gate_inp, int T, int E, i
 void launch_router_select(const RouterParams& p, int T, RouteBufs& b, cudaStream_t s);
 // Work items of the tensor-core grouped GEMM (int4 {expert, row tile, first sorted position,
 // tokens}): per active expert in increasing order, its token tiles of <= nt, each times the
-// row tiles of the matrix.  Built by the dispatch scan when `gu` is set, which also zeroes
-// *zero (the GEMM's status word).
+// row tiles of the matrix.  Built by the dispatch scan when `gu` is set.  The dispatch also
+// zeroes *zero when given (the expert GEMMs' status word).
 struct ItemLists {
     int4* gu = nullptr;
     int* n_gu = nullptr;
@@ -55,7 +55,18 @@ struct ItemLists {
     int nt = 128;
     int* zero = nullptr;
 };
-void launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s, const ItemLists& items = ItemLists());
+// returns the number of kernels launched
+int launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s, const ItemLists& items = ItemLists());
+// Decode-sized grouped GEMV with bulk-copy staged weight tiles (decode.cu): Q4_K/Q6_K only,
+// 16-byte aligned rows (Q6_K in the registry's 224-byte layout).  status gets 0x200 if a staged
+// copy did not complete in time.
+bool dec_supported(int cg, int cu, int cd, int inter, int n_in, int n_out, int q6s);
+int launch_dec_gateup(const ExpertTable& tab, int cg, int cu, const int* active, const int* n_active, int n_active_max,
+                      const int* off, const int* ilist, int tok_div, const float* X, int inter, int n_in, float* act,
+                      int q6s, int* status, cudaStream_t s);
+int launch_dec_down(const ExpertTable& tab, int cd, const int* active, const int* n_active, int n_active_max,
+                    const int* off, const float* act, int inter, int n_out, float* y, int q6s, int* status,
+                    cudaStream_t s);
 // d[0] = a, d[1] = b (small device-side constants, stream ordered and graph capturable)
 void launch_set_pair(int* d, int a, int b, cudaStream_t s);
 

@@ -70,10 +70,15 @@ __global__ void __launch_bounds__(32 * TY) router_logits_kernel(const float* __r
 // Rows are padded to 132 floats so the rows a warp reads at one k fall in distinct bank
 // groups.  Needs H % 4 == 0 and 16-byte aligned X and W.
 namespace rl {
-constexpr int KC = 128, LD = KC + 4, TT = 8, TE = 32, NS = 3, NTH = 128;
+constexpr int KC = 128, LD = KC + 4, TT = 8, TE = 32, NTH = 128;
 constexpr int NV = (TT + TE) * (KC / 4);   // 16-byte copies per chunk
 constexpr int PER = NV / NTH;
-constexpr int kSmem = NS * (TT + TE) * LD * 4;
+// ring depth: 3 chunks when each chunk carries enough work (many tokens), 8 for decode-sized
+// batches, where a chunk is only ~512 cycles of add chain against ~2 us of cold HBM latency
+template <int NS>
+constexpr int smem_bytes() {
+    return NS * (TT + TE) * LD * 4;
+}
 static_assert(NV % NTH == 0, "copies per thread");
 }
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
@@ -81,6 +86,7 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_b
                  "l"(src), "r"(src_bytes)
                  : "memory");
 }
+template <int NS>
 __global__ void __launch_bounds__(rl::NTH) router_logits_v2(const float* __restrict__ X, const float* __restrict__ W,
                                                             int T, int E, int H, float* __restrict__ logits,
                                                             int* __restrict__ zero_err) {
@@ -117,12 +123,12 @@ __global__ void __launch_bounds__(rl::NTH) router_logits_v2(const float* __restr
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    issue(0);
-    issue(1);
+#pragma unroll
+    for (int c = 0; c < NS - 1; c++) issue(c);
     float a0 = 0.f, a1 = 0.f;
     for (int c = 0; c < nc; c++) {
-        issue(c + 2);
-        asm volatile("cp.async.wait_group 2;" ::: "memory");
+        issue(c + NS - 1);
+        asm volatile("cp.async.wait_group %0;" ::"n"(NS - 1) : "memory");
         __syncthreads();
         const float* st = rl_smem + (c % NS) * (TT + TE) * LD;
         const float4* xr = reinterpret_cast<const float4*>(st + ti * LD);
@@ -140,13 +146,33 @@ __global__ void __launch_bounds__(rl::NTH) router_logits_v2(const float* __restr
             a1 = __fadd_rn(a1, __fmul_rn(xv.w, v.w));
         };
         if (kq == KC / 4) {
-            // full chunk, fully unrolled: the loads run ahead of the two add chains
+            // full chunk, fully unrolled, loads issued two steps ahead of the two add chains
+            float4 x0 = xr[0], u0 = w0r[0], v0 = w1r[0];
+            float4 x1 = xr[1], u1 = w0r[1], v1 = w1r[1];
 #pragma unroll
-            for (int q = 0; q < KC / 4; q++) step(xr[q], w0r[q], w1r[q]);
+            for (int q = 0; q < KC / 4; q += 2) {
+                float4 x2 = x0, u2 = u0, v2 = v0, x3 = x1, u3 = u1, v3 = v1;
+                if (q + 2 < KC / 4) {
+                    x2 = xr[q + 2];
+                    u2 = w0r[q + 2];
+                    v2 = w1r[q + 2];
+                    x3 = xr[q + 3];
+                    u3 = w0r[q + 3];
+                    v3 = w1r[q + 3];
+                }
+                step(x0, u0, v0);
+                step(x1, u1, v1);
+                x0 = x2;
+                u0 = u2;
+                v0 = v2;
+                x1 = x3;
+                u1 = u3;
+                v1 = v3;
+            }
         } else {
             for (int q = 0; q < kq; q++) step(xr[q], w0r[q], w1r[q]);
         }
-        __syncthreads();   // stage c % NS is refilled by the next iteration's issue(c + 3)
+        __syncthreads();   // stage c % NS is refilled by the next iteration's issue(c + NS)
     }
     const int t = t0 + ti, e = e0 + ep;
     if (t < T) {
@@ -158,13 +184,20 @@ __global__ void __launch_bounds__(rl::NTH) router_logits_v2(const float* __restr
 void launch_router_logits(const float* X, const float* W, int T, int E, int H, float* logits,
                           cudaStream_t s, int* zero_err) {
     const bool vec_ok = H % 4 == 0 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0;
-    if (T <= 4 || !vec_ok) {
+    if (!vec_ok) {
         dim3 grid((E + 31) / 32, (T + 3) / 4);
         router_logits_kernel<4, 1><<<grid, dim3(32, 4), 0, s>>>(X, W, T, E, H, logits, zero_err);
     } else {
-        cudaFuncSetAttribute(router_logits_v2, cudaFuncAttributeMaxDynamicSharedMemorySize, rl::kSmem);
         dim3 grid((T + 7) / 8, (E + 31) / 32);
-        router_logits_v2<<<grid, rl::NTH, rl::kSmem, s>>>(X, W, T, E, H, logits, zero_err);
+        if (T <= 16) {
+            constexpr int sm = rl::smem_bytes<8>();
+            cudaFuncSetAttribute(router_logits_v2<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+            router_logits_v2<8><<<grid, rl::NTH, sm, s>>>(X, W, T, E, H, logits, zero_err);
+        } else {
+            constexpr int sm = rl::smem_bytes<3>();
+            cudaFuncSetAttribute(router_logits_v2<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+            router_logits_v2<3><<<grid, rl::NTH, sm, s>>>(X, W, T, E, H, logits, zero_err);
+        }
     }
 }
 
@@ -457,6 +490,7 @@ __global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restr
         off[0] = 0;
         *n_active = sa[kMaxExperts - 1];
     }
+    if (e == 0 && il.zero) *il.zero = 0;
     if (!il.gu) return;
     // tensor-core items, one per (token tile, row tile): tile j belongs to the expert whose
     // inclusive tile prefix first exceeds j
@@ -464,7 +498,6 @@ __global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restr
     if (e == 0) {
         *il.n_gu = n_tiles * il.mt_gu;
         *il.n_dn = n_tiles * il.mt_dn;
-        *il.zero = 0;
     }
     const int mt_sum = il.mt_gu + il.mt_dn;
     for (int j = e; j < n_tiles * mt_sum; j += kMaxExperts) {
@@ -510,13 +543,83 @@ __global__ void __launch_bounds__(kChunk) dispatch_place_kernel(const int* __res
     }
 }
 
-void launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s, const ItemLists& items) {
+// All three passes in one block when the assignments fit one chunk (decode-sized batches).
+__global__ void __launch_bounds__(kChunk) dispatch_single_kernel(const int* __restrict__ order, int n, int E,
+                                                                int* __restrict__ counts, int* __restrict__ off,
+                                                                int* __restrict__ active, int* __restrict__ n_active,
+                                                                int* __restrict__ ilist, int* __restrict__ pos_of,
+                                                                int* __restrict__ zero) {
+    __shared__ int cnt[kMaxExperts];
+    if (zero && threadIdx.x == 0) *zero = 0;
+    __shared__ int sv[kMaxExperts];
+    __shared__ int sa[kMaxExperts];
+    const int tid = threadIdx.x;
+    if (tid < kMaxExperts) cnt[tid] = 0;
+    __syncthreads();
+    int e = tid < n ? order[tid] : -1;
+    if (e >= E) e = -1;
+    if (e >= 0) atomicAdd(&cnt[e], 1);
+    __syncthreads();
+    if (tid < kMaxExperts) {
+        sv[tid] = cnt[tid];
+        sa[tid] = cnt[tid] > 0 ? 1 : 0;
+    }
+    __syncthreads();
+    for (int o = 1; o < kMaxExperts; o <<= 1) {   // inclusive scans over experts
+        int v = 0, a = 0;
+        if (tid < kMaxExperts && tid >= o) {
+            v = sv[tid - o];
+            a = sa[tid - o];
+        }
+        __syncthreads();
+        if (tid < kMaxExperts) {
+            sv[tid] += v;
+            sa[tid] += a;
+        }
+        __syncthreads();
+    }
+    if (tid < E) {
+        const int c = cnt[tid];
+        counts[tid] = c;
+        off[tid + 1] = sv[tid];
+        if (c > 0) active[sa[tid] - 1] = tid;
+    }
+    if (tid == 0) {
+        off[0] = 0;
+        *n_active = sa[kMaxExperts - 1];
+    }
+    // placement: within an expert, assignments keep increasing i (warps take turns)
+    __shared__ int cursor[kMaxExperts];
+    if (tid < kMaxExperts) cursor[tid] = sv[tid] - cnt[tid];
+    __syncthreads();
+    const int lane = tid & 31, warp = tid >> 5;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    for (int w = 0; w < (n + 31) / 32; w++) {
+        if (warp == w && e >= 0) {
+            const int p = cursor[e] + rank;
+            ilist[p] = tid;
+            pos_of[tid] = p;
+        }
+        __syncwarp();
+        if (warp == w && e >= 0 && rank == 0) cursor[e] += __popc(peers);
+        __syncthreads();
+    }
+}
+
+int launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s, const ItemLists& items) {
     const int n = T * K;
     const int n_chunks = max(1, (n + kChunk - 1) / kChunk);
+    if (n_chunks == 1 && !items.gu) {   // one chunk: count, scan and place in one block
+        dispatch_single_kernel<<<1, kChunk, 0, s>>>(b.order, n, E, b.counts, b.off, b.active, b.n_active, b.ilist,
+                                                    b.pos_of, items.zero);
+        return 1;
+    }
     dispatch_count_kernel<<<n_chunks, kChunk, 0, s>>>(b.order, n, E, b.chunk_counts);
     dispatch_scan_kernel<<<1, kMaxExperts, 0, s>>>(b.chunk_counts, n_chunks, E, b.counts, b.off, b.active,
                                                    b.n_active, items);
     dispatch_place_kernel<<<n_chunks, kChunk, 0, s>>>(b.order, n, E, b.chunk_counts, b.ilist, b.pos_of);
+    return 3;
 }
 
 // host expf replica over an array (test hook)

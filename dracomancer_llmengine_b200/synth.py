@@ -19,6 +19,8 @@ same value, so the router itself produces the skewed logits.
 from __future__ import annotations
 
 import dataclasses
+import os
+
 import numpy as np
 
 CODE_Q8_0 = 0
@@ -38,6 +40,11 @@ def _f16_bytes(v: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(v.astype(np.float16)).view(np.uint8).reshape(*v.shape, 2)
 
 
+def _random_bytes(rng: np.random.Generator, n: int) -> np.ndarray:
+    """n uniform random bytes (the generator's raw 64-bit outputs, little-endian)."""
+    return rng.bit_generator.random_raw((n + 7) // 8).view(np.uint8)[:n]
+
+
 def q4k_blocks(rng: np.random.Generator, n: int) -> np.ndarray:
     """`n` Q4_K superblocks, uint8 [n, 144]."""
     sc = rng.integers(8, 64, size=(n, 8), dtype=np.int32)
@@ -52,14 +59,14 @@ def q4k_blocks(rng: np.random.Generator, n: int) -> np.ndarray:
     s[:, 4:8] = mn[:, 0:4] | ((mn[:, 4:8] >> 4) << 6)
     s[:, 8:12] = (sc[:, 4:8] & 0xF) | ((mn[:, 4:8] & 0xF) << 4)
     out[:, 4:16] = s.astype(np.uint8)
-    out[:, 16:144] = rng.integers(0, 256, size=(n, 128), dtype=np.uint8)
+    out[:, 16:144] = _random_bytes(rng, n * 128).reshape(n, 128)   # uniform nibbles
     return out
 
 
 def q6k_blocks(rng: np.random.Generator, n: int) -> np.ndarray:
     """`n` Q6_K superblocks, uint8 [n, 210]."""
     out = np.empty((n, 210), np.uint8)
-    out[:, 0:192] = rng.integers(0, 256, size=(n, 192), dtype=np.uint8)
+    out[:, 0:192] = _random_bytes(rng, n * 192).reshape(n, 192)   # uniform ql/qh bits
     mag = rng.integers(16, 128, size=(n, 16), dtype=np.int32)
     sgn = np.where(rng.integers(0, 2, size=(n, 16)) == 0, -1, 1)
     sc = (mag * sgn).astype(np.int8)
@@ -87,6 +94,22 @@ def quant_matrix(rng: np.random.Generator, code: int, n_mat: int, n_out: int, n_
     nb = n_in // BLOCK_VALUES[code]
     blocks = _GEN[code](rng, n_mat * n_out * nb)
     return blocks.reshape(n_mat, n_out * nb * BLOCK_BYTES[code])
+
+
+def expert_matrices(seed, code: int, n_mat: int, n_out: int, n_in: int) -> np.ndarray:
+    """Like quant_matrix, with matrix e drawn from its own stream default_rng([*seed, e]), so the
+    experts are generated in parallel (threads; numpy releases the GIL) and still reproducibly."""
+    import concurrent.futures
+    nb = n_in // BLOCK_VALUES[code]
+    per = n_out * nb * BLOCK_BYTES[code]
+    out = np.empty((n_mat, per), np.uint8)
+
+    def one(e):
+        out[e] = _GEN[code](np.random.default_rng([*seed, e]), n_out * nb).reshape(per)
+
+    with concurrent.futures.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as ex:
+        list(ex.map(one, range(n_mat)))
+    return out
 
 
 def rms_normed(rng: np.random.Generator, t: int, h: int) -> np.ndarray:
@@ -165,11 +188,10 @@ def make_layer(hidden: int, n_exp: int, n_used: int, inter: int, scoring: str = 
                **_unused) -> MoELayer:
     """Expert weights, router and shared expert come from independent seeded streams, so
     `weights=False` (router only, empty expert tensors) routes exactly like the full layer."""
-    rng = np.random.default_rng([seed, 0])
     if weights:
-        gate = quant_matrix(rng, code_gu, n_exp, inter, hidden)
-        up = quant_matrix(rng, code_gu, n_exp, inter, hidden)
-        down = quant_matrix(rng, code_d, n_exp, hidden, inter)
+        gate = expert_matrices((seed, 0, 0), code_gu, n_exp, inter, hidden)
+        up = expert_matrices((seed, 0, 1), code_gu, n_exp, inter, hidden)
+        down = expert_matrices((seed, 0, 2), code_d, n_exp, hidden, inter)
     else:
         gate = up = down = np.zeros((n_exp, 0), np.uint8)
     rng = np.random.default_rng([seed, 1])
