@@ -525,6 +525,7 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
             for (int e = 0; e < n; e++) dptr[3 * e + k] = (uint64_t)(uintptr_t)(d + dp * e);
         } else {
             t.stacked = false;
+            size_t dp0 = 0;
             for (int e = 0; e < n; e++) {
                 size_t dp = 0;
                 const uint8_t* d = dev_matrix(c, (const void*)(uintptr_t)ptrs[3 * e + k], kcode[k], krows[k], kin[k],
@@ -532,10 +533,11 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
                 if (!d) return nullptr;
                 t.mats.push_back(MatKey{(uintptr_t)ptrs[3 * e + k], kcode[k], krows[k], kin[k], 1, mat, d, dp});
                 dptr[3 * e + k] = (uint64_t)(uintptr_t)d;
+                if (e == 0) dp0 = dp;
             }
             if (n == 1) {
                 t.base[k] = (const uint8_t*)(uintptr_t)dptr[k];
-                t.dev_per[k] = mat;
+                t.dev_per[k] = dp0;   // the device copy's size (Q6_K padded)
             }
         }
     }
@@ -563,7 +565,7 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
         return nullptr;
     }
     // tensor-core path: stacked, densely packed copies of supported formats
-    if (t.stacked && n > 1 && tc_supported(t.cg, t.cu, t.cd, inter, n_in, n_out) &&
+    if ((t.stacked || n == 1) && tc_supported(t.cg, t.cu, t.cd, inter, n_in, n_out) &&
         t.dev_per[0] == (size_t)inter * row_bytes(t.cg, n_in, t.q6s) &&
         t.dev_per[1] == (size_t)inter * row_bytes(t.cu, n_in, t.q6s) &&
         t.dev_per[2] == (size_t)n_out * row_bytes(t.cd, inter, t.q6s)) {
@@ -634,16 +636,16 @@ struct LayerBufs {
     __half *xs_h, *act_h;          // tensor-core path operands
     int4 *items_gu, *items_dn;
     int *n_items, *tc_err;
-    bool use_tc = false;
+    int4 *items_sh_gu = nullptr, *items_sh_dn = nullptr;   // shared expert on the tensor-core path
+    int* n_items_sh = nullptr;
+    bool use_tc = false, sh_tc = false;
 };
 
 bool want_tc(const LayerArgs& a, int T) {
     const int mode = gemm_path();
     if (mode == 1 || !a.tab || !a.tab->tc || g_act_mode == 1) return false;
     if (mode == 2) return true;
-    // the tensor-core path decodes every weight once per token tile; with fewer than ~4 tokens
-    // per expert the CUDA-core GEMV over staged tiles reads the weights at HBM speed instead
-    return T * a.K >= tc_min_assignments() && T * a.K >= 4 * a.E;
+    return T * a.K >= tc_min_assignments();
 }
 
 int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
@@ -668,8 +670,17 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
     const size_t o_igu = cv.take<int4>(b.use_tc ? tc_items_capacity((int)n, na_max, tc_tiles_gateup(a.inter)) : 0);
     const size_t o_idn = cv.take<int4>(b.use_tc ? tc_items_capacity((int)n, na_max, tc_tiles_down(a.n_out)) : 0);
     const size_t o_ni = cv.take<int>(2), o_terr = cv.take<int>(1);
+    // shared expert on the tensor-core path: reuses Xs and act_h after the routed GEMMs
+    b.sh_tc = b.use_tc && a.sh && a.sh->tc && (size_t)T * a.sh_ff <= n * a.inter;
+    const size_t sh_tiles = (size_t)T / 64 + 1;
+    const size_t o_sgu = cv.take<int4>(b.sh_tc ? sh_tiles * tc_tiles_gateup(a.sh_ff) : 0);
+    const size_t o_sdn = cv.take<int4>(b.sh_tc ? sh_tiles * tc_tiles_down(a.n_out) : 0);
+    const size_t o_nsh = cv.take<int>(2);
     if (int rc = ensure_ws(c, cv.off)) return rc;
     char* w = c->ws;
+    b.items_sh_gu = (int4*)(w + o_sgu);
+    b.items_sh_dn = (int4*)(w + o_sdn);
+    b.n_items_sh = (int*)(w + o_nsh);
     b.xs_h = (__half*)(w + o_xs);
     b.act_h = (__half*)(w + o_ah);
     b.items_gu = (int4*)(w + o_igu);
@@ -701,14 +712,27 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
 
 // dense one-expert FFN over T token rows: act = silu(G x) * (U x), y = D act
 int dense_ffn(Ctx* c, Table* t, int T, const float* x, int ff, int n_in, int n_out, float* act, float* y,
-              cudaStream_t s) {
+              int* status, cudaStream_t s) {
     launch_set_pair(c->d_consts + 2, 0, T, s);   // the one expert's token list [0, T)
     ExpertTable et{t->d_w};
     {
         PhaseScope ps(kShared, s);
-        launch_gateup_codes(et, t->cg, t->cu, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, nullptr, 1, x, ff,
-                            n_in, act, s, t->q6s);
-        launch_down_code(et, t->cd, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, act, ff, n_out, y, s, t->q6s);
+        if (status && t->aligned16 && dec_supported(t->cg, t->cu, t->cd, ff, n_in, n_out, t->q6s)) {
+            int rc = launch_dec_gateup(et, t->cg, t->cu, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, nullptr, 1,
+                                       x, ff, n_in, act, t->q6s, status, s);
+            if (rc == 0)
+                rc = launch_dec_down(et, t->cd, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, act, ff, n_out, y,
+                                     t->q6s, status, s);
+            if (rc) {
+                set_err("shared-expert GEMV launch failed (%d)", rc);
+                return -3;
+            }
+        } else {
+            launch_gateup_codes(et, t->cg, t->cu, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, nullptr, 1, x,
+                                ff, n_in, act, s, t->q6s);
+            launch_down_code(et, t->cd, c->d_consts, c->d_consts + 1, 1, c->d_consts + 2, act, ff, n_out, y, s,
+                             t->q6s);
+        }
     }
     g_launches += 3;
     CK(cudaGetLastError());
@@ -826,8 +850,25 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     }
     }
     CK(cudaGetLastError());
-    if (a.sh) {
-        if (int rc = dense_ffn(c, a.sh, T, b.x, a.sh_ff, a.n_in, a.n_out, b.act_sh, b.y_sh, s)) return rc;
+    if (a.sh && b.sh_tc) {
+        // dense shared expert: the tensor-core GEMMs over all T token rows
+        PhaseScope ps(kShared, s);
+        TcCall sc;
+        int rc = tc_prepare(&sc, a.sh->cg, a.sh->cd, 1, a.sh_ff, a.n_in, a.n_out, T, b.xs_h, b.act_h);
+        const TcMaps& maps = *(const TcMaps*)a.sh->tc;
+        if (rc == 0) {
+            tc_dense_items(sc, b.items_sh_gu, b.n_items_sh, b.items_sh_dn, b.n_items_sh + 1, s);
+            tc_gather(sc, b.x, nullptr, 1, b.xs_h, s);
+            rc = tc_gateup(sc, maps, b.items_sh_gu, b.n_items_sh, b.act_h, b.tc_err, nullptr, s);
+        }
+        if (rc == 0) rc = tc_down(sc, maps, b.items_sh_dn, b.n_items_sh + 1, b.y_sh, b.tc_err, nullptr, s);
+        if (rc) {
+            set_err("shared-expert tensor-core GEMM launch failed (%d)", rc);
+            return -3;
+        }
+        g_launches += 4;
+    } else if (a.sh) {
+        if (int rc = dense_ffn(c, a.sh, T, b.x, a.sh_ff, a.n_in, a.n_out, b.act_sh, b.y_sh, b.tc_err, s)) return rc;
     }
     {
         PhaseScope ps(kCombine, s);
@@ -1112,7 +1153,7 @@ static int shexp_impl(const float* x, const uint64_t* shp, const int* shc, float
     float* dsg = (float*)(c->ws + o_sg);
     cudaStream_t s = c->stream;
     CK(cudaMemcpyAsync(dx, x, sizeof(float) * h, cudaMemcpyHostToDevice, s));
-    if (int rc = dense_ffn(c, t, 1, dx, shi, h, h, da, dy, s)) return rc;
+    if (int rc = dense_ffn(c, t, 1, dx, shi, h, h, da, dy, nullptr, s)) return rc;
     launch_shexp_gate(dx, gw, h, dy, dsg, dout, 1, s);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(out, dout, sizeof(float) * h, cudaMemcpyDeviceToHost, s));

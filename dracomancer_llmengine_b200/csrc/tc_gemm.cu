@@ -739,6 +739,24 @@ __global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
 }
 
 // ---------------------------------------------------------------- helpers
+// items of one dense matrix triple over T token rows (a shared expert): tile-major, row tiles inner
+__global__ void dense_items_kernel(int T, int nt, int mt_gu, int mt_dn, int4* __restrict__ gu, int* __restrict__ n_gu,
+                                   int4* __restrict__ dn, int* __restrict__ n_dn) {
+    const int tiles = (T + nt - 1) / nt;
+    for (int j = threadIdx.x; j < tiles * mt_gu; j += blockDim.x) {
+        const int t = j / mt_gu;
+        gu[j] = make_int4(0, j % mt_gu, t * nt, min(nt, T - t * nt));
+    }
+    for (int j = threadIdx.x; j < tiles * mt_dn; j += blockDim.x) {
+        const int t = j / mt_dn;
+        dn[j] = make_int4(0, j % mt_dn, t * nt, min(nt, T - t * nt));
+    }
+    if (threadIdx.x == 0) {
+        *n_gu = tiles * mt_gu;
+        *n_dn = tiles * mt_dn;
+    }
+}
+
 // fp16 copy of the token rows in expert-sorted order: Xs[p] = X[ilist[p] / tok_div]
 __global__ void gather_half_kernel(const float* __restrict__ X, const int* __restrict__ ilist, int tok_div, int P,
                                    int H, __half* __restrict__ Xs) {
@@ -892,6 +910,11 @@ int tc_prepare(TcCall* call, int cg, int cd, int n_exp, int inter, int n_in, int
         !cached_act_maps(&call->ma, act_h, (size_t)P, (size_t)inter))
         return -2;
     return 0;
+}
+
+void tc_dense_items(const TcCall& c, int4* items_gu, int* n_gu, int4* items_dn, int* n_dn, cudaStream_t s) {
+    tc::dense_items_kernel<<<1, 256, 0, s>>>(c.P, c.nt, tc_tiles_gateup(c.inter), tc_tiles_down(c.n_out), items_gu,
+                                             n_gu, items_dn, n_dn);
 }
 
 void tc_gather(const TcCall& c, const float* X, const int* ilist, int tok_div, __half* Xs, cudaStream_t s) {

@@ -39,6 +39,8 @@ int tc_make_weight_maps(TcMaps* maps, const uint8_t* gate, const uint8_t* up, co
 int tc_prepare(TcCall* call, int cg, int cd, int n_exp, int inter, int n_in, int n_out, int P, __half* Xs,
                __half* act_h);
 void tc_gather(const TcCall& call, const float* X, const int* ilist, int tok_div, __half* Xs, cudaStream_t s);
+// item lists of a dense (shared-expert) call: one expert, call.P token rows in order
+void tc_dense_items(const TcCall& call, int4* items_gu, int* n_gu, int4* items_dn, int* n_dn, cudaStream_t s);
 int tc_gateup(const TcCall& call, const TcMaps& maps, const int4* items, const int* n_items, __half* act_h, int* err,
               unsigned long long* stats, cudaStream_t s);
 int tc_down(const TcCall& call, const TcMaps& maps, const int4* items, const int* n_items, float* y, int* err,
