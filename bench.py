@@ -15,8 +15,11 @@ chunked prefill of 512 tokens through the H2048/E128/top-8/F768 Q4_K+Q6_K layer 
   e2e    the same layer through the C ABI with pinned host X/out: the host->device copy of X and
          the device->host copy of the output are inside the timed region.
 
-Under torchrun (N > 1) every rank runs the same per-GPU workload on its own GPU (replicas,
-weak scaling); the time is the max over ranks.  `--impl reference` times the reference's own
+Under torchrun (N > 1) the layer runs expert-parallel (dracomancer_llmengine_b200.ep): each rank
+holds E/N experts and its own batch of the configuration's token count (weak scaling: tokens per
+GPU fixed), routes it, exchanges token rows with the expert owners by NCCL all-to-all, and adds
+the returned partial rows and the shared expert at home; the time is the max over ranks and
+`value` counts the tokens of all ranks.  `--impl reference` times the reference's own
 CPU path of the layer on the host cores: routing restated from src/qwen35_prefill.py:180-188
 (numpy) + the reference's m6_moe_tok with its fused AVX-512 GEMM (oracle/_ref, compiled from
 the reference's sources); rank 0 only.
@@ -49,11 +52,15 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def layer_work(layer, order, T):
+def layer_work(layer, order, T, experts=None):
     """Algorithmic bytes and FLOPs of one layer call (weights of distinct experts touched once,
-    router, activations in/out), and the gate/up kernel's share."""
+    router, activations in/out), and the gate/up kernel's share.  `experts` = (first, count)
+    restricts the expert work to one rank's slice (expert parallelism; `order` then holds the
+    routing of every rank's tokens)."""
     from dracomancer_llmengine_b200.synth import row_bytes
     H, F = layer.hidden, layer.inter
+    lo, n = experts if experts else (0, layer.n_exp)
+    order = np.where((order >= lo) & (order < lo + n), order, -1)
     distinct = len(np.unique(order[(order >= 0) & (order < layer.n_exp)]))
     gu = 2 * F * row_bytes(layer.code_gu, H)
     dn = H * row_bytes(layer.code_d, F)
@@ -205,6 +212,8 @@ def main():
     ap.add_argument("--config", default="cfg2_prefill")
     ap.add_argument("--impl", default="draco", choices=["draco", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="fixed", choices=["fixed", "compact"],
+                    help="expert-parallel token exchange (N > 1)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -251,6 +260,8 @@ def main():
     L = dm.lib()
 
     layer, Xh = synth.make_config(args.config)
+    if rank:
+        Xh = synth.make_tokens(layer, T, cfgd["seed"] + 1000 * rank, cfgd["zipf"])
     keep: list = []
     desc = dm.layer_desc(layer, keep)
     dev = torch.device("cuda", local)
@@ -261,8 +272,16 @@ def main():
     # a dedicated (non-default) stream, as an engine would give the library
     stream = torch.cuda.Stream(dev)
     import ctypes as ct
+    ep = None
+    if world > 1:
+        from dracomancer_llmengine_b200.ep import ExpertParallelMoE
+        with torch.cuda.stream(stream):
+            ep = ExpertParallelMoE(layer, T, exchange=args.exchange, device=dev)
 
     def fwd():
+        if ep is not None:
+            ep.forward(X, out)
+            return
         rc = L.draco_b200_moe_forward(ct.byref(desc), X.data_ptr(), T, out.data_ptr(), order.data_ptr(),
                                       wtop.data_ptr(), stream.cuda_stream)
         if rc != 0:
@@ -280,8 +299,17 @@ def main():
         for _ in range(max(args.warmup, 3)):
             fwd()
     torch.cuda.synchronize()
-    order_h = order.cpu().numpy()
-    work = layer_work(layer, order_h, T)
+    experts = None
+    if ep is not None:
+        # every rank's routing, for the work of this rank's expert slice
+        mine = ep._bufs["order"][:T].contiguous()
+        allo = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allo, mine)
+        order_h = torch.cat(allo).cpu().numpy()
+        experts = (ep.ops.first, ep.ops.e_loc)
+    else:
+        order_h = order.cpu().numpy()
+    work = layer_work(layer, order_h, T, experts)
 
     # ---- value: device-resident timed region ----
     launches0 = L.draco_b200_launch_count()
@@ -318,11 +346,18 @@ def main():
     ms_per_step = tot_ms / args.steps
     value = world * T * args.steps / (tot_ms / 1e3)
 
-    # ---- e2e: through the C ABI with pinned host buffers ----
+    # ---- e2e: through the public API with pinned host buffers ----
     Xp = torch.from_numpy(Xh).pin_memory()
     Op = torch.empty((T, layer.hidden), dtype=torch.float32).pin_memory()
 
     def fwd_host():
+        if ep is not None:
+            with torch.cuda.stream(stream):
+                X.copy_(Xp, non_blocking=True)
+                ep.forward(X, out)
+                Op.copy_(out, non_blocking=True)
+            stream.synchronize()
+            return
         rc = L.draco_b200_moe_forward(ct.byref(desc), Xp.data_ptr(), T, Op.data_ptr(), None, None, None)
         if rc != 0:
             raise RuntimeError(dm.last_error())
@@ -356,8 +391,9 @@ def main():
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF superblocks)",
-            "config": dict(config, parallelism=f"replicas x{world}" if world > 1 else "single GPU",
-                           distinct_experts=work["distinct"]),
+            "config": dict(config, parallelism=(f"expert parallel x{world}: {layer.n_exp // world} experts/GPU, "
+                                                f"NCCL all-to-all ({args.exchange} blocks)") if world > 1
+                           else "single GPU", distinct_experts=work["distinct"]),
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": int(T * layer.hidden * 4),
                     "d2h_bytes_per_step": int(T * layer.hidden * 4)},
             "gpu_launches": int(launches), "roofline": roof, "clocks": clk.summary()}

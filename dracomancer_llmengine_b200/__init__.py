@@ -90,6 +90,12 @@ _SIGS = {
     "draco_b200_device_count": ([], ct.c_int),
     "draco_b200_moe_forward": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, _vp, _vp], ct.c_int),
     "draco_b200_route": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, _vp], ct.c_int),
+    "draco_b200_experts_forward": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, ct.c_int, ct.c_int, _vp,
+                                    ct.c_int, _vp], ct.c_int),
+    "draco_b200_ep_plan": ([_vp, ct.c_int, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _vp, _vp, _vp, _vp], ct.c_int),
+    "draco_b200_ep_pack": ([_vp, _vp, _vp, _vp, ct.c_int, _vp, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _vp, _vp,
+                            _vp], ct.c_int),
+    "draco_b200_ep_combine": ([_vp, _vp, ct.c_int, ct.c_int, ct.c_int, _vp, _vp, _vp], ct.c_int),
     "draco_b200_set_act_mode": ([ct.c_int], ct.c_int),
     "draco_b200_set_gemm_path": ([ct.c_int], ct.c_int),
     "draco_b200_profile": ([ct.c_int], ct.c_int),

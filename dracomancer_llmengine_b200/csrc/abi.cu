@@ -17,6 +17,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <map>
 #include <mutex>
 #include <string>
@@ -166,6 +167,18 @@ struct Region {
     bool from_device = false;   // copied from caller device memory (no host bytes to re-check)
 };
 
+// After an in-place copy of host range [h, h + bytes) into a region, the device bytes of every
+// other recorded sub-range that overlaps it are no longer that sub-range's contents: forget
+// them, so their next lookup copies again instead of trusting a matching signature.
+void forget_overlaps(Region& r, uintptr_t h, size_t bytes) {
+    for (auto it = r.subs.begin(); it != r.subs.end();) {
+        const uintptr_t a = it->first.first;
+        const size_t n = it->first.second;
+        if (a < h + bytes && h < a + n && !(a == h && n == bytes)) it = r.subs.erase(it);
+        else ++it;
+    }
+}
+
 // Signature of a host range from 16 sampled 8-byte words (first, last, evenly between).
 uint64_t host_sig(const void* p, size_t bytes) {
     const uint8_t* b = (const uint8_t*)p;
@@ -219,6 +232,7 @@ struct Ctx {
     // last use of it (recorded on its stream) before its first use
     cudaEvent_t ws_event = nullptr;
     bool ws_event_set = false;
+    cudaEvent_t legacy_event = nullptr;   // orders the library stream after the legacy default stream
     // set once a call was captured into an application's CUDA graph: that graph keeps the
     // workspace addresses, so a workspace that is outgrown is retired instead of freed
     bool ws_captured = false;
@@ -235,6 +249,15 @@ struct Ctx {
 };
 
 Ctx* g_ctx[64];
+
+// Host -> device copy that is complete on return.  cudaMemcpy from pageable memory may return
+// once the data is staged, before the DMA lands, and the library's kernels run on a non-blocking
+// stream that does not wait for the legacy stream the copy runs on.
+cudaError_t upload_sync(void* d, const void* h, size_t n) {
+    cudaError_t e = cudaMemcpy(d, h, n, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    return e;
+}
 
 bool is_device_ptr(const void* p) {
     if (!p) return false;
@@ -262,16 +285,34 @@ Ctx* get_ctx() {
         c->dev = dev;
         if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
             cudaMalloc(&c->d_consts, 4 * sizeof(int)) != cudaSuccess ||
-            cudaEventCreateWithFlags(&c->ws_event, cudaEventDisableTiming) != cudaSuccess) {
+            cudaEventCreateWithFlags(&c->ws_event, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->legacy_event, cudaEventDisableTiming) != cudaSuccess) {
             set_err("CUDA context set-up failed: %s", cudaGetErrorString(cudaGetLastError()));
             delete c;
             return nullptr;
         }
         const int init[4] = {0, 1, 0, 0};
-        cudaMemcpy(c->d_consts, init, sizeof init, cudaMemcpyHostToDevice);
+        upload_sync(c->d_consts, init, sizeof init);
         g_ctx[dev] = c;
     }
     return g_ctx[dev];
+}
+
+// Device buffers handed over without a stream may have been written on the legacy default
+// stream (a framework's default stream), which the library's non-blocking stream does not wait
+// for by itself.
+int after_legacy_stream(Ctx* c) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(c->stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (cudaEventRecord(c->legacy_event, cudaStreamLegacy) != cudaSuccess ||
+        cudaStreamWaitEvent(c->stream, c->legacy_event, 0) != cudaSuccess) {
+        set_err("ordering after the default stream failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return -3;
+    }
+    return 0;
 }
 
 void free_table(Table& t) {
@@ -316,10 +357,11 @@ const uint8_t* dev_range(Ctx* c, const void* host, size_t bytes) {
             if (sub == r.subs.end() || sub->second != sig) {
                 // new or changed contents at a known address: copy them again, in place
                 cudaDeviceSynchronize();
-                if (cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+                if (upload_sync(d, host, bytes) != cudaSuccess) {
                     set_err("weight refresh failed: %s", cudaGetErrorString(cudaGetLastError()));
                     return nullptr;
                 }
+                forget_overlaps(r, h, bytes);
                 r.subs[std::make_pair(h, bytes)] = sig;
             }
             return d;
@@ -334,7 +376,7 @@ const uint8_t* dev_range(Ctx* c, const void* host, size_t bytes) {
         set_err("cudaMalloc of %zu weight bytes failed: %s", bytes, cudaGetErrorString(cudaGetLastError()));
         return nullptr;
     }
-    if (cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+    if (upload_sync(d, host, bytes) != cudaSuccess) {
         set_err("weight upload failed: %s", cudaGetErrorString(cudaGetLastError()));
         cudaFree(d);
         return nullptr;
@@ -401,6 +443,7 @@ const uint8_t* dev_matrix(Ctx* c, const void* host, int code, int rows, int n_in
                     if (sub == r.subs.end() || sub->second != sig) {
                         cudaDeviceSynchronize();
                         if (upload_q6(d, host, false, n_mats, host_per, rows, nb)) return nullptr;
+                        forget_overlaps(r, h, bytes);
                         r.subs[std::make_pair(h, bytes)] = sig;
                     }
                 }
@@ -560,7 +603,7 @@ Table* get_table(Ctx* c, const uint64_t* ptrs, const int* codes, int n, int inte
         }
     }
     if (cudaMalloc((void**)&t.d_w, sizeof(uint64_t) * 3 * n) != cudaSuccess ||
-        cudaMemcpy((void*)t.d_w, dptr.data(), sizeof(uint64_t) * 3 * n, cudaMemcpyHostToDevice) != cudaSuccess) {
+        upload_sync((void*)t.d_w, dptr.data(), sizeof(uint64_t) * 3 * n) != cudaSuccess) {
         set_err("pointer table upload failed: %s", cudaGetErrorString(cudaGetLastError()));
         return nullptr;
     }
@@ -625,6 +668,16 @@ struct LayerArgs {
     int E = 0, K = 0, inter = 0, n_in = 0, n_out = 0;
     RouterParams rp{};
     const float* d_gi = nullptr; // router weights (device), null when routing is given
+    bool no_routed = false;      // shared expert only
+};
+
+// routing supplied by the caller: rows of ld entries, expert ids minus e_base index the layer's
+// experts (others are skipped); order == nullptr means no routed experts at all
+struct GivenRoute {
+    const int* order = nullptr;
+    const float* wtop = nullptr;
+    int ld = 0;
+    int e_base = 0;
 };
 
 struct LayerBufs {
@@ -743,6 +796,10 @@ int dense_ffn(Ctx* c, Table* t, int T, const float* x, int ff, int n_in, int n_o
 // otherwise b.rb.order / b.rb.wtop already hold it.
 int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     RouteBufs& rb = b.rb;
+    if (a.no_routed) {
+        CK(cudaMemsetAsync(rb.err, 0, sizeof(int), s));
+        CK(cudaMemsetAsync(b.tc_err, 0, sizeof(int), s));
+    } else {
     if (a.d_gi) {
         PhaseScope ps(kRoute, s);
         launch_router_logits(b.x, a.d_gi, T, a.E, a.n_in, rb.logits, s, rb.err);   // also zeroes err
@@ -780,7 +837,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         const TcMaps& maps = *(const TcMaps*)a.tab->tc;
         if (rc == 0) {
             PhaseScope ps(kGather, s);
-            tc_gather(call, b.x, rb.ilist, a.K, b.xs_h, s);
+            tc_gather(call, b.x, rb.ilist, rb.off + a.E, a.K, b.xs_h, s);
         }
         if (rc == 0) {
             PhaseScope ps(kGateUp, s);
@@ -849,6 +906,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         g_launches += 1;
     }
     }
+    }   // routed experts
     CK(cudaGetLastError());
     if (a.sh && b.sh_tc) {
         // dense shared expert: the tensor-core GEMMs over all T token rows
@@ -858,7 +916,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         const TcMaps& maps = *(const TcMaps*)a.sh->tc;
         if (rc == 0) {
             tc_dense_items(sc, b.items_sh_gu, b.n_items_sh, b.items_sh_dn, b.n_items_sh + 1, s);
-            tc_gather(sc, b.x, nullptr, 1, b.xs_h, s);
+            tc_gather(sc, b.x, nullptr, nullptr, 1, b.xs_h, s);
             rc = tc_gateup(sc, maps, b.items_sh_gu, b.n_items_sh, b.act_h, b.tc_err, nullptr, s);
         }
         if (rc == 0) rc = tc_down(sc, maps, b.items_sh_dn, b.n_items_sh + 1, b.y_sh, b.tc_err, nullptr, s);
@@ -872,7 +930,8 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     }
     {
         PhaseScope ps(kCombine, s);
-        launch_combine(b.y, rb.order, rb.wtop, rb.pos_of, T, a.K, a.E, a.n_out, a.sh ? b.y_sh : nullptr, b.out, s);
+        launch_combine(b.y, rb.order, rb.wtop, rb.pos_of, T, a.no_routed ? 0 : a.K, a.E, a.n_out,
+                       a.sh ? b.y_sh : nullptr, b.out, s);
         g_launches += 1;
     }
     CK(cudaGetLastError());
@@ -975,7 +1034,9 @@ int graph_call(Ctx* c, const std::vector<uint64_t>& key, cudaStream_t s, F&& bod
 int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, const float* gate_inp,
                const float* probs_b, int scoring, int n_exp, int n_used, int n_group, int n_group_used, int norm_w,
                float w_scale, int inter, int n_in, int n_out, const uint64_t* sh3, const int* shc3, int sh_ff,
-               float* out, int* order_out, float* wtop_out, cudaStream_t user_stream) {
+               float* out, int* order_out, float* wtop_out, cudaStream_t user_stream,
+               const GivenRoute* gr = nullptr) {
+    // gr given: the routing is the caller's and gate_inp is not used
     if (int rc = validate_shape(n_exp, n_used, inter, n_in, n_out, scoring ? n_group : 1, n_group_used)) return rc;
     if (T <= 0) return 0;
     Ctx* c = get_ctx();
@@ -992,10 +1053,13 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
     unsigned long gen0 = 0;
     for (int attempt = 0; attempt < 3; attempt++) {
         gen0 = c->gen;
-        a.d_gi = (const float*)dev_range(c, gate_inp, sizeof(float) * (size_t)n_exp * n_in);
-        if (!a.d_gi) return -1;
+        a.d_gi = nullptr;
+        if (!gr) {
+            a.d_gi = (const float*)dev_range(c, gate_inp, sizeof(float) * (size_t)n_exp * n_in);
+            if (!a.d_gi) return -1;
+        }
         a.rp.probs_b = nullptr;
-        if (scoring && probs_b) {
+        if (!gr && scoring && probs_b) {
             a.rp.probs_b = (const float*)dev_range(c, probs_b, sizeof(float) * n_exp);
             if (!a.rp.probs_b) return -1;
         }
@@ -1021,6 +1085,11 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
     a.rp.n_group_used = n_group_used;
     a.rp.norm_w = norm_w;
     a.rp.w_scale = w_scale;
+    a.no_routed = gr && !gr->order;
+    if (a.no_routed && !a.sh) {
+        set_err("no routed experts and no shared expert: nothing to compute");
+        return -1;
+    }
     LayerBufs b;
     if (int rc = carve_layer(c, a, T, b)) return rc;
     const bool dev_io = dev_kind(x);
@@ -1028,7 +1097,13 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
         set_err("device activations and outputs must be 16-byte aligned");
         return -1;
     }
+    if (gr && gr->order && (dev_kind(gr->order) != dev_io || dev_kind(gr->wtop) != dev_io)) {
+        set_err("order and wtop must live where the activations live (all host or all device)");
+        return -1;
+    }
     cudaStream_t s = (dev_io && user_stream) ? user_stream : c->stream;
+    if (dev_io && !user_stream)
+        if (int rc = after_legacy_stream(c)) return rc;
     // a stream being captured by the caller: no ordering against work outside the capture
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(s, &cap) != cudaSuccess) cudaGetLastError();
@@ -1044,6 +1119,20 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
         CK(cudaMemcpyAsync(b.x, x, sizeof(float) * (size_t)T * n_in, cudaMemcpyHostToDevice, s));
     }
     auto body = [&]() -> int {
+        if (gr && gr->order) {
+            if (dev_io) {
+                launch_route_in(gr->order, gr->wtop, gr->ld, gr->e_base, T, n_used, b.rb.order, b.rb.wtop, s);
+                g_launches += 1;
+            } else {
+                const size_t w = sizeof(int) * n_used, ld = sizeof(int) * gr->ld;
+                CK(cudaMemcpy2DAsync(b.rb.order, w, gr->order, ld, w, T, cudaMemcpyHostToDevice, s));
+                CK(cudaMemcpy2DAsync(b.rb.wtop, w, gr->wtop, ld, w, T, cudaMemcpyHostToDevice, s));
+                if (gr->e_base) {
+                    launch_route_in(b.rb.order, b.rb.wtop, n_used, gr->e_base, T, n_used, b.rb.order, b.rb.wtop, s);
+                    g_launches += 1;
+                }
+            }
+        }
         if (int rc = run_layer(c, a, T, b, s)) return rc;
         if (dev_io) {
             if (order_out)
@@ -1061,7 +1150,9 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
             (uint64_t)T, (uintptr_t)s, (uint64_t)n_exp, (uint64_t)n_used, (uint64_t)inter, (uint64_t)n_in,
             (uint64_t)n_out, (uint64_t)a.sh_ff, (uint64_t)a.rp.scoring, (uint64_t)a.rp.n_group,
             (uint64_t)a.rp.n_group_used, (uint64_t)a.rp.norm_w, (uint64_t)__float_as_uint_host(a.rp.w_scale),
-            (uint64_t)gemm_path(), (uint64_t)g_act_mode, (uint64_t)b.use_tc};
+            (uint64_t)gemm_path(), (uint64_t)g_act_mode, (uint64_t)b.use_tc, (uint64_t)(gr != nullptr),
+            (uintptr_t)(gr ? gr->order : nullptr), (uintptr_t)(gr ? gr->wtop : nullptr), (uint64_t)(gr ? gr->ld : 0),
+            (uint64_t)(gr ? gr->e_base : 0)};
         const int rc = captured ? body() : graph_call(c, key, s, body);
         if (!captured) ws_release(c, s);
         return rc;
@@ -1195,6 +1286,7 @@ static int moe_tok_impl(const float* X, const int* order, const float* wtop, con
         return -1;
     }
     if (dev_io) {
+        if (int rc = after_legacy_stream(c)) return rc;
         b.x = const_cast<float*>(X);
         b.out = out;
         CK(cudaMemcpyAsync(b.rb.order, order, sizeof(int) * n, cudaMemcpyDeviceToDevice, s));
@@ -1425,6 +1517,28 @@ int draco_b200_moe_forward(const DracoMoeLayer* L, const float* X, int T, float*
                       (cudaStream_t)stream);
 }
 
+int draco_b200_experts_forward(const DracoMoeLayer* L, const float* X, int T, const int* order, const float* wtop,
+                               int ld, int first_expert, float* out, int with_shared, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (order && (!wtop || (ld != 0 && ld < L->n_used) || first_expert < 0)) {
+        set_err("draco_b200_experts_forward: wtop missing, ld < n_used or first_expert < 0");
+        return -1;
+    }
+    GivenRoute gr;
+    gr.order = order;
+    gr.wtop = wtop;
+    gr.ld = ld ? ld : L->n_used;
+    gr.e_base = first_expert;
+    const uint64_t sh3[3] = {(uint64_t)(uintptr_t)L->sh_gate, (uint64_t)(uintptr_t)L->sh_up,
+                             (uint64_t)(uintptr_t)L->sh_down};
+    const int shc3[3] = {L->sh_code_g, L->sh_code_u, L->sh_code_d};
+    const bool has_sh = with_shared && L->sh_gate && L->sh_up && L->sh_down && L->sh_ff > 0;
+    return layer_call(X, T, L->exp_ptrs, L->exp_codes, L->gate_inp, L->probs_b, L->scoring, L->n_exp, L->n_used,
+                      L->n_group, L->n_group_used, L->norm_w, L->w_scale, L->inter, L->n_in, L->n_out,
+                      has_sh ? sh3 : nullptr, shc3, has_sh ? L->sh_ff : 0, out, nullptr, nullptr,
+                      (cudaStream_t)stream, &gr);
+}
+
 int draco_b200_route(const DracoMoeLayer* L, const float* X, int T, int* order, float* wtop, void* stream) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (int rc = validate_shape(L->n_exp, L->n_used, L->inter, L->n_in, L->n_out, L->scoring ? L->n_group : 1,
@@ -1453,6 +1567,8 @@ int draco_b200_route(const DracoMoeLayer* L, const float* X, int T, int* order, 
     b.err = (int*)(c->ws + o_e);
     const bool dev_io = dev_kind(X);
     cudaStream_t s = (dev_io && stream) ? (cudaStream_t)stream : c->stream;
+    if (dev_io && !stream)
+        if (int rc = after_legacy_stream(c)) return rc;
     const float* dx = X;
     if (!dev_io) {
         CK(cudaMemcpyAsync(c->ws + o_x, X, sizeof(float) * (size_t)T * L->n_in, cudaMemcpyHostToDevice, s));
@@ -1496,6 +1612,65 @@ int draco_b200_profile_read(double* ms, long* counts, int n) {
         if (counts) counts[i] = g_phase_n[i];
     }
     return kPhases;
+}
+
+// ---- expert-parallel exchange kernels (device pointers, asynchronous on the given stream) ----
+static bool ep_ptrs_ok(std::initializer_list<const void*> ps, const char* who) {
+    for (const void* p : ps) {
+        if (p && (!dev_kind(p) || ((uintptr_t)p & 15))) {
+            set_err("%s: buffers must be 16-byte aligned device memory", who);
+            return false;
+        }
+    }
+    return true;
+}
+
+int draco_b200_ep_plan(const int* order, int T, int K, int n_exp, int n_ranks, int block, int* counts, int* row_of,
+                       int* src_tok, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (n_ranks < 1 || n_ranks > kEpMaxRanks || n_exp % n_ranks || K < 1 || T < 0 || (block && block < T) ||
+        block < 0) {
+        set_err("draco_b200_ep_plan: need 1 <= n_ranks <= %d dividing n_exp, K >= 1, block 0 or >= T", kEpMaxRanks);
+        return -1;
+    }
+    if (!order || !counts || !row_of || !src_tok || !ep_ptrs_ok({order, counts, row_of, src_tok}, "draco_b200_ep_plan"))
+        return -1;
+    launch_ep_plan(order, T, K, n_exp, n_ranks, block, counts, row_of, src_tok, (cudaStream_t)stream);
+    g_launches += 1;
+    CK(cudaGetLastError());
+    return 0;
+}
+
+int draco_b200_ep_pack(const float* X, const int* order, const float* wtop, const int* counts, int n_ranks,
+                       const int* src_tok, int block, int cap, int K, int H, float* send_x, int* send_meta,
+                       void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (n_ranks < 1 || n_ranks > kEpMaxRanks || H % 4 || K < 1 || cap < 0 || block < 0) {
+        set_err("draco_b200_ep_pack: need 1 <= n_ranks <= %d, H %% 4 == 0, K >= 1", kEpMaxRanks);
+        return -1;
+    }
+    if (!ep_ptrs_ok({X, order, wtop, counts, src_tok, send_x, send_meta}, "draco_b200_ep_pack")) return -1;
+    if (cap == 0) return 0;
+    launch_ep_pack(X, order, wtop, counts, n_ranks, src_tok, block, cap, K, H, send_x, send_meta,
+                   (cudaStream_t)stream);
+    g_launches += 1;
+    CK(cudaGetLastError());
+    return 0;
+}
+
+int draco_b200_ep_combine(const float* back, const int* row_of, int T, int n_ranks, int H, const float* shared,
+                          float* out, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (n_ranks < 1 || n_ranks > kEpMaxRanks || H % 4 || T < 0) {
+        set_err("draco_b200_ep_combine: need 1 <= n_ranks <= %d, H %% 4 == 0", kEpMaxRanks);
+        return -1;
+    }
+    if (!ep_ptrs_ok({back, row_of, shared, out}, "draco_b200_ep_combine")) return -1;
+    if (T == 0) return 0;
+    launch_ep_combine(back, row_of, T, n_ranks, H, shared, out, (cudaStream_t)stream);
+    g_launches += 1;
+    CK(cudaGetLastError());
+    return 0;
 }
 
 long draco_b200_launch_count(void) {

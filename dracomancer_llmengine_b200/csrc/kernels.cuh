@@ -102,6 +102,23 @@ void launch_shexp_gate(const float* x, const float* gw, int h, const float* y, f
 // host expf replica over an array (test hook)
 void launch_expf(const float* x, float* y, long n, cudaStream_t s);
 
+// ---- expert parallelism: token exchange over G ranks (experts split contiguously) ----
+constexpr int kEpMaxRanks = 16;
+// per-rank send plan of one rank's tokens: counts[G], row_of[T*G] (row or -1), src_tok[rows];
+// block > 0 places rank r's rows from r*block on
+void launch_ep_plan(const int* order, int T, int K, int E, int G, int block, int* counts, int* row_of,
+                    int* src_tok, cudaStream_t s);
+// send rows: X[src_tok[row]] and the routing row (K ids, K weight bits) for every planned row
+void launch_ep_pack(const float* X, const int* order, const float* wtop, const int* counts, int G,
+                    const int* src_tok, int block, int cap, int K, int H, float* send_x, int* send_meta,
+                    cudaStream_t s);
+// out[t] = sum over ranks (ascending) of back[row_of[t*G + r]] + shared[t]
+void launch_ep_combine(const float* back, const int* row_of, int T, int G, int H, const float* shared,
+                       float* out, cudaStream_t s);
+// given routing rows (row stride ld) into contiguous [T][K] buffers, ids minus e_base
+void launch_route_in(const int* order, const float* wtop, int ld, int e_base, int T, int K, int* o_order,
+                     float* o_wtop, cudaStream_t s);
+
 // ---- Q8_K activation mode ----
 void launch_q8k_quantize(const float* x, int rows, int n, float* d, int8_t* q, int16_t* bsums,
                          cudaStream_t s);

@@ -10,7 +10,7 @@
 //   down mode:    128 rows of the down matrix, B = act; the epilogue writes y (fp32).
 //
 // Data path per 256-value superblock column of the tile:
-//   TMA (no multicast) copies the 128 rows' raw superblocks (Q4_K 144 B, Q6_K 224 B padded)
+//   TMA copies (each CTA its own) the 128 rows' raw superblocks (Q4_K 144 B, Q6_K 224 B padded)
 //   into a shared-memory ring -> 16 dequant warps (4 warpgroups, thread = TMEM lane) decode
 //   64 values at a time to fp16 in registers and store them into TMEM (tcgen05.st), where
 //   they are the MMA's A operand -> one elected thread issues tcgen05.mma.kind::f16 with the
@@ -60,7 +60,6 @@ constexpr int kSlots = 4;                     // A slots in TMEM (K steps decode
 constexpr int kDone = 8;                      // ring of per-step completion barriers (>= every stage count)
 constexpr int kMaxBStages = 8;                // activation stages
 constexpr int kTmemCols = 512;
-constexpr int kAccCols = 128;                 // per accumulator buffer
 constexpr int kABase = 256;                   // A slots (64 columns each) start here
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // bounded waits give up after 2 s
 // try_wait may suspend the polling thread up to this long (0: poll with test_wait)
@@ -758,10 +757,14 @@ __global__ void dense_items_kernel(int T, int nt, int mt_gu, int mt_dn, int4* __
 }
 
 // fp16 copy of the token rows in expert-sorted order: Xs[p] = X[ilist[p] / tok_div]
-__global__ void gather_half_kernel(const float* __restrict__ X, const int* __restrict__ ilist, int tok_div, int P,
-                                   int H, __half* __restrict__ Xs) {
+// rows [0, n) with n = *n_valid when given (the assignments the dispatch placed; routing entries
+// that name no expert of the table leave the tail of ilist unwritten), else P
+__global__ void gather_half_kernel(const float* __restrict__ X, const int* __restrict__ ilist,
+                                   const int* __restrict__ n_valid, int tok_div, int P, int H,
+                                   __half* __restrict__ Xs) {
     const int per_row = H / 8;
-    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < (long)P * per_row;
+    const int n = n_valid ? min(*n_valid, P) : P;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < (long)n * per_row;
          i += (long)gridDim.x * blockDim.x) {
         const int p = (int)(i / per_row), c8 = (int)(i % per_row) * 8;
         const int t = ilist ? ilist[p] / tok_div : p;
@@ -917,8 +920,9 @@ void tc_dense_items(const TcCall& c, int4* items_gu, int* n_gu, int4* items_dn, 
                                              n_gu, items_dn, n_dn);
 }
 
-void tc_gather(const TcCall& c, const float* X, const int* ilist, int tok_div, __half* Xs, cudaStream_t s) {
-    if (c.P > 0) tc::gather_half_kernel<<<148 * 8, 256, 0, s>>>(X, ilist, tok_div, c.P, c.n_in, Xs);
+void tc_gather(const TcCall& c, const float* X, const int* ilist, const int* n_valid, int tok_div, __half* Xs,
+               cudaStream_t s) {
+    if (c.P > 0) tc::gather_half_kernel<<<148 * 8, 256, 0, s>>>(X, ilist, n_valid, tok_div, c.P, c.n_in, Xs);
 }
 
 int tc_gateup(const TcCall& c, const TcMaps& maps, const int4* items, const int* n_items, __half* act_h, int* err,

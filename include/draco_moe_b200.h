@@ -149,6 +149,41 @@ int draco_b200_moe_forward(const DracoMoeLayer* L, const float* X, int T, float*
 int draco_b200_route(const DracoMoeLayer* L, const float* X, int T, int* order, float* wtop,
                      void* stream);
 
+/* Routed experts on caller-given routing (no reference counterpart; the expert-parallel
+ * building block).  L describes a contiguous slice of a larger expert set: routing ids e with
+ * first_expert <= e < first_expert + L->n_exp select L's expert e - first_expert, all other ids
+ * (other slices, negative) are skipped.  Rows of order/wtop are ld entries apart (0: n_used);
+ * the first n_used of each row are used.
+ *   out[t] = sum over k ascending of wtop[t][k] * expert(X[t])   (+ the shared expert when
+ *            with_shared != 0 and L has one)
+ * order == NULL: no routed experts, out = shared expert (L must have one).  Pointers are all
+ * host (synchronous) or all device (asynchronous on stream when given).  gate_inp/probs_b of L
+ * are not used. */
+int draco_b200_experts_forward(const DracoMoeLayer* L, const float* X, int T, const int* order,
+                               const float* wtop, int ld, int first_expert, float* out,
+                               int with_shared, void* stream);
+
+/* Expert-parallel token exchange over n_ranks ranks that split n_exp experts contiguously
+ * (rank r owns [r*n_exp/n_ranks, (r+1)*n_exp/n_ranks)).  Device pointers, 16-byte aligned,
+ * asynchronous on stream.
+ *  ep_plan: for T local tokens with routing order[T][K]: counts[r] = rows sent to rank r (a token
+ *    sends one row to each rank owning any of its experts); row_of[t*n_ranks + r] = that row's
+ *    index in the rank-major send buffer or -1; src_tok[row] = t.  block == 0: compact rows
+ *    (rank r's rows follow rank r-1's; capacity T*min(K, n_ranks)); block >= T: rank r's rows
+ *    start at r*block (capacity n_ranks*block), the layout of an equal-split all-to-all.
+ *  ep_pack: send_x[row] = X[src_tok[row]] (H floats), send_meta[row] = {order[t][0..K),
+ *    bits of wtop[t][0..K)} (2K ints) for the first min(rows, cap) rows; with block > 0 the
+ *    unused rows of each block get ids -1 (no expert) and their activations are left as is.
+ *  ep_combine: out[t] = sum over r ascending of back[row_of[t*n_ranks + r]] (+ shared[t]);
+ *    back holds the owners' partial rows in send order. */
+int draco_b200_ep_plan(const int* order, int T, int K, int n_exp, int n_ranks, int block, int* counts,
+                       int* row_of, int* src_tok, void* stream);
+int draco_b200_ep_pack(const float* X, const int* order, const float* wtop, const int* counts, int n_ranks,
+                       const int* src_tok, int block, int cap, int K, int H, float* send_x, int* send_meta,
+                       void* stream);
+int draco_b200_ep_combine(const float* back, const int* row_of, int T, int n_ranks, int H,
+                          const float* shared, float* out, void* stream);
+
 /* Allocation-free m6_moe_tok, for callers that cannot let a library allocate device memory
  * (an engine that reserves HBM for weights and KV cache up front and forbids allocations
  * outside its pool; a decode loop that cannot take cudaMalloc's implicit synchronisation).

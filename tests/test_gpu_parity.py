@@ -173,12 +173,17 @@ def test_moe_tok_cfg2_shape(dlib, port):
     assert rel_l2(got, ref) <= REL_L2_TOL
 
 
-def test_moe_tok_skips_invalid_and_zero_tokens(dlib, port):
+@pytest.mark.parametrize("T", [12, 200])   # 200 x 4 assignments: the tensor-core path
+def test_moe_tok_skips_invalid_and_zero_tokens(dlib, port, T):
     layer = synth.make_layer(hidden=512, n_exp=16, n_used=4, inter=256, seed=41)
-    X = synth.make_tokens(layer, 12, 41)
+    X = synth.make_tokens(layer, T, 41)
     order, wtop = port.route(layer, X)
     order[0, 1] = -1          # skipped by the reference's scatter (src/m6_moe_tok.c:154)
     order[3, 2] = 16          # out of range: skipped as well
+    if T > 12:
+        rng = np.random.default_rng(3)
+        order[rng.random(order.shape) < 0.2] = -1
+        order[rng.random(order.shape) < 0.1] = 99
     ref = port.moe_tok(layer, X, order, wtop)
     got = dm.moe_tok(layer, X, order, wtop)
     assert rel_l2(got, ref) <= REL_L2_TOL
