@@ -212,8 +212,9 @@ def main():
     ap.add_argument("--config", default="cfg2_prefill")
     ap.add_argument("--impl", default="draco", choices=["draco", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="fixed", choices=["fixed", "compact"],
-                    help="expert-parallel token exchange (N > 1)")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "fixed", "compact"],
+                    help="expert-parallel token exchange (N > 1): peer-memory stores/loads with flag barriers, "
+                         "or NCCL all-to-all with fixed blocks / exchanged counts")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -381,19 +382,21 @@ def main():
     gu_ms = prof["gateup"][0] / max(prof["gateup"][1], 1)
     gu_gbs = work["gateup_bytes"] / (gu_ms / 1e3) / 1e9
     roof = {"kernel": "gateup (grouped dequant GEMM, gate+up+SwiGLU)", "bound": "hbm", "achieved": gu_gbs,
-            "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm, "traffic": profiled_traffic(args.config),
+            "peak": hbm, "unit": "GB/s", "frac": gu_gbs / hbm, "traffic": profiled_traffic(args.config) if world == 1 else None,
             "algorithmic_bytes": work["gateup_bytes"],
             "peak_source": src, "kernel_ms": gu_ms,
             "layer_gbs": work["bytes"] / (ms_per_step / 1e3) / 1e9,
             "layer_tflops": work["flops"] / (ms_per_step / 1e3) / 1e12,
             "phase_ms": {k: (v[0] / v[1] if v[1] else None) for k, v in prof.items()}}
 
+    par = "single GPU"
+    if world > 1:
+        par = f"expert parallel x{world}: {layer.n_exp // world} experts/GPU, " + (
+            "peer-memory exchange over NVLink" if args.exchange == "p2p" else f"NCCL all-to-all ({args.exchange})")
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded GGUF superblocks)",
-            "config": dict(config, parallelism=(f"expert parallel x{world}: {layer.n_exp // world} experts/GPU, "
-                                                f"NCCL all-to-all ({args.exchange} blocks)") if world > 1
-                           else "single GPU", distinct_experts=work["distinct"]),
+            "config": dict(config, parallelism=par, distinct_experts=work["distinct"]),
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": int(T * layer.hidden * 4),
                     "d2h_bytes_per_step": int(T * layer.hidden * 4)},
             "gpu_launches": int(launches), "roofline": roof, "clocks": clk.summary()}
@@ -405,6 +408,9 @@ def main():
                                 "sample": f"{len(times)} full layer calls of {T} tokens, median, ~20 s budget"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if ep is not None:
+        ep.check()
+        ep.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

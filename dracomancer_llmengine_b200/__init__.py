@@ -96,6 +96,15 @@ _SIGS = {
     "draco_b200_ep_pack": ([_vp, _vp, _vp, _vp, ct.c_int, _vp, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _vp, _vp,
                             _vp], ct.c_int),
     "draco_b200_ep_combine": ([_vp, _vp, ct.c_int, ct.c_int, ct.c_int, _vp, _vp, _vp], ct.c_int),
+    "draco_b200_ep_mem_alloc": ([ct.c_size_t, ct.POINTER(ct.c_void_p), _vp], ct.c_int),
+    "draco_b200_ep_mem_open": ([_vp, ct.POINTER(ct.c_void_p)], ct.c_int),
+    "draco_b200_ep_mem_close": ([_vp], ct.c_int),
+    "draco_b200_ep_mem_free": ([_vp], ct.c_int),
+    "draco_b200_ep_push": ([_vp, _vp, _vp, _vp, ct.c_int, ct.c_int, _vp, ct.c_int, ct.c_int, ct.c_int, _vp, _vp,
+                            _vp], ct.c_int),
+    "draco_b200_ep_barrier": ([_vp, _vp, _vp, ct.c_int, ct.c_int, _vp, _vp], ct.c_int),
+    "draco_b200_ep_pull_combine": ([_vp, _vp, ct.c_int, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _vp, _vp, _vp],
+                                   ct.c_int),
     "draco_b200_set_act_mode": ([ct.c_int], ct.c_int),
     "draco_b200_set_gemm_path": ([ct.c_int], ct.c_int),
     "draco_b200_profile": ([ct.c_int], ct.c_int),

@@ -1673,6 +1673,106 @@ int draco_b200_ep_combine(const float* back, const int* row_of, int T, int n_ran
     return 0;
 }
 
+// ---- peer memory for the expert-parallel exchange (CUDA IPC; one process per GPU) ----
+int draco_b200_ep_mem_alloc(size_t bytes, void** ptr, void* handle) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!ptr || !handle || bytes == 0) {
+        set_err("draco_b200_ep_mem_alloc: null output or zero size");
+        return -1;
+    }
+    *ptr = nullptr;
+    void* p = nullptr;
+    CK(cudaMalloc(&p, bytes));
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        set_err("draco_b200_ep_mem_alloc: %s", cudaGetErrorString(e));
+        return -3;
+    }
+    memcpy(handle, &h, sizeof h);
+    *ptr = p;
+    return 0;
+}
+
+int draco_b200_ep_mem_open(const void* handle, void** ptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!ptr || !handle) {
+        set_err("draco_b200_ep_mem_open: null argument");
+        return -1;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    CK(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return 0;
+}
+
+int draco_b200_ep_mem_close(void* ptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    CK(cudaDeviceSynchronize());
+    CK(cudaIpcCloseMemHandle(ptr));
+    return 0;
+}
+
+int draco_b200_ep_mem_free(void* ptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    CK(cudaDeviceSynchronize());
+    CK(cudaFree(ptr));
+    return 0;
+}
+
+int draco_b200_ep_push(const float* X, const int* order, const float* wtop, const int* counts, int n_ranks, int rank,
+                       const int* src_tok, int block, int K, int H, float* const* dst_x, int* const* dst_meta,
+                       void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (n_ranks < 1 || n_ranks > kEpMaxRanks || rank < 0 || rank >= n_ranks || H % 4 || K < 1 || block < 1) {
+        set_err("draco_b200_ep_push: need 0 <= rank < n_ranks <= %d, H %% 4 == 0, K >= 1, block >= 1", kEpMaxRanks);
+        return -1;
+    }
+    if (!X || !order || !wtop || !counts || !src_tok || !dst_x || !dst_meta ||
+        !ep_ptrs_ok({X, order, wtop, counts, src_tok, dst_x, dst_meta}, "draco_b200_ep_push"))
+        return -1;
+    launch_ep_push(X, order, wtop, counts, n_ranks, rank, src_tok, block, K, H, dst_x, dst_meta,
+                   (cudaStream_t)stream);
+    g_launches += 1;
+    CK(cudaGetLastError());
+    return 0;
+}
+
+int draco_b200_ep_barrier(unsigned* const* peer_flags, unsigned* my_flags, unsigned* epoch, int n_ranks, int rank,
+                          int* status, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (n_ranks < 1 || n_ranks > kEpMaxRanks || rank < 0 || rank >= n_ranks) {
+        set_err("draco_b200_ep_barrier: need 0 <= rank < n_ranks <= %d", kEpMaxRanks);
+        return -1;
+    }
+    if (!peer_flags || !my_flags || !epoch || !status ||
+        !ep_ptrs_ok({peer_flags, my_flags, epoch, status}, "draco_b200_ep_barrier"))
+        return -1;
+    launch_ep_barrier(peer_flags, my_flags, epoch, n_ranks, rank, status, (cudaStream_t)stream);
+    g_launches += 1;
+    CK(cudaGetLastError());
+    return 0;
+}
+
+int draco_b200_ep_pull_combine(const float* const* src_partial, const int* row_of, int T, int n_ranks, int rank,
+                               int block, int H, const float* shared, float* out, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (n_ranks < 1 || n_ranks > kEpMaxRanks || rank < 0 || rank >= n_ranks || H % 4 || T < 0 || block < T) {
+        set_err("draco_b200_ep_pull_combine: need 0 <= rank < n_ranks <= %d, H %% 4 == 0, T <= block", kEpMaxRanks);
+        return -1;
+    }
+    if (!src_partial || !row_of || !out || !ep_ptrs_ok({src_partial, row_of, shared, out}, "draco_b200_ep_pull_combine"))
+        return -1;
+    if (T == 0) return 0;
+    launch_ep_pull_combine(src_partial, row_of, T, n_ranks, rank, block, H, shared, out, (cudaStream_t)stream);
+    g_launches += 1;
+    CK(cudaGetLastError());
+    return 0;
+}
+
 long draco_b200_launch_count(void) {
     std::lock_guard<std::mutex> lk(g_mu);
     return g_launches;

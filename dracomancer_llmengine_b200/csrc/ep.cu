@@ -180,7 +180,136 @@ __global__ void route_in_kernel(const int* order, const float* wtop, int ld, int
     }
 }
 
+// ---- peer-memory exchange (CUDA IPC mappings of the other ranks' buffers, plain loads/stores) ----
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Dispatch by stores into the owners' receive buffers: the row for (token t, rank d) goes to
+// row rank*block + j of rank d's buffer (j = its place among the rows this rank sends to d), and
+// the unused rows of that block get routing ids -1.  Every thread fences its stores at system
+// scope before the kernel ends, so the barrier that follows publishes them.
+__global__ void ep_push_kernel(const float* __restrict__ X, const int* __restrict__ order,
+                               const float* __restrict__ wtop, const int* __restrict__ counts, int G, int rank,
+                               const int* __restrict__ src_tok, int block, int K, int H, float* const* dst_x,
+                               int* const* dst_meta) {
+    const int lane = threadIdx.x & 31;
+    const int wpb = blockDim.x >> 5;
+    const int S = G * block;
+    for (int row = blockIdx.x * wpb + (threadIdx.x >> 5); row < S; row += gridDim.x * wpb) {
+        const int d = row / block, j = row - d * block;
+        const size_t drow = (size_t)rank * block + j;
+        int* meta = dst_meta[d] + drow * 2 * K;
+        if (j >= counts[d]) {
+            for (int k = lane; k < K; k += 32) {
+                meta[k] = -1;
+                meta[K + k] = 0;
+            }
+            continue;
+        }
+        const int t = src_tok[row];
+        const float4* src = reinterpret_cast<const float4*>(X + (size_t)t * H);
+        float4* dst = reinterpret_cast<float4*>(dst_x[d] + drow * H);
+        for (int i = lane; i < H / 4; i += 32) dst[i] = src[i];
+        for (int k = lane; k < K; k += 32) {
+            meta[k] = order[(size_t)t * K + k];
+            meta[K + k] = __float_as_int(wtop[(size_t)t * K + k]);
+        }
+    }
+    __threadfence_system();
+}
+
+// All ranks meet: rank r's flag word `rank` is set to this barrier's epoch in every peer's flag
+// array (release, system scope), then each rank waits until all G words of its own array reach
+// the epoch (acquire).  The epoch counter lives in device memory, so a captured graph replays
+// correctly.  The wait gives up after kWaitNs and sets 0x400 in *status.
+constexpr uint64_t kWaitNs = 2000000000ull;
+__global__ void ep_barrier_kernel(unsigned* const* peer_flags, unsigned* my_flags, unsigned* epoch_ctr, int G,
+                                  int rank, int* status) {
+    __shared__ unsigned e;
+    if (threadIdx.x == 0) {
+        e = *epoch_ctr + 1;
+        *epoch_ctr = e;
+    }
+    __syncthreads();
+    __threadfence_system();
+    const int r = threadIdx.x;
+    if (r < G) {
+        st_release_sys(peer_flags[r] + rank, e);
+        const uint64_t t0 = global_ns();
+        for (unsigned i = 0; ld_acquire_sys(my_flags + r) - e > 0x7fffffffu; i++) {   // flag < e (wrapping)
+            if ((i & 255) == 255 && global_ns() - t0 > kWaitNs) {
+                atomicOr(status, 0x400);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// Combine by loads from the owners' partial buffers: out[t] = sum over r ascending of
+// partial_r[rank*block + j_r(t)] (+ shared[t]), j_r(t) = row_of[t][r] - r*block.
+__global__ void ep_pull_combine_kernel(const float* const* src_partial, const int* __restrict__ row_of, int T,
+                                       int G, int rank, int block, int H, const float* __restrict__ shared,
+                                       float* __restrict__ out) {
+    const int H4 = H / 4;
+    const size_t n = (size_t)T * H4;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / H4), c = (int)(i % H4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < G; r++) {
+            const int row = row_of[(size_t)t * G + r];
+            if (row < 0) continue;
+            const size_t srow = (size_t)rank * block + (row - r * block);
+            const float4 v = reinterpret_cast<const float4*>(src_partial[r] + srow * H)[c];
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        if (shared) {
+            const float4 v = reinterpret_cast<const float4*>(shared + (size_t)t * H)[c];
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        reinterpret_cast<float4*>(out + (size_t)t * H)[c] = acc;
+    }
+}
+
 }  // namespace
+
+void launch_ep_push(const float* X, const int* order, const float* wtop, const int* counts, int G, int rank,
+                    const int* src_tok, int block, int K, int H, float* const* dst_x, int* const* dst_meta,
+                    cudaStream_t s) {
+    const int rows = G * block;
+    const int blocks = std::max(1, std::min(148 * 4, (rows + 7) / 8));
+    ep_push_kernel<<<blocks, 256, 0, s>>>(X, order, wtop, counts, G, rank, src_tok, block, K, H, dst_x, dst_meta);
+}
+
+void launch_ep_barrier(unsigned* const* peer_flags, unsigned* my_flags, unsigned* epoch_ctr, int G, int rank,
+                       int* status, cudaStream_t s) {
+    ep_barrier_kernel<<<1, 32, 0, s>>>(peer_flags, my_flags, epoch_ctr, G, rank, status);
+}
+
+void launch_ep_pull_combine(const float* const* src_partial, const int* row_of, int T, int G, int rank, int block,
+                            int H, const float* shared, float* out, cudaStream_t s) {
+    const size_t n = (size_t)T * (H / 4);
+    const int blocks = (int)std::max<size_t>(1, std::min<size_t>(148 * 8, (n + 255) / 256));
+    ep_pull_combine_kernel<<<blocks, 256, 0, s>>>(src_partial, row_of, T, G, rank, block, H, shared, out);
+}
 
 void launch_ep_plan(const int* order, int T, int K, int E, int G, int block, int* counts, int* row_of,
                     int* src_tok, cudaStream_t s) {

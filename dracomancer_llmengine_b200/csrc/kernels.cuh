@@ -115,6 +115,16 @@ void launch_ep_pack(const float* X, const int* order, const float* wtop, const i
 // out[t] = sum over ranks (ascending) of back[row_of[t*G + r]] + shared[t]
 void launch_ep_combine(const float* back, const int* row_of, int T, int G, int H, const float* shared,
                        float* out, cudaStream_t s);
+// peer-memory exchange: dispatch stores into the owners' buffers (dst_x/dst_meta: device arrays
+// of G peer pointers), a flag barrier over G ranks (bounded wait, 0x400 in *status), combine
+// loads from the owners' partial buffers
+void launch_ep_push(const float* X, const int* order, const float* wtop, const int* counts, int G, int rank,
+                    const int* src_tok, int block, int K, int H, float* const* dst_x, int* const* dst_meta,
+                    cudaStream_t s);
+void launch_ep_barrier(unsigned* const* peer_flags, unsigned* my_flags, unsigned* epoch_ctr, int G, int rank,
+                       int* status, cudaStream_t s);
+void launch_ep_pull_combine(const float* const* src_partial, const int* row_of, int T, int G, int rank,
+                            int block, int H, const float* shared, float* out, cudaStream_t s);
 // given routing rows (row stride ld) into contiguous [T][K] buffers, ids minus e_base
 void launch_route_in(const int* order, const float* wtop, int ld, int e_base, int T, int K, int* o_order,
                      float* o_wtop, cudaStream_t s);

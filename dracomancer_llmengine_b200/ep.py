@@ -12,7 +12,12 @@ Two layouts:
   and adds the shared expert it computed for its own tokens.  ``exchange="fixed"`` sends blocks
   of ``max_tokens`` rows to every rank (equal splits: no count exchange, no host round trip, the
   step can be captured in a CUDA graph); ``exchange="compact"`` exchanges the row counts first
-  and sends only real rows (fewer bytes at large token counts, one host synchronisation).
+  and sends only real rows (fewer bytes at large token counts, one host synchronisation);
+  ``exchange="p2p"`` needs no collective at all: every rank maps the other ranks' receive and
+  partial buffers (CUDA IPC), the pack kernel stores the token rows straight into the owners'
+  receive buffers over NVLink, a flag barrier kernel (bounded wait) publishes them, the owners
+  compute, a second barrier, and the home's combine kernel loads the partial rows from the
+  owners' memory.
 * ``"replicated"`` (decode; every rank holds the same tokens).  Each rank routes all tokens,
   runs its own experts on them (rank 0 adds the shared expert) and an all-reduce sums the
   partial outputs.
@@ -32,7 +37,7 @@ import numpy as np
 from . import DracoError, DracoMoeLayer, _check, _u64, _i, layer_desc, lib
 
 LAYOUTS = ("a2a", "replicated")
-EXCHANGES = ("fixed", "compact")
+EXCHANGES = ("fixed", "compact", "p2p")
 
 
 def slice_desc(full: DracoMoeLayer, first: int, count: int, keep: list) -> DracoMoeLayer:
@@ -50,6 +55,85 @@ def slice_desc(full: DracoMoeLayer, first: int, count: int, keep: list) -> Draco
     d.scoring, d.n_group, d.n_group_used = 0, 1, 1
     keep.append(d)
     return d
+
+
+def tensor_at(ptr: int, shape, dtype, device):
+    """A torch tensor over existing device memory (no copy; the memory must outlive it)."""
+    import torch
+    typestr = {torch.float32: "<f4", torch.int32: "<i4", torch.int64: "<i8", torch.uint32: "<u4"}[dtype]
+
+    class _Cai:
+        pass
+    o = _Cai()
+    o.__cuda_array_interface__ = {"shape": tuple(int(v) for v in shape), "typestr": typestr, "data": (ptr, False),
+                                  "version": 3, "strides": None}
+    return torch.as_tensor(o, device=device)
+
+
+class PeerBuffers:
+    """One rank's buffers of the peer-memory exchange, allocated by the library with CUDA IPC
+    handles: receive rows x [G*B, H] fp32, routing rows meta [G*B, 2K] int32, partial rows
+    [G*B, H] fp32 and a control block (flag words [16] u32 at byte 0, barrier epoch at 64,
+    status at 128).  `link` maps every rank's buffers and builds the device pointer arrays the
+    kernels take."""
+    CTL = 256
+
+    def __init__(self, G, rank, B, H, K, device):
+        import torch
+        self.L, self.G, self.rank, self.device = lib(), G, rank, device
+        sizes = {"x": G * B * H * 4, "meta": G * B * 2 * K * 4, "partial": G * B * H * 4, "ctl": self.CTL}
+        self.own, self.handles, self.opened = {}, {}, []
+        for name, n in sizes.items():
+            p, h = ct.c_void_p(), (ct.c_char * 64)()
+            _check(self.L.draco_b200_ep_mem_alloc(n, ct.byref(p), h), "draco_b200_ep_mem_alloc")
+            self.own[name], self.handles[name] = p.value, bytes(h)
+        self.x = tensor_at(self.own["x"], (G * B, H), torch.float32, device)
+        self.meta = tensor_at(self.own["meta"], (G * B, 2 * K), torch.int32, device)
+        self.partial = tensor_at(self.own["partial"], (G * B, H), torch.float32, device)
+        ctl = self.own["ctl"]
+        self.my_flags, self.epoch, self.status = ctl, ctl + 64, ctl + 128
+        self.status_t = tensor_at(self.status, (1,), torch.int32, device)
+
+    def link(self, ptrs):
+        """ptrs[r][name]: every rank's buffer addresses in this process."""
+        import torch
+
+        def arr(name, off=0):
+            return torch.tensor([ptrs[r][name] + off for r in range(self.G)], dtype=torch.int64, device=self.device)
+        self.dst_x, self.dst_meta = arr("x"), arr("meta")
+        self.src_partial, self.peer_flags = arr("partial"), arr("ctl")
+
+    def open_peers(self, all_handles):
+        """Map the other ranks' buffers from their handles (one process per GPU)."""
+        ptrs = []
+        for r, hs in enumerate(all_handles):
+            if r == self.rank:
+                ptrs.append(dict(self.own))
+                continue
+            d = {}
+            for name, h in hs.items():
+                q = ct.c_void_p()
+                _check(self.L.draco_b200_ep_mem_open(h, ct.byref(q)), "draco_b200_ep_mem_open")
+                d[name] = q.value
+                self.opened.append(q.value)
+            ptrs.append(d)
+        self.link(ptrs)
+
+    def close_peers(self):
+        """Unmap the other ranks' buffers (waits for this device's work first)."""
+        for p in self.opened:
+            self.L.draco_b200_ep_mem_close(p)
+        self.opened = []
+
+    def free(self):
+        """Release this rank's buffers; every rank must have unmapped them first."""
+        for p in self.own.values():
+            self.L.draco_b200_ep_mem_free(p)
+        self.own = {}
+
+    def close(self):
+        self.close_peers()
+        self.free()
 
 
 class DeviceOps:
@@ -108,6 +192,20 @@ class DeviceOps:
                                             sh.data_ptr() if sh is not None else None, out.data_ptr(), self._s()),
                "draco_b200_ep_combine")
 
+    def push(self, x, order, wtop, counts, G, rank, src_tok, block, K, H, pb: PeerBuffers):
+        _check(self.L.draco_b200_ep_push(x.data_ptr(), order.data_ptr(), wtop.data_ptr(), counts.data_ptr(), G, rank,
+                                         src_tok.data_ptr(), block, K, H, pb.dst_x.data_ptr(), pb.dst_meta.data_ptr(),
+                                         self._s()), "draco_b200_ep_push")
+
+    def barrier(self, G, rank, pb: PeerBuffers):
+        _check(self.L.draco_b200_ep_barrier(pb.peer_flags.data_ptr(), pb.my_flags, pb.epoch, G, rank, pb.status,
+                                            self._s()), "draco_b200_ep_barrier")
+
+    def pull_combine(self, row_of, T, G, rank, block, H, sh, out, pb: PeerBuffers):
+        _check(self.L.draco_b200_ep_pull_combine(pb.src_partial.data_ptr(), row_of.data_ptr(), T, G, rank, block, H,
+                                                 sh.data_ptr() if sh is not None else None, out.data_ptr(),
+                                                 self._s()), "draco_b200_ep_pull_combine")
+
 
 class TorchGroup:
     """The collectives of a torch.distributed process group."""
@@ -124,6 +222,14 @@ class TorchGroup:
 
     def all_reduce(self, t):
         self.dist.all_reduce(t, group=self.group)
+
+    def barrier(self):
+        self.dist.barrier(group=self.group)
+
+    def all_gather_object(self, obj):
+        out = [None] * self.world
+        self.dist.all_gather_object(out, obj, group=self.group)
+        return out
 
 
 class ExpertParallelMoE:
@@ -156,7 +262,7 @@ class ExpertParallelMoE:
         f32, i32 = torch.float32, torch.int32
         b = {"order": o.empty((B, K), i32), "wtop": o.empty((B, K), f32), "out": o.empty((B, H), f32)}
         if self.layout == "a2a":
-            cap = G * B if self.exchange == "fixed" else B * min(K, G)
+            cap = G * B if self.exchange != "compact" else B * min(K, G)
             rcap = G * B
             b.update(counts=o.empty((G,), i32), rcounts=o.empty((G,), i32), row_of=o.empty((B, G), i32),
                      src_tok=o.empty((max(cap, 1),), i32), send_x=o.empty((cap, H), f32),
@@ -164,8 +270,30 @@ class ExpertParallelMoE:
                      recv_meta=o.empty((rcap, 2 * K), i32), partial=o.empty((rcap, H), f32),
                      back=o.empty((cap, H), f32), sh=o.empty((B, H), f32) if o.has_shared else None)
             b["cap"] = cap
+            if self.exchange == "p2p":
+                for k in ("send_x", "send_meta", "recv_x", "recv_meta", "partial", "back", "rcounts"):
+                    b[k] = None
+                self.peer = PeerBuffers(G, self.rank, B, H, K, o.device)
+                if hasattr(self.comm, "all_gather_object"):
+                    self.peer.open_peers(self.comm.all_gather_object(self.peer.handles))
         self._bufs = b
         return b
+
+    def check(self):
+        """Raise if a barrier of the peer-memory exchange gave up waiting (status read back)."""
+        if self.exchange == "p2p" and self._bufs is not None:
+            st = int(self.peer.status_t.item())
+            if st:
+                raise DracoError(f"expert-parallel barrier timed out on rank {self.rank} (status 0x{st:x})")
+
+    def close(self):
+        """Release the peer-memory buffers (collective over the group when it has a barrier)."""
+        if getattr(self, "peer", None) is not None:
+            self.peer.close_peers()
+            if hasattr(self.comm, "barrier"):
+                self.comm.barrier()
+            self.peer.free()
+            self.peer = None
 
     def forward(self, x, out=None):
         """MoE layer output for this rank's token rows x [T, H] (fp32).  With layout "replicated"
@@ -178,7 +306,24 @@ class ExpertParallelMoE:
             out = b["out"][:T]
         if self.layout == "replicated":
             return self._forward_replicated(x, T, b, out)
+        if self.exchange == "p2p":
+            return self._forward_p2p(x, T, b, out)
         return self._forward_a2a(x, T, b, out)
+
+    def _forward_p2p(self, x, T, b, out):
+        o, G, K, H, E, B, pb = self.ops, self.G, self.K, self.H, self.E, self.B, self.peer
+        o.route(x, T, b["order"], b["wtop"])
+        o.plan(b["order"], T, K, E, G, B, b["counts"], b["row_of"], b["src_tok"])
+        sh = None
+        if o.has_shared:
+            sh = b["sh"][:T]
+            o.shared(x, T, sh)
+        o.push(x, b["order"], b["wtop"], b["counts"], G, self.rank, b["src_tok"], B, K, H, pb)
+        o.barrier(G, self.rank, pb)                 # every rank's rows have landed
+        o.experts_meta(pb.x, G * B, pb.meta, K, pb.partial)
+        o.barrier(G, self.rank, pb)                 # every owner's partial rows are final
+        o.pull_combine(b["row_of"], T, G, self.rank, B, H, sh, out, pb)
+        return out
 
     def _forward_replicated(self, x, T, b, out):
         o = self.ops
@@ -222,6 +367,40 @@ class ExpertParallelMoE:
         return out
 
 
+def emulate_p2p(ranks: list, xs: list) -> list:
+    """The peer-memory exchange of G ranks that share one GPU in one process: the ranks' buffers
+    are linked directly, and the steps run rank after rank in one stream, which orders them the
+    way the barriers do across GPUs (no barrier kernel runs: ranks on one GPU must not wait on
+    one another in separate launches)."""
+    G = len(ranks)
+    assert all(r.G == G and r.exchange == "p2p" for r in ranks)
+    for r in ranks:
+        if r._bufs is None:
+            r._alloc()
+    ptrs = [dict(r.peer.own) for r in ranks]
+    for r in ranks:
+        r.peer.link(ptrs)
+    sts = []
+    for r, x in zip(ranks, xs):
+        o, b, T = r.ops, r._bufs, int(x.shape[0])
+        o.route(x, T, b["order"], b["wtop"])
+        o.plan(b["order"], T, r.K, r.E, G, r.B, b["counts"], b["row_of"], b["src_tok"])
+        sh = None
+        if o.has_shared:
+            sh = b["sh"][:T]
+            o.shared(x, T, sh)
+        o.push(x, b["order"], b["wtop"], b["counts"], G, r.rank, b["src_tok"], r.B, r.K, r.H, r.peer)
+        sts.append((T, sh))
+    for r in ranks:
+        r.ops.experts_meta(r.peer.x, G * r.B, r.peer.meta, r.K, r.peer.partial)
+    outs = []
+    for r, (T, sh) in zip(ranks, sts):
+        out = r._bufs["out"][:T]
+        r.ops.pull_combine(r._bufs["row_of"], T, G, r.rank, r.B, r.H, sh, out, r.peer)
+        outs.append(out)
+    return outs
+
+
 def emulate(ranks: list, xs: list) -> list:
     """Run the a2a layout of several ExpertParallelMoE ranks that live in one process (one GPU or
     CPU) with the exchanges done by copies: the data path of G ranks without G devices.  The
@@ -229,6 +408,8 @@ def emulate(ranks: list, xs: list) -> list:
     import torch
     G = len(ranks)
     assert all(r.G == G and r.layout == "a2a" for r in ranks)
+    if ranks[0].exchange == "p2p":
+        return emulate_p2p(ranks, xs)
     st = []
     for r, x in zip(ranks, xs):
         o, b = r.ops, r._bufs or r._alloc()
@@ -274,4 +455,5 @@ def emulate(ranks: list, xs: list) -> list:
     return outs
 
 
-__all__ = ["ExpertParallelMoE", "DeviceOps", "TorchGroup", "emulate", "slice_desc", "DracoError"]
+__all__ = ["ExpertParallelMoE", "DeviceOps", "PeerBuffers", "TorchGroup", "emulate", "emulate_p2p", "slice_desc",
+           "tensor_at", "DracoError"]

@@ -184,6 +184,31 @@ int draco_b200_ep_pack(const float* X, const int* order, const float* wtop, cons
 int draco_b200_ep_combine(const float* back, const int* row_of, int T, int n_ranks, int H,
                           const float* shared, float* out, void* stream);
 
+/* Peer-memory exchange (one process per GPU of one node; replaces the all-to-alls).
+ *  ep_mem_alloc: zeroed device buffer plus its CUDA IPC handle (64 bytes) for the other ranks;
+ *    ep_mem_open/close map/unmap a peer's buffer from its handle; ep_mem_free releases.
+ *  ep_push: the dispatch of ep_pack with block > 0, written straight into the owners' receive
+ *    buffers: row j of the block for rank d lands at row rank*block + j of dst_x[d] (H floats)
+ *    and dst_meta[d] (2K ints); unused rows of the block get ids -1.  dst_x/dst_meta are device
+ *    arrays of n_ranks pointers (this rank's own buffers at index rank).
+ *  ep_barrier: every rank sets its word in each peer's flag array (peer_flags: device array of
+ *    n_ranks pointers to the ranks' flag arrays of n_ranks words) to the next epoch (*epoch, a
+ *    device counter) and waits until its own array my_flags holds that epoch from all ranks.
+ *    The wait is bounded (2 s), after which 0x400 is set in *status and the kernel returns.
+ *  ep_pull_combine: ep_combine reading the owners' partial rows in place: out[t] = sum over r
+ *    ascending of src_partial[r][rank*block + row_of[t][r] - r*block] (+ shared[t]). */
+int draco_b200_ep_mem_alloc(size_t bytes, void** ptr, void* handle);
+int draco_b200_ep_mem_open(const void* handle, void** ptr);
+int draco_b200_ep_mem_close(void* ptr);
+int draco_b200_ep_mem_free(void* ptr);
+int draco_b200_ep_push(const float* X, const int* order, const float* wtop, const int* counts, int n_ranks,
+                       int rank, const int* src_tok, int block, int K, int H, float* const* dst_x,
+                       int* const* dst_meta, void* stream);
+int draco_b200_ep_barrier(unsigned* const* peer_flags, unsigned* my_flags, unsigned* epoch, int n_ranks,
+                          int rank, int* status, void* stream);
+int draco_b200_ep_pull_combine(const float* const* src_partial, const int* row_of, int T, int n_ranks,
+                               int rank, int block, int H, const float* shared, float* out, void* stream);
+
 /* Allocation-free m6_moe_tok, for callers that cannot let a library allocate device memory
  * (an engine that reserves HBM for weights and KV cache up front and forbids allocations
  * outside its pool; a decode loop that cannot take cudaMalloc's implicit synchronisation).

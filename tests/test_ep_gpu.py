@@ -12,7 +12,7 @@ import torch
 
 import dracomancer_llmengine_b200 as dm
 from dracomancer_llmengine_b200 import synth
-from dracomancer_llmengine_b200.ep import DeviceOps, ExpertParallelMoE, emulate, slice_desc
+from dracomancer_llmengine_b200.ep import DeviceOps, ExpertParallelMoE, PeerBuffers, emulate, slice_desc
 from ep_host_ops import plan_ref
 
 pytestmark = pytest.mark.gpu
@@ -161,6 +161,59 @@ def test_ep_emulated_on_one_gpu(port, name, G, exchange, T):
     assert rel(got, single) < 2 * REL_L2_TOL
 
 
+@pytest.mark.parametrize("name", list(LAYERS))
+@pytest.mark.parametrize("G,T", [(2, 40), (4, 150), (8, 96)])
+def test_ep_p2p_emulated_matches_fixed_exchange(port, name, G, T):
+    """Peer-memory dispatch/combine (push and pull kernels) on G ranks sharing one GPU: the same
+    rows reach the owners as with the fixed-block all-to-all, so the outputs are identical."""
+    layer = synth.make_layer(**LAYERS[name])
+    Ts = [T - (i % 3) for i in range(G)]
+    xs = [torch.from_numpy(synth.make_tokens(layer, t, 400 + i, False)).cuda() for i, t in enumerate(Ts)]
+    dev = torch.device("cuda")
+    res = {}
+    for exchange in ("fixed", "p2p"):
+        ranks = [ExpertParallelMoE(layer, max(Ts), comm=types.SimpleNamespace(world=G, rank=r),
+                                   ops=DeviceOps(layer, r, G, dev), exchange=exchange) for r in range(G)]
+        outs = emulate(ranks, xs)
+        torch.cuda.synchronize()
+        res[exchange] = np.concatenate([o.cpu().numpy() for o in outs])
+        for r in ranks:
+            r.close()
+    assert np.array_equal(res["p2p"].view(np.uint32), res["fixed"].view(np.uint32))
+    X = np.concatenate([x.cpu().numpy() for x in xs])
+    assert rel(res["p2p"], port.layer_forward(layer, X)) < REL_L2_TOL
+
+
+def test_ep_barrier_one_rank_and_bounded_wait(dlib):
+    """The flag barrier: alone it passes at once and counts epochs; with a second rank that never
+    arrives (a flag nothing sets) it gives up after its time limit, reports 0x400 and the device
+    stays usable."""
+    import time
+    dev = torch.device("cuda")
+    pb = PeerBuffers(1, 0, 1, 4, 1, dev)
+    pb.link([dict(pb.own)])
+    s = torch.cuda.current_stream().cuda_stream
+    for _ in range(3):
+        assert dlib.draco_b200_ep_barrier(pb.peer_flags.data_ptr(), pb.my_flags, pb.epoch, 1, 0, pb.status, s) == 0
+    torch.cuda.synchronize()
+    from dracomancer_llmengine_b200.ep import tensor_at
+    ctl = tensor_at(pb.own["ctl"], (64,), torch.int32, dev).cpu().numpy()
+    assert ctl[0] == 3 and ctl[16] == 3 and ctl[32] == 0      # flag, epoch, status
+    # two ranks, the second absent
+    other = PeerBuffers(1, 0, 1, 4, 1, dev)
+    pb2 = PeerBuffers(2, 0, 1, 4, 1, dev)
+    pb2.link([dict(pb2.own), dict(other.own)])
+    t0 = time.time()
+    assert dlib.draco_b200_ep_barrier(pb2.peer_flags.data_ptr(), pb2.my_flags, pb2.epoch, 2, 0, pb2.status, s) == 0
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    assert int(pb2.status_t.item()) == 0x400
+    assert 1.0 < waited < 30.0
+    assert torch.ones(4, device=dev).sum().item() == 4.0
+    for b in (pb, other, pb2):
+        b.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -183,11 +236,13 @@ def _nccl_worker(rank, world, port_no, name, out_dir):
         res = {}
         stream = torch.cuda.Stream(dev)
         with torch.cuda.stream(stream):
-            for exchange in ("fixed", "compact"):
+            for exchange in ("fixed", "compact", "p2p"):
                 ep = ExpertParallelMoE(layer, max(Ts), exchange=exchange, device=dev)
                 x = torch.from_numpy(xs[rank]).to(dev)
                 res[exchange] = ep.forward(x).cpu().numpy()
                 res[exchange + "_again"] = ep.forward(x).cpu().numpy()
+                ep.check()
+                ep.close()
             allx = torch.from_numpy(np.concatenate(xs)).to(dev)
             rep = ExpertParallelMoE(layer, allx.shape[0], layout="replicated", device=dev)
             res["replicated"] = rep.forward(allx).cpu().numpy()
@@ -210,12 +265,13 @@ def test_ep_nccl(port, tmp_path, name):
     X = np.concatenate(xs)
     ref = port.layer_forward(layer, X)
     r = [np.load(os.path.join(tmp_path, f"rank{i}.npz")) for i in range(world)]
-    for exchange in ("fixed", "compact"):
+    for exchange in ("fixed", "compact", "p2p"):
         got = np.concatenate([r[i][exchange] for i in range(world)])
         assert rel(got, ref) < REL_L2_TOL, exchange
         again = np.concatenate([r[i][exchange + "_again"] for i in range(world)])
         assert np.array_equal(got, again)
     for i in range(world):
         assert np.array_equal(r[i]["fixed"], r[i]["compact"])
+        assert np.array_equal(r[i]["fixed"], r[i]["p2p"])
         assert np.array_equal(r[i]["replicated"], r[0]["replicated"])
     assert rel(r[0]["replicated"], ref) < REL_L2_TOL
