@@ -431,6 +431,78 @@ __global__ void combine_kernel(const float* __restrict__ y, const int* __restric
     }
 }
 
+// The same sums for n_out % 4 == 0, one block per token row: warp 0 stages the row's valid
+// (weight, y row) pairs in k order in shared memory, then every thread runs the identical fma
+// chain over float4 columns with the y loads of four assignments issued ahead of their fmas.
+constexpr int kCombineMaxK = 64;
+constexpr int kCombineThreads = 128;
+__device__ __forceinline__ void fma4(float4& a, float w, const float4& v) {
+    a.x = fmaf(w, v.x, a.x);
+    a.y = fmaf(w, v.y, a.y);
+    a.z = fmaf(w, v.z, a.z);
+    a.w = fmaf(w, v.w, a.w);
+}
+__global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(
+    const float* __restrict__ y, const int* __restrict__ order, const float* __restrict__ wtop,
+    const int* __restrict__ pos_of, int K, int E, int n_out, const float* __restrict__ shared,
+    float* __restrict__ out) {
+    __shared__ float sw[kCombineMaxK];
+    __shared__ const float4* sy[kCombineMaxK];
+    __shared__ int sn;
+    const int t = blockIdx.x;
+    const int n4 = n_out / 4;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        int base = 0;
+        for (int k0 = 0; k0 < K; k0 += 32) {
+            const int k = k0 + lane;
+            bool v = false;
+            int p = 0;
+            float w = 0.f;
+            if (k < K) {
+                const int e = order[(size_t)t * K + k];
+                v = e >= 0 && e < E;
+                if (v) {
+                    p = pos_of[(size_t)t * K + k];
+                    w = wtop[(size_t)t * K + k];
+                }
+            }
+            const unsigned m = __ballot_sync(0xffffffffu, v);
+            if (v) {
+                const int j = base + __popc(m & ((1u << lane) - 1u));
+                sw[j] = w;
+                sy[j] = reinterpret_cast<const float4*>(y + (size_t)p * n_out);
+            }
+            base += __popc(m);
+        }
+        if (lane == 0) sn = base;
+    }
+    __syncthreads();
+    const int n = sn;
+    const float4* sh = shared ? reinterpret_cast<const float4*>(shared + (size_t)t * n_out) : nullptr;
+    float4* o = reinterpret_cast<float4*>(out + (size_t)t * n_out);
+    for (int c = threadIdx.x; c < n4; c += kCombineThreads) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        int j = 0;
+        for (; j + 4 <= n; j += 4) {
+            const float4 v0 = sy[j][c], v1 = sy[j + 1][c], v2 = sy[j + 2][c], v3 = sy[j + 3][c];
+            fma4(acc, sw[j], v0);
+            fma4(acc, sw[j + 1], v1);
+            fma4(acc, sw[j + 2], v2);
+            fma4(acc, sw[j + 3], v3);
+        }
+        for (; j < n; j++) fma4(acc, sw[j], sy[j][c]);
+        if (sh) {
+            const float4 v = sh[c];
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        o[c] = acc;
+    }
+}
+
 __global__ void set_pair_kernel(int* d, int a, int b) {
     d[0] = a;
     d[1] = b;
@@ -439,6 +511,12 @@ void launch_set_pair(int* d, int a, int b, cudaStream_t s) { set_pair_kernel<<<1
 
 void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T, int K, int E,
                     int n_out, const float* shared, float* out, cudaStream_t s) {
+    const bool vec = n_out % 4 == 0 && K <= kCombineMaxK && !((uintptr_t)y & 15) && !((uintptr_t)out & 15) &&
+                     !((uintptr_t)shared & 15);
+    if (vec) {
+        if (T > 0) combine_rows_kernel<<<T, kCombineThreads, 0, s>>>(y, order, wtop, pos_of, K, E, n_out, shared, out);
+        return;
+    }
     dim3 grid((n_out + 255) / 256, T);
     combine_kernel<<<grid, 256, 0, s>>>(y, order, wtop, pos_of, T, K, E, n_out, shared, out);
 }
