@@ -181,13 +181,134 @@ __global__ void __launch_bounds__(rl::NTH) router_logits_v2(const float* __restr
     }
 }
 
+// Register-tiled variant: a block of NW warps shares one tile of TE = 32*EPL experts; warp w owns
+// TPW token rows (read as warp-wide broadcasts of 4 consecutive k) and lane l the experts
+// l + 32 j (rows 68 floats apart, so one 128-bit read per expert is conflict-free).  Per 4 k a
+// lane reads TPW + EPL float4 and updates TPW*EPL chains, each still one rounded product and
+// one rounded add per k in ascending order.  k-chunks of 64 stream into an NS-stage cp.async
+// ring.  Needs H % 4 == 0 and 16-byte aligned X and W.
+namespace rt {
+constexpr int KC = 64, LD = KC + 4;
+template <int TPW, int EPL, int NW, int NS>
+constexpr int smem_bytes() {
+    return NS * (TPW * NW + 32 * EPL) * LD * 4;
+}
+}  // namespace rt
+template <int TPW, int EPL, int NW, int NS>
+__global__ void __launch_bounds__(32 * NW) router_tile_kernel(const float* __restrict__ X, const float* __restrict__ W,
+                                                              int T, int E, int H, float* __restrict__ logits,
+                                                              int* __restrict__ zero_err) {
+    using namespace rt;
+    constexpr int TT = TPW * NW, TE = 32 * EPL, NTH = 32 * NW, ROWS = TT + TE, NV = ROWS * (KC / 4);
+    extern __shared__ __align__(16) float rt_smem[];
+    if (zero_err && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *zero_err = 0;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE;
+    const int nc = (H + KC - 1) / KC;
+    auto issue = [&](int c) {
+        if (c < nc) {
+            float* st = rt_smem + (c % NS) * ROWS * LD;
+            const int k0 = c * KC;
+            for (int i = tid; i < NV; i += NTH) {
+                const int rr = i / (KC / 4), k4 = (i % (KC / 4)) * 4;
+                const bool is_x = rr < TT;
+                const int row = is_x ? t0 + rr : e0 + rr - TT;
+                const bool in = (is_x ? row < T : row < E) && k0 + k4 < H;
+                const float* src = in ? (is_x ? X : W) + (size_t)row * H + k0 + k4 : X;
+                cp_async16(st + rr * LD + k4, src, in ? 16 : 0);   // zero-fill outside
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+#pragma unroll
+    for (int c = 0; c < NS - 1; c++) issue(c);
+    float acc[TPW][EPL];
+#pragma unroll
+    for (int i = 0; i < TPW; i++)
+#pragma unroll
+        for (int j = 0; j < EPL; j++) acc[i][j] = 0.f;
+    auto step = [&](const float4 (&xv)[TPW], const float4 (&wv)[EPL]) {
+#pragma unroll
+        for (int i = 0; i < TPW; i++)
+#pragma unroll
+            for (int j = 0; j < EPL; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(xv[i].x, wv[j].x));
+#pragma unroll
+        for (int i = 0; i < TPW; i++)
+#pragma unroll
+            for (int j = 0; j < EPL; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(xv[i].y, wv[j].y));
+#pragma unroll
+        for (int i = 0; i < TPW; i++)
+#pragma unroll
+            for (int j = 0; j < EPL; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(xv[i].z, wv[j].z));
+#pragma unroll
+        for (int i = 0; i < TPW; i++)
+#pragma unroll
+            for (int j = 0; j < EPL; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(xv[i].w, wv[j].w));
+    };
+    for (int c = 0; c < nc; c++) {
+        issue(c + NS - 1);
+        asm volatile("cp.async.wait_group %0;" ::"n"(NS - 1) : "memory");
+        __syncthreads();
+        const float* st = rt_smem + (c % NS) * ROWS * LD;
+        const float4* xr = reinterpret_cast<const float4*>(st + warp * TPW * LD);
+        const float4* wr = reinterpret_cast<const float4*>(st + (TT + lane) * LD);
+        const int kq = min(KC, H - c * KC) / 4;   // H is a multiple of 4
+        auto load = [&](int q, float4 (&xv)[TPW], float4 (&wv)[EPL]) {
+#pragma unroll
+            for (int j = 0; j < EPL; j++) wv[j] = wr[j * 32 * (LD / 4) + q];
+#pragma unroll
+            for (int i = 0; i < TPW; i++) xv[i] = xr[i * (LD / 4) + q];
+        };
+        if (kq == KC / 4) {
+            float4 xa[TPW], wa[EPL], xb[TPW], wb[EPL];
+            load(0, xa, wa);
+#pragma unroll
+            for (int q = 0; q < KC / 4; q += 2) {
+                load(q + 1, xb, wb);
+                step(xa, wa);
+                if (q + 2 < KC / 4) load(q + 2, xa, wa);
+                step(xb, wb);
+            }
+        } else {
+            for (int q = 0; q < kq; q++) {
+                float4 xa[TPW], wa[EPL];
+                load(q, xa, wa);
+                step(xa, wa);
+            }
+        }
+        __syncthreads();   // stage c % NS is refilled by the next iteration's issue(c + NS)
+    }
+#pragma unroll
+    for (int i = 0; i < TPW; i++) {
+        const int t = t0 + warp * TPW + i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < EPL; j++) {
+            const int e = e0 + lane + 32 * j;
+            if (e < E) logits[(size_t)t * E + e] = acc[i][j];
+        }
+    }
+}
+
+template <int TPW, int EPL, int NW, int NS>
+static void launch_router_tile(const float* X, const float* W, int T, int E, int H, float* logits, cudaStream_t s,
+                               int* zero_err) {
+    constexpr int sm = rt::smem_bytes<TPW, EPL, NW, NS>();
+    cudaFuncSetAttribute(router_tile_kernel<TPW, EPL, NW, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    dim3 grid((T + TPW * NW - 1) / (TPW * NW), (E + 32 * EPL - 1) / (32 * EPL));
+    router_tile_kernel<TPW, EPL, NW, NS><<<grid, 32 * NW, sm, s>>>(X, W, T, E, H, logits, zero_err);
+}
+
+static int router_tiles(int T, int E, int tt, int te) { return ((T + tt - 1) / tt) * ((E + te - 1) / te); }
+
 void launch_router_logits(const float* X, const float* W, int T, int E, int H, float* logits,
                           cudaStream_t s, int* zero_err) {
     const bool vec_ok = H % 4 == 0 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0;
-    if (!vec_ok) {
-        dim3 grid((E + 31) / 32, (T + 3) / 4);
-        router_logits_kernel<4, 1><<<grid, dim3(32, 4), 0, s>>>(X, W, T, E, H, logits, zero_err);
-    } else {
+    if (vec_ok) {
+        if (router_tiles(T, E, 64, 64) >= 148) {   // enough 64 x 64 tiles for every SM: 16 chains a lane
+            launch_router_tile<8, 2, 8, 3>(X, W, T, E, H, logits, s, zero_err);
+            return;
+        }
         dim3 grid((T + 7) / 8, (E + 31) / 32);
         if (T <= 16) {
             constexpr int sm = rl::smem_bytes<8>();
@@ -198,7 +319,10 @@ void launch_router_logits(const float* X, const float* W, int T, int E, int H, f
             cudaFuncSetAttribute(router_logits_v2<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
             router_logits_v2<3><<<grid, rl::NTH, sm, s>>>(X, W, T, E, H, logits, zero_err);
         }
+        return;
     }
+    dim3 grid((E + 31) / 32, (T + 3) / 4);
+    router_logits_kernel<4, 1><<<grid, dim3(32, 4), 0, s>>>(X, W, T, E, H, logits, zero_err);
 }
 
 // ------------------------------------------------------------------------------------------
