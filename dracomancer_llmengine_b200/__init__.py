@@ -115,6 +115,7 @@ _SIGS = {
     "draco_b200_reset": ([], None),
     "draco_b200_registered_bytes": ([], ct.c_size_t),
     "draco_b200_expf": ([_f, _f, ct.c_long], ct.c_int),
+    "draco_b200_router_logits": ([_f, _f, ct.c_int, ct.c_int, ct.c_int, _f], ct.c_int),
     "draco_b200_q8k_quantize": ([_f, ct.c_int, _f, _i8, _i16], ct.c_int),
     "draco_b200_q8k_block_dots": ([ct.c_int, _u8, ct.c_int, ct.c_int, _i8, _i16, _i32], ct.c_int),
     "draco_b200_gemv_q8k": ([ct.c_int, _u8, ct.c_int, ct.c_int, _i8, _f, _i16, _f], ct.c_int),

@@ -1577,6 +1577,7 @@ int draco_b200_route(const DracoMoeLayer* L, const float* X, int T, int* order, 
     CK(cudaMemsetAsync(b.err, 0, sizeof(int), s));
     launch_router_logits(dx, d_gi, T, L->n_exp, L->n_in, b.logits, s);
     launch_router_select(rp, T, b, s);
+    g_launches += 2;
     CK(cudaGetLastError());
     const cudaMemcpyKind k = dev_io ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
     CK(cudaMemcpyAsync(order, b.order, sizeof(int) * n, k, s));
@@ -1846,6 +1847,25 @@ int draco_b200_expf(const float* x, float* y, long n) {
     launch_expf((const float*)(c->ws + o_x), (float*)(c->ws + o_y), n, s);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(y, c->ws + o_y, sizeof(float) * n, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int draco_b200_router_logits(const float* X, const float* W, int T, int E, int H, float* logits) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (T <= 0 || E <= 0 || H <= 0) return -1;
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    Carver cv;
+    const size_t o_x = cv.take<float>((size_t)T * H), o_w = cv.take<float>((size_t)E * H);
+    const size_t o_l = cv.take<float>((size_t)T * E);
+    if (int rc = ensure_ws(c, cv.off)) return rc;
+    cudaStream_t s = c->stream;
+    if (int rc = stage_in(c, s, o_x, X, (size_t)T * H)) return rc;
+    if (int rc = stage_in(c, s, o_w, W, (size_t)E * H)) return rc;
+    launch_router_logits((const float*)(c->ws + o_x), (const float*)(c->ws + o_w), T, E, H, (float*)(c->ws + o_l), s);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(logits, c->ws + o_l, sizeof(float) * T * E, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
     return 0;
 }

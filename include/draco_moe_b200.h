@@ -254,6 +254,8 @@ size_t draco_b200_registered_bytes(void);
 
 /* Test hooks (device arrays or host arrays, synchronous). */
 int draco_b200_expf(const float* x, float* y, long n);
+/* logits[t][e] = sum over k ascending of rounded x[t][k]*W[e][k] (router logits alone) */
+int draco_b200_router_logits(const float* X, const float* W, int T, int E, int H, float* logits);
 int draco_b200_q8k_quantize(const float* x, int n, float* d, int8_t* q, int16_t* bsums);
 int draco_b200_q8k_block_dots(int code, const uint8_t* W, int rows, int n_in, const int8_t* q,
                               const int16_t* bsums, int32_t* out2);

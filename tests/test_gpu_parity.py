@@ -72,6 +72,45 @@ def test_router_bitexact(dlib, port, name):
     assert np.array_equal(bits(w_gpu), bits(w_ref)), "gate weights differ in bits"
 
 
+def logits_ref(X, W):
+    """Sequential float32 sums of rounded products, k ascending (the reference's C order)."""
+    X = np.asarray(X, np.float32)
+    W = np.asarray(W, np.float32)
+    acc = np.zeros((X.shape[0], W.shape[0]), np.float32)
+    for k in range(X.shape[1]):
+        acc = acc + np.multiply.outer(X[:, k], W[:, k])   # float32 product rounded, then float32 add
+    return acc
+
+
+# shapes reaching every logits kernel: the small-batch tiles (deep and shallow rings, partial last
+# chunk), the register-tiled kernel for many tiles, the scalar fallback (width % 4 != 0)
+@pytest.mark.parametrize("T,E,H", [(5, 128, 2048), (48, 384, 1024), (300, 128, 512), (600, 128, 2048),
+                                   (2400, 256, 256), (2400, 256, 260), (40, 64, 258)])
+def test_router_logits_exact_order(dlib, T, E, H):
+    rng = np.random.default_rng(T + E + H)
+    X = rng.standard_normal((T, H), dtype=np.float32)
+    W = (rng.standard_normal((E, H), dtype=np.float32) * 0.02).astype(np.float32)
+    got = np.empty((T, E), np.float32)
+    assert dlib.draco_b200_router_logits(X.ctypes.data_as(dm._f), W.ctypes.data_as(dm._f), T, E, H,
+                                         got.ctypes.data_as(dm._f)) == 0, dm.last_error()
+    ref = logits_ref(X, W)
+    bad = np.nonzero(bits(got) != bits(ref))
+    assert bad[0].size == 0, f"{bad[0].size} logits differ, first (t, e) {list(zip(bad[0][:4], bad[1][:4]))}"
+
+
+@pytest.mark.parametrize("name,T", [("softmax_e128", 600), ("sigmoid_groups_e256", 2400), ("sigmoid_k2_e384", 200)])
+def test_router_bitexact_large_batches(dlib, port, name, T):
+    """Token batches large enough for the register-tiled logits kernel."""
+    c = dict(ROUTER_CASES[name])
+    zipf = c.pop("zipf", False)
+    layer = synth.make_layer(zipf=zipf, weights=False, **c)
+    X = synth.make_tokens(layer, T, c["seed"] + 1, zipf=zipf)
+    o_gpu, w_gpu = dm.route(layer, X)
+    o_ref, w_ref = port.route(layer, X)
+    assert np.array_equal(o_gpu, o_ref), f"index mismatch rows {np.nonzero((o_gpu != o_ref).any(1))[0][:8]}"
+    assert np.array_equal(bits(w_gpu), bits(w_ref)), "gate weights differ in bits"
+
+
 def test_router_ties_lower_index(dlib, port):
     layer = synth.make_layer(hidden=256, n_exp=32, n_used=8, inter=256, seed=27)
     # duplicate router rows: experts 2k and 2k+1 score identically -> ties everywhere
