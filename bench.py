@@ -260,11 +260,13 @@ def main():
     import dracomancer_llmengine_b200 as dm
     L = dm.lib()
 
-    layer, Xh = synth.make_config(args.config)
+    # expert parallel: each rank generates (and uploads) only its own slice of the experts
+    experts = (rank * (cfgd["n_exp"] // world), cfgd["n_exp"] // world) if world > 1 else None
+    layer, Xh = synth.make_config(args.config, experts=experts)
     if rank:
         Xh = synth.make_tokens(layer, T, cfgd["seed"] + 1000 * rank, cfgd["zipf"])
     keep: list = []
-    desc = dm.layer_desc(layer, keep)
+    desc = dm.layer_desc(layer, keep) if world == 1 else None
     dev = torch.device("cuda", local)
     X = torch.from_numpy(Xh).to(dev)
     out = torch.empty((T, layer.hidden), device=dev, dtype=torch.float32)

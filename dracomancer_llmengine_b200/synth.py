@@ -96,16 +96,17 @@ def quant_matrix(rng: np.random.Generator, code: int, n_mat: int, n_out: int, n_
     return blocks.reshape(n_mat, n_out * nb * BLOCK_BYTES[code])
 
 
-def expert_matrices(seed, code: int, n_mat: int, n_out: int, n_in: int) -> np.ndarray:
+def expert_matrices(seed, code: int, n_mat: int, n_out: int, n_in: int, first: int = 0) -> np.ndarray:
     """Like quant_matrix, with matrix e drawn from its own stream default_rng([*seed, e]), so the
-    experts are generated in parallel (threads; numpy releases the GIL) and still reproducibly."""
+    experts are generated in parallel (threads; numpy releases the GIL) and still reproducibly;
+    `first` > 0 generates matrices first .. first + n_mat - 1 of the same sequence."""
     import concurrent.futures
     nb = n_in // BLOCK_VALUES[code]
     per = n_out * nb * BLOCK_BYTES[code]
     out = np.empty((n_mat, per), np.uint8)
 
     def one(e):
-        out[e] = _GEN[code](np.random.default_rng([*seed, e]), n_out * nb).reshape(per)
+        out[e] = _GEN[code](np.random.default_rng([*seed, first + e]), n_out * nb).reshape(per)
 
     with concurrent.futures.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as ex:
         list(ex.map(one, range(n_mat)))
@@ -142,9 +143,12 @@ class MoELayer:
     sh_up: np.ndarray | None = None
     sh_down: np.ndarray | None = None
     sh_gate_inp: np.ndarray | None = None  # fp32 [hidden] scalar-gated shared expert, or None
+    expert0: int = 0            # gate/up/down hold experts expert0 .. expert0 + len - 1 (an
+                                # expert-parallel rank's slice); all n_exp when 0 and full
 
     def ptr_table(self):
-        """(ep uint64[3E], ec int32[3E]) host pointer table as the reference drivers build it."""
+        """(ep uint64[3E], ec int32[3E]) host pointer table as the reference drivers build it;
+        entries of experts this layer object does not hold are 0."""
         E = self.n_exp
         ep = np.zeros(3 * E, np.uint64)
         ec = np.zeros(3 * E, np.int32)
@@ -152,7 +156,8 @@ class MoELayer:
                                            (self.down, self.code_d))):
             base = buf.ctypes.data
             per = buf.shape[1]
-            ep[idx::3] = base + per * np.arange(E, dtype=np.uint64)
+            n = buf.shape[0]
+            ep[3 * self.expert0 + idx:3 * (self.expert0 + n):3] = base + per * np.arange(n, dtype=np.uint64)
             ec[idx::3] = code
         return ep, ec
 
@@ -185,13 +190,16 @@ def make_layer(hidden: int, n_exp: int, n_used: int, inter: int, scoring: str = 
                n_group: int = 1, n_group_used: int = 1, w_scale: float = 0.0,
                shared_inter: int = 0, bias: bool = False, zipf: bool = False, seed: int = 0,
                code_gu: int = CODE_Q4_K, code_d: int = CODE_Q6_K, weights: bool = True,
-               **_unused) -> MoELayer:
+               experts: tuple | None = None, **_unused) -> MoELayer:
     """Expert weights, router and shared expert come from independent seeded streams, so
-    `weights=False` (router only, empty expert tensors) routes exactly like the full layer."""
+    `weights=False` (router only, empty expert tensors) routes exactly like the full layer, and
+    `experts=(first, count)` (one expert-parallel rank's slice) holds exactly those experts of
+    the full layer."""
+    first, count = experts if experts else (0, n_exp)
     if weights:
-        gate = expert_matrices((seed, 0, 0), code_gu, n_exp, inter, hidden)
-        up = expert_matrices((seed, 0, 1), code_gu, n_exp, inter, hidden)
-        down = expert_matrices((seed, 0, 2), code_d, n_exp, hidden, inter)
+        gate = expert_matrices((seed, 0, 0), code_gu, count, inter, hidden, first)
+        up = expert_matrices((seed, 0, 1), code_gu, count, inter, hidden, first)
+        down = expert_matrices((seed, 0, 2), code_d, count, hidden, inter, first)
     else:
         gate = up = down = np.zeros((n_exp, 0), np.uint8)
     rng = np.random.default_rng([seed, 1])
@@ -208,7 +216,7 @@ def make_layer(hidden: int, n_exp: int, n_used: int, inter: int, scoring: str = 
     layer = MoELayer(n_exp=n_exp, n_used=n_used, inter=inter, hidden=hidden, gate=gate, up=up,
                      down=down, gate_inp=gi, code_gu=code_gu, code_d=code_d, scoring=scoring,
                      probs_b=probs_b, n_group=n_group, n_group_used=n_group_used, norm_w=1,
-                     w_scale=w_scale)
+                     w_scale=w_scale, expert0=first if weights else 0)
     if shared_inter and weights:
         rng = np.random.default_rng([seed, 2])
         layer.shared_inter = shared_inter
@@ -227,9 +235,10 @@ def make_tokens(layer: MoELayer, tokens: int, seed: int, zipf: bool = False) -> 
     return x
 
 
-def make_config(name: str, tokens: int | None = None, weights: bool = True):
-    """(layer, X) for a named configuration; `tokens` overrides the token count."""
+def make_config(name: str, tokens: int | None = None, weights: bool = True, experts: tuple | None = None):
+    """(layer, X) for a named configuration; `tokens` overrides the token count, `experts` =
+    (first, count) generates only that slice of the expert weights."""
     c = dict(CONFIGS[name])
-    layer = make_layer(weights=weights, **c)
+    layer = make_layer(weights=weights, experts=experts, **c)
     x = make_tokens(layer, c["tokens"] if tokens is None else tokens, c["seed"], c["zipf"])
     return layer, x
