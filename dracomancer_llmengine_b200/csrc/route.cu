@@ -550,11 +550,12 @@ void launch_router_select(const RouterParams& p, int T, RouteBufs& b, cudaStream
 }
 
 // ------------------------------------------------------------------------------------------
-// Dispatch: stable counting sort of assignments i = t*K + k by expert (the order of
+// Dispatch: counting sort of assignments i = t*K + k by expert (the grouping of
 // src/m6_moe_tok.c:53-70), in three passes over chunks of 1024 assignments: per-chunk expert
-// counts; per-expert prefix over chunks plus expert offsets; placement, where a chunk's warps
-// take turns and each ranks its lanes among equal experts with a match mask, so every
-// expert's list is in increasing i.
+// counts; per-expert prefix over chunks plus expert offsets; placement by warp-aggregated
+// shared-memory atomics.  Chunks keep increasing i from one to the next; inside a chunk the
+// slot order of one expert's assignments follows the atomics, which no result depends on
+// (every later step works per slot and each output row reads its own slots).
 // ------------------------------------------------------------------------------------------
 constexpr int kChunk = 1024;
 
@@ -582,12 +583,24 @@ __global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restr
     const int e = threadIdx.x;
     // per expert: exclusive prefix over chunks (in place), total
     int c = 0;
-    if (e < E)
-        for (int k = 0; k < n_chunks; k++) {
+    if (e < E) {   // eight independent loads in flight, then the in-place exclusive prefix
+        int k = 0;
+        for (; k + 8 <= n_chunks; k += 8) {
+            int v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = chunk_counts[(size_t)(k + u) * E + e];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                chunk_counts[(size_t)(k + u) * E + e] = c;
+                c += v[u];
+            }
+        }
+        for (; k < n_chunks; k++) {
             const int v = chunk_counts[(size_t)k * E + e];
             chunk_counts[(size_t)k * E + e] = c;
             c += v;
         }
+    }
     if (e < E) counts[e] = c;
     const int tiles = (c + il.nt - 1) / il.nt;
     sv[e] = c;
@@ -608,8 +621,8 @@ __global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restr
     if (e < E) {
         off[e + 1] = sv[e];
         if (c > 0) active[sa[e] - 1] = e;
-        for (int k = 0; k < n_chunks; k++) chunk_counts[(size_t)k * E + e] += base;
     }
+    (void)base;   // the place kernel adds off[e] to the per-chunk prefix
     if (e == 0) {
         off[0] = 0;
         *n_active = sa[kMaxExperts - 1];
@@ -642,28 +655,30 @@ __global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restr
     }
 }
 
+// Placement: a chunk's assignments of expert e take the slots off[e] + (the expert's count in
+// earlier chunks) + (a per-chunk shared-memory counter).  Within a chunk the slot order follows
+// the atomics, not i: every consumer of the sorted order works per slot (an assignment's row of
+// Xs, act and y), so which slot an assignment gets does not change any result.
 __global__ void __launch_bounds__(kChunk) dispatch_place_kernel(const int* __restrict__ order, int n, int E,
                                                                const int* __restrict__ chunk_base,
+                                                               const int* __restrict__ off,
                                                                int* __restrict__ ilist, int* __restrict__ pos_of) {
     __shared__ int cursor[kMaxExperts];
-    for (int e = threadIdx.x; e < E; e += blockDim.x) cursor[e] = chunk_base[(size_t)blockIdx.x * E + e];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cursor[e] = off[e] + chunk_base[(size_t)blockIdx.x * E + e];
     __syncthreads();
     const int i = blockIdx.x * kChunk + threadIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int e = i < n ? order[i] : -1;
     if (e >= E) e = -1;
+    const int lane = threadIdx.x & 31;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    const bool leader = rank == 0;
-    for (int w = 0; w < kChunk / 32; w++) {
-        if (warp == w && e >= 0) {
-            const int p = cursor[e] + rank;
-            ilist[p] = i;
-            pos_of[i] = p;
-        }
-        __syncwarp();
-        if (warp == w && e >= 0 && leader) cursor[e] += __popc(peers);
-        __syncthreads();
+    const int leader = __ffs(peers) - 1;
+    int base = 0;
+    if (e >= 0 && lane == leader) base = atomicAdd(&cursor[e], __popc(peers));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (e >= 0) {
+        const int p = base + __popc(peers & ((1u << lane) - 1u));
+        ilist[p] = i;
+        pos_of[i] = p;
     }
 }
 
@@ -712,22 +727,20 @@ __global__ void __launch_bounds__(kChunk) dispatch_single_kernel(const int* __re
         off[0] = 0;
         *n_active = sa[kMaxExperts - 1];
     }
-    // placement: within an expert, assignments keep increasing i (warps take turns)
+    // placement as in dispatch_place_kernel (slot order within an expert follows the atomics)
     __shared__ int cursor[kMaxExperts];
     if (tid < kMaxExperts) cursor[tid] = sv[tid] - cnt[tid];
     __syncthreads();
-    const int lane = tid & 31, warp = tid >> 5;
+    const int lane = tid & 31;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    for (int w = 0; w < (n + 31) / 32; w++) {
-        if (warp == w && e >= 0) {
-            const int p = cursor[e] + rank;
-            ilist[p] = tid;
-            pos_of[tid] = p;
-        }
-        __syncwarp();
-        if (warp == w && e >= 0 && rank == 0) cursor[e] += __popc(peers);
-        __syncthreads();
+    const int leader = __ffs(peers) - 1;
+    int base = 0;
+    if (e >= 0 && lane == leader) base = atomicAdd(&cursor[e], __popc(peers));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (e >= 0) {
+        const int p = base + __popc(peers & ((1u << lane) - 1u));
+        ilist[p] = tid;
+        pos_of[tid] = p;
     }
 }
 
@@ -742,7 +755,7 @@ int launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s, const Ite
     dispatch_count_kernel<<<n_chunks, kChunk, 0, s>>>(b.order, n, E, b.chunk_counts);
     dispatch_scan_kernel<<<1, kMaxExperts, 0, s>>>(b.chunk_counts, n_chunks, E, b.counts, b.off, b.active,
                                                    b.n_active, items);
-    dispatch_place_kernel<<<n_chunks, kChunk, 0, s>>>(b.order, n, E, b.chunk_counts, b.ilist, b.pos_of);
+    dispatch_place_kernel<<<n_chunks, kChunk, 0, s>>>(b.order, n, E, b.chunk_counts, b.off, b.ilist, b.pos_of);
     return 3;
 }
 
