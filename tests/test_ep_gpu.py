@@ -96,6 +96,27 @@ LAYERS = {
 }
 
 
+def test_ep_hot_experts_p2p_emulated(port):
+    """Zipf-skewed routing (a few experts take most tokens, so one owner gets far more rows than the
+    others) through the peer-memory exchange of 4 ranks on one GPU."""
+    layer = synth.make_layer(hidden=1024, n_exp=64, n_used=8, inter=512, scoring="sigmoid", w_scale=2.0,
+                             bias=True, zipf=True, shared_inter=256, seed=44)
+    G, T = 4, 120
+    xs = [synth.make_tokens(layer, T, 500 + i, zipf=True) for i in range(G)]
+    dev = torch.device("cuda")
+    order, _ = port.route(layer, np.concatenate(xs))
+    per_rank = np.bincount(order.reshape(-1) // (layer.n_exp // G), minlength=G)
+    assert per_rank.max() > 1.5 * per_rank.min()      # the skew reaches the owners
+    ranks = [ExpertParallelMoE(layer, T, comm=types.SimpleNamespace(world=G, rank=r),
+                               ops=DeviceOps(layer, r, G, dev), exchange="p2p") for r in range(G)]
+    outs = emulate(ranks, [torch.from_numpy(x).to(dev) for x in xs])
+    torch.cuda.synchronize()
+    got = np.concatenate([o.cpu().numpy() for o in outs])
+    for r in ranks:
+        r.close()
+    assert rel(got, port.layer_forward(layer, np.concatenate(xs))) < REL_L2_TOL
+
+
 @pytest.mark.parametrize("name", list(LAYERS))
 @pytest.mark.parametrize("T", [3, 200])
 def test_experts_forward_given_routing(dlib, port, name, T):
