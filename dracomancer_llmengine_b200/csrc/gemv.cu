@@ -444,13 +444,14 @@ __device__ __forceinline__ void fma4(float4& a, float w, const float4& v) {
 }
 __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(
     const float* __restrict__ y, const int* __restrict__ order, const float* __restrict__ wtop,
-    const int* __restrict__ pos_of, int K, int E, int n_out, const float* __restrict__ shared,
+    const int* __restrict__ pos_of, int K, int E, int n_out, int cpb, const float* __restrict__ shared,
     float* __restrict__ out) {
     __shared__ float sw[kCombineMaxK];
     __shared__ const float4* sy[kCombineMaxK];
     __shared__ int sn;
     const int t = blockIdx.x;
     const int n4 = n_out / 4;
+    const int c0 = blockIdx.y * cpb, c1 = min(n4, c0 + cpb);   // this block's float4 columns
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         int base = 0;
@@ -481,7 +482,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(
     const int n = sn;
     const float4* sh = shared ? reinterpret_cast<const float4*>(shared + (size_t)t * n_out) : nullptr;
     float4* o = reinterpret_cast<float4*>(out + (size_t)t * n_out);
-    for (int c = threadIdx.x; c < n4; c += kCombineThreads) {
+    for (int c = c0 + threadIdx.x; c < c1; c += kCombineThreads) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         int j = 0;
         for (; j + 4 <= n; j += 4) {
@@ -514,7 +515,13 @@ void launch_combine(const float* y, const int* order, const float* wtop, const i
     const bool vec = n_out % 4 == 0 && K <= kCombineMaxK && !((uintptr_t)y & 15) && !((uintptr_t)out & 15) &&
                      !((uintptr_t)shared & 15);
     if (vec) {
-        if (T > 0) combine_rows_kernel<<<T, kCombineThreads, 0, s>>>(y, order, wtop, pos_of, K, E, n_out, shared, out);
+        // few rows: each row split over blocks of one float4 column a thread, so small batches
+        // still spread over the SMs
+        const int n4 = n_out / 4;
+        const int cpb = T >= 148 ? n4 : kCombineThreads;
+        dim3 grid(T, (n4 + cpb - 1) / cpb);
+        if (T > 0)
+            combine_rows_kernel<<<grid, kCombineThreads, 0, s>>>(y, order, wtop, pos_of, K, E, n_out, cpb, shared, out);
         return;
     }
     dim3 grid((n_out + 255) / 256, T);
