@@ -42,6 +42,17 @@
 #ifndef DRACO_TC_RAW_STAGES_Q6K
 #define DRACO_TC_RAW_STAGES_Q6K 3
 #endif
+// 64-token tiles (decode and lightly loaded experts): fewer activation stages (their rows come
+// from L2), deeper weight rings (measured: 1.6 % faster on the K2 decode shape, 1 % on cfg2)
+#ifndef DRACO_TC_B_STAGES_64
+#define DRACO_TC_B_STAGES_64 4
+#endif
+#ifndef DRACO_TC_RAW_STAGES_Q4K_64
+#define DRACO_TC_RAW_STAGES_Q4K_64 8
+#endif
+#ifndef DRACO_TC_RAW_STAGES_Q6K_64
+#define DRACO_TC_RAW_STAGES_Q6K_64 5
+#endif
 #ifndef DRACO_TC_SUSPEND_NS
 #define DRACO_TC_SUSPEND_NS 1000
 #endif
@@ -401,11 +412,12 @@ struct Cfg {
     static constexpr int kAccStride = kIssuers * NT;
     static constexpr int kBB = CODE == DRACO_CODE_Q4_K ? 144 : kQ6Padded;   // raw bytes per row superblock
     static constexpr int kRawStage = 128 * kBB;
-    // activation stages: one K step = two 64-wide chunks x NT tokens x 128 B; 128 KB in all
+    // activation stages: one K step = two 64-wide chunks x NT tokens x 128 B
     static constexpr int kBStage = NT * 256;
-    static constexpr int kBStages = NT == 64 ? 8 : 4;
+    static constexpr int kBStages = NT == 64 ? DRACO_TC_B_STAGES_64 : 4;
     // weight stages next to them (227 KB per block)
-    static constexpr int kRawStages = CODE == DRACO_CODE_Q4_K ? DRACO_TC_RAW_STAGES_Q4K : DRACO_TC_RAW_STAGES_Q6K;
+    static constexpr int kRawStages = NT == 64 ? (CODE == DRACO_CODE_Q4_K ? DRACO_TC_RAW_STAGES_Q4K_64 : DRACO_TC_RAW_STAGES_Q6K_64)
+                                               : (CODE == DRACO_CODE_Q4_K ? DRACO_TC_RAW_STAGES_Q4K : DRACO_TC_RAW_STAGES_Q6K);
     static constexpr int kBOff = kRawStages * kRawStage;                 // 1024-aligned below
     static constexpr int kBOffAligned = (kBOff + 1023) / 1024 * 1024;
     static constexpr int kBarOff = kBOffAligned + kBStages * kBStage;
