@@ -722,6 +722,7 @@ struct LayerBufs {
     __half *xs_h, *act_h;          // tensor-core path operands
     int4 *items_gu, *items_dn;
     int *n_items, *tc_err;
+    int* item_tiles = nullptr;     // dispatch scratch for the item lists
     int4 *items_sh_gu = nullptr, *items_sh_dn = nullptr;   // shared expert on the tensor-core path
     int* n_items_sh = nullptr;
     bool use_tc = false, sh_tc = false;
@@ -756,6 +757,7 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
     const size_t o_igu = cv.take<int4>(b.use_tc ? tc_items_capacity((int)n, na_max, tc_tiles_gateup(a.inter)) : 0);
     const size_t o_idn = cv.take<int4>(b.use_tc ? tc_items_capacity((int)n, na_max, tc_tiles_down(a.n_out)) : 0);
     const size_t o_ni = cv.take<int>(2), o_terr = cv.take<int>(1);
+    const size_t o_tiles = cv.take<int>(b.use_tc ? a.E : 0);
     // shared expert on the tensor-core path: reuses Xs and act_h after the routed GEMMs
     b.sh_tc = b.use_tc && a.sh && a.sh->tc && (size_t)T * a.sh_ff <= n * a.inter;
     const size_t sh_tiles = (size_t)T / 64 + 1;
@@ -773,6 +775,7 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
     b.items_dn = (int4*)(w + o_idn);
     b.n_items = (int*)(w + o_ni);
     b.tc_err = (int*)(w + o_terr);
+    b.item_tiles = (int*)(w + o_tiles);
     b.x = (float*)(w + o_x);
     b.out = (float*)(w + o_out);
     b.rb.logits = (float*)(w + o_lg);
@@ -852,6 +855,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
             il.dn = b.items_dn;
             il.n_dn = b.n_items + 1;
             il.mt_dn = tc_tiles_down(a.n_out);
+            il.tiles = b.item_tiles;
             il.nt = tc_token_tile(T * a.K, a.E);
         }
         g_launches += launch_dispatch(T, a.K, a.E, rb, s, il);

@@ -54,6 +54,7 @@ struct ItemLists {
     int mt_dn = 0;
     int nt = 128;
     int* zero = nullptr;
+    int* tiles = nullptr;   // [E] scratch: inclusive token-tile prefix per expert
 };
 // returns the number of kernels launched
 int launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s, const ItemLists& items = ItemLists());

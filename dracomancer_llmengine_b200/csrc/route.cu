@@ -636,20 +636,28 @@ __global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restr
         *il.n_gu = n_tiles * il.mt_gu;
         *il.n_dn = n_tiles * il.mt_dn;
     }
+    if (e < E) il.tiles[e] = st[e];   // inclusive token-tile prefix, for dispatch_items_kernel
+}
+
+// Tensor-core items, one per (token tile, row tile), built in parallel: tile j belongs to the
+// expert whose inclusive tile prefix first exceeds j (binary search over tiles[]).
+__global__ void dispatch_items_kernel(ItemLists il, const int* __restrict__ off, int E) {
+    const int n_tiles = il.tiles[E - 1];
     const int mt_sum = il.mt_gu + il.mt_dn;
-    for (int j = e; j < n_tiles * mt_sum; j += kMaxExperts) {
+    const int total = n_tiles * mt_sum;
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < total; j += gridDim.x * blockDim.x) {
         const int tile = j / mt_sum, r = j % mt_sum;
-        int lo = 0, hi = kMaxExperts - 1;
+        int lo = 0, hi = E - 1;
         while (lo < hi) {
             const int mid = (lo + hi) >> 1;
-            if (st[mid] > tile) hi = mid;
+            if (il.tiles[mid] > tile) hi = mid;
             else lo = mid + 1;
         }
         const int x = lo;
-        const int cx = sv[x] - (x ? sv[x - 1] : 0);
-        const int first_tile = st[x] - (cx + il.nt - 1) / il.nt;
+        const int cx = off[x + 1] - off[x];
+        const int first_tile = il.tiles[x] - (cx + il.nt - 1) / il.nt;
         const int t0 = (tile - first_tile) * il.nt;
-        const int4 item = make_int4(x, r < il.mt_gu ? r : r - il.mt_gu, sv[x] - cx + t0, min(il.nt, cx - t0));
+        const int4 item = make_int4(x, r < il.mt_gu ? r : r - il.mt_gu, off[x] + t0, min(il.nt, cx - t0));
         if (r < il.mt_gu) il.gu[tile * il.mt_gu + r] = item;
         else il.dn[tile * il.mt_dn + r - il.mt_gu] = item;
     }
@@ -756,7 +764,9 @@ int launch_dispatch(int T, int K, int E, RouteBufs& b, cudaStream_t s, const Ite
     dispatch_scan_kernel<<<1, kMaxExperts, 0, s>>>(b.chunk_counts, n_chunks, E, b.counts, b.off, b.active,
                                                    b.n_active, items);
     dispatch_place_kernel<<<n_chunks, kChunk, 0, s>>>(b.order, n, E, b.chunk_counts, b.off, b.ilist, b.pos_of);
-    return 3;
+    if (!items.gu) return 3;
+    dispatch_items_kernel<<<148 * 2, 256, 0, s>>>(items, b.off, E);
+    return 4;
 }
 
 // host expf replica over an array (test hook)
