@@ -1671,8 +1671,11 @@ int draco_b200_ep_plan(const int* order, int T, int K, int n_exp, int n_ranks, i
         set_err("draco_b200_ep_plan: need 1 <= n_ranks <= %d dividing n_exp, K >= 1, block 0 or >= T", kEpMaxRanks);
         return -1;
     }
-    if (!order || !counts || !row_of || !src_tok || !ep_ptrs_ok({order, counts, row_of, src_tok}, "draco_b200_ep_plan"))
+    if (!order || !counts || !row_of || !src_tok) {
+        set_err("draco_b200_ep_plan: null pointer");
         return -1;
+    }
+    if (!ep_ptrs_ok({order, counts, row_of, src_tok}, "draco_b200_ep_plan")) return -1;
     launch_ep_plan(order, T, K, n_exp, n_ranks, block, counts, row_of, src_tok, (cudaStream_t)stream);
     g_launches += 1;
     CK(cudaGetLastError());
@@ -1703,8 +1706,12 @@ int draco_b200_ep_combine(const float* back, const int* row_of, int T, int n_ran
         set_err("draco_b200_ep_combine: need 1 <= n_ranks <= %d, H %% 4 == 0", kEpMaxRanks);
         return -1;
     }
-    if (!ep_ptrs_ok({back, row_of, shared, out}, "draco_b200_ep_combine")) return -1;
     if (T == 0) return 0;
+    if (!back || !row_of || !out) {
+        set_err("draco_b200_ep_combine: null pointer");
+        return -1;
+    }
+    if (!ep_ptrs_ok({back, row_of, shared, out}, "draco_b200_ep_combine")) return -1;
     launch_ep_combine(back, row_of, T, n_ranks, H, shared, out, (cudaStream_t)stream);
     g_launches += 1;
     CK(cudaGetLastError());
@@ -1769,9 +1776,11 @@ int draco_b200_ep_push(const float* X, const int* order, const float* wtop, cons
         set_err("draco_b200_ep_push: need 0 <= rank < n_ranks <= %d, H %% 4 == 0, K >= 1, block >= 1", kEpMaxRanks);
         return -1;
     }
-    if (!X || !order || !wtop || !counts || !src_tok || !dst_x || !dst_meta ||
-        !ep_ptrs_ok({X, order, wtop, counts, src_tok, dst_x, dst_meta}, "draco_b200_ep_push"))
+    if (!X || !order || !wtop || !counts || !src_tok || !dst_x || !dst_meta) {
+        set_err("draco_b200_ep_push: null pointer");
         return -1;
+    }
+    if (!ep_ptrs_ok({X, order, wtop, counts, src_tok, dst_x, dst_meta}, "draco_b200_ep_push")) return -1;
     launch_ep_push(X, order, wtop, counts, n_ranks, rank, src_tok, block, K, H, dst_x, dst_meta,
                    (cudaStream_t)stream);
     g_launches += 1;
@@ -1786,9 +1795,11 @@ int draco_b200_ep_barrier(unsigned* const* peer_flags, unsigned* my_flags, unsig
         set_err("draco_b200_ep_barrier: need 0 <= rank < n_ranks <= %d", kEpMaxRanks);
         return -1;
     }
-    if (!peer_flags || !my_flags || !epoch || !status ||
-        !ep_ptrs_ok({peer_flags, my_flags, epoch, status}, "draco_b200_ep_barrier"))
+    if (!peer_flags || !my_flags || !epoch || !status) {
+        set_err("draco_b200_ep_barrier: null pointer");
         return -1;
+    }
+    if (!ep_ptrs_ok({peer_flags, my_flags, epoch, status}, "draco_b200_ep_barrier")) return -1;
     launch_ep_barrier(peer_flags, my_flags, epoch, n_ranks, rank, status, (cudaStream_t)stream);
     g_launches += 1;
     CK(cudaGetLastError());
@@ -1802,9 +1813,12 @@ int draco_b200_ep_pull_combine(const float* const* src_partial, const int* row_o
         set_err("draco_b200_ep_pull_combine: need 0 <= rank < n_ranks <= %d, H %% 4 == 0, T <= block", kEpMaxRanks);
         return -1;
     }
-    if (!src_partial || !row_of || !out || !ep_ptrs_ok({src_partial, row_of, shared, out}, "draco_b200_ep_pull_combine"))
-        return -1;
     if (T == 0) return 0;
+    if (!src_partial || !row_of || !out) {
+        set_err("draco_b200_ep_pull_combine: null pointer");
+        return -1;
+    }
+    if (!ep_ptrs_ok({src_partial, row_of, shared, out}, "draco_b200_ep_pull_combine")) return -1;
     launch_ep_pull_combine(src_partial, row_of, T, n_ranks, rank, block, H, shared, out, (cudaStream_t)stream);
     g_launches += 1;
     CK(cudaGetLastError());

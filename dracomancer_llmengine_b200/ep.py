@@ -304,6 +304,8 @@ class ExpertParallelMoE:
         b = self._bufs or self._alloc()
         if out is None:
             out = b["out"][:T]
+        if T == 0:
+            x = b["out"]   # a rank without tokens still takes part in the exchange; nothing reads x
         if self.layout == "replicated":
             return self._forward_replicated(x, T, b, out)
         if self.exchange == "p2p":
@@ -383,6 +385,8 @@ def emulate_p2p(ranks: list, xs: list) -> list:
     sts = []
     for r, x in zip(ranks, xs):
         o, b, T = r.ops, r._bufs, int(x.shape[0])
+        if T == 0:
+            x = b["out"]
         o.route(x, T, b["order"], b["wtop"])
         o.plan(b["order"], T, r.K, r.E, G, r.B, b["counts"], b["row_of"], b["src_tok"])
         sh = None
@@ -414,6 +418,8 @@ def emulate(ranks: list, xs: list) -> list:
     for r, x in zip(ranks, xs):
         o, b = r.ops, r._bufs or r._alloc()
         T = int(x.shape[0])
+        if T == 0:
+            x = b["out"]
         block = r.B if r.exchange == "fixed" else 0
         o.route(x, T, b["order"], b["wtop"])
         o.plan(b["order"], T, r.K, r.E, G, block, b["counts"], b["row_of"], b["src_tok"])

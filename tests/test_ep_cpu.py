@@ -37,12 +37,14 @@ def test_plan_ref_layout():
 
 
 @pytest.mark.parametrize("name", list(LAYERS))
-@pytest.mark.parametrize("G,exchange", [(1, "fixed"), (2, "fixed"), (2, "compact"), (4, "compact")])
-def test_emulated_ranks_match_single_process(port, name, G, exchange):
+@pytest.mark.parametrize("G,exchange,Ts", [(1, "fixed", [5]), (2, "fixed", [5, 3]), (2, "compact", [5, 3]),
+                                           (4, "compact", [5, 3, 6, 4]), (4, "fixed", [5, 0, 6, 4]),
+                                           (4, "compact", [0, 3, 0, 4])])
+def test_emulated_ranks_match_single_process(port, name, G, exchange, Ts):
+    """Ranks with ragged token counts, including ranks without tokens, in one process."""
     layer = synth.make_layer(**LAYERS[name])
     if layer.n_exp // G < layer.n_used:
         pytest.skip("fewer experts per rank than n_used")
-    Ts = [5, 3, 6, 4][:G]
     xs = [synth.make_tokens(layer, T, 100 + i, False) for i, T in enumerate(Ts)]
     ranks = [ExpertParallelMoE(layer, max(Ts), comm=types.SimpleNamespace(world=G, rank=r),
                                ops=HostOps(layer, r, G, port), exchange=exchange) for r in range(G)]

@@ -183,12 +183,13 @@ def test_ep_emulated_on_one_gpu(port, name, G, exchange, T):
 
 
 @pytest.mark.parametrize("name", list(LAYERS))
-@pytest.mark.parametrize("G,T", [(2, 40), (4, 150), (8, 96)])
+@pytest.mark.parametrize("G,T", [(2, 40), (4, 150), (8, 96), (4, 0)])
 def test_ep_p2p_emulated_matches_fixed_exchange(port, name, G, T):
     """Peer-memory dispatch/combine (push and pull kernels) on G ranks sharing one GPU: the same
-    rows reach the owners as with the fixed-block all-to-all, so the outputs are identical."""
+    rows reach the owners as with the fixed-block all-to-all, so the outputs are identical.
+    T = 0: every other rank has no tokens."""
     layer = synth.make_layer(**LAYERS[name])
-    Ts = [T - (i % 3) for i in range(G)]
+    Ts = [T - (i % 3) for i in range(G)] if T else [(23 if i % 2 else 0) for i in range(G)]
     xs = [torch.from_numpy(synth.make_tokens(layer, t, 400 + i, False)).cuda() for i, t in enumerate(Ts)]
     dev = torch.device("cuda")
     res = {}
