@@ -882,7 +882,9 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         }
         if (rc == 0) {
             PhaseScope ps(kDown, s);
-            rc = tc_down(call, maps, b.items_dn, b.n_items + 1, b.y, b.tc_err, stats ? stats + kTcStatSites : nullptr, s);
+            // expert outputs as fp16 rows: half the bytes the down GEMM writes and the combine reads
+            rc = tc_down(call, maps, b.items_dn, b.n_items + 1, b.y, true, b.tc_err,
+                         stats ? stats + kTcStatSites : nullptr, s);
         }
         if (stats) {
             cudaStreamSynchronize(s);
@@ -956,7 +958,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
             tc_gather(sc, b.x, nullptr, nullptr, 1, b.xs_h, s);
             rc = tc_gateup(sc, maps, b.items_sh_gu, b.n_items_sh, b.act_h, b.tc_err, nullptr, s);
         }
-        if (rc == 0) rc = tc_down(sc, maps, b.items_sh_dn, b.n_items_sh + 1, b.y_sh, b.tc_err, nullptr, s);
+        if (rc == 0) rc = tc_down(sc, maps, b.items_sh_dn, b.n_items_sh + 1, b.y_sh, false, b.tc_err, nullptr, s);
         if (rc) {
             set_err("shared-expert tensor-core GEMM launch failed (%d)", rc);
             return -3;
@@ -967,8 +969,12 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     }
     {
         PhaseScope ps(kCombine, s);
-        launch_combine(b.y, rb.order, rb.wtop, rb.pos_of, T, a.no_routed ? 0 : a.K, a.E, a.n_out,
-                       a.sh ? b.y_sh : nullptr, b.out, s);
+        if (b.use_tc && !a.no_routed)
+            launch_combine_half(reinterpret_cast<const __half*>(b.y), rb.order, rb.wtop, rb.pos_of, T, a.K, a.E,
+                                a.n_out, a.sh ? b.y_sh : nullptr, b.out, s);
+        else
+            launch_combine(b.y, rb.order, rb.wtop, rb.pos_of, T, a.no_routed ? 0 : a.K, a.E, a.n_out,
+                           a.sh ? b.y_sh : nullptr, b.out, s);
         g_launches += 1;
     }
     CK(cudaGetLastError());

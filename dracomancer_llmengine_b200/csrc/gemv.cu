@@ -414,7 +414,18 @@ void launch_dequant(int code, const uint8_t* W, int rows, int n_in, float* out, 
 // combine: out[t][r] = fma(w[t,K-1], y, ... fma(w[t,0], y, 0)) (+ shared[t][r])
 // (src/m6_moe_tok.c:148-159; the ungated shared expert is added after, src/m6_engine.c:348)
 // ------------------------------------------------------------------------------------------
-__global__ void combine_kernel(const float* __restrict__ y, const int* __restrict__ order,
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+__device__ __forceinline__ float4 load4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 load4(const __half* p) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <typename Y>
+__global__ void combine_kernel(const Y* __restrict__ y, const int* __restrict__ order,
                                const float* __restrict__ wtop, const int* __restrict__ pos_of, int T, int K,
                                int E, int n_out, const float* __restrict__ shared, float* __restrict__ out) {
     const int t = blockIdx.y;
@@ -424,7 +435,7 @@ __global__ void combine_kernel(const float* __restrict__ y, const int* __restric
             const int i = t * K + k;
             const int e = order[i];
             if (e < 0 || e >= E) continue;
-            acc = fmaf(wtop[i], y[(size_t)pos_of[i] * n_out + r], acc);
+            acc = fmaf(wtop[i], to_f(y[(size_t)pos_of[i] * n_out + r]), acc);
         }
         if (shared) acc = __fadd_rn(acc, shared[(size_t)t * n_out + r]);
         out[(size_t)t * n_out + r] = acc;
@@ -442,12 +453,13 @@ __device__ __forceinline__ void fma4(float4& a, float w, const float4& v) {
     a.z = fmaf(w, v.z, a.z);
     a.w = fmaf(w, v.w, a.w);
 }
+template <typename Y>
 __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(
-    const float* __restrict__ y, const int* __restrict__ order, const float* __restrict__ wtop,
+    const Y* __restrict__ y, const int* __restrict__ order, const float* __restrict__ wtop,
     const int* __restrict__ pos_of, int K, int E, int n_out, int cpb, const float* __restrict__ shared,
     float* __restrict__ out) {
     __shared__ float sw[kCombineMaxK];
-    __shared__ const float4* sy[kCombineMaxK];
+    __shared__ const Y* sy[kCombineMaxK];
     __shared__ int sn;
     const int t = blockIdx.x;
     const int n4 = n_out / 4;
@@ -472,7 +484,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(
             if (v) {
                 const int j = base + __popc(m & ((1u << lane) - 1u));
                 sw[j] = w;
-                sy[j] = reinterpret_cast<const float4*>(y + (size_t)p * n_out);
+                sy[j] = y + (size_t)p * n_out;
             }
             base += __popc(m);
         }
@@ -486,13 +498,14 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         int j = 0;
         for (; j + 4 <= n; j += 4) {
-            const float4 v0 = sy[j][c], v1 = sy[j + 1][c], v2 = sy[j + 2][c], v3 = sy[j + 3][c];
+            const float4 v0 = load4(sy[j] + 4 * c), v1 = load4(sy[j + 1] + 4 * c), v2 = load4(sy[j + 2] + 4 * c),
+                         v3 = load4(sy[j + 3] + 4 * c);
             fma4(acc, sw[j], v0);
             fma4(acc, sw[j + 1], v1);
             fma4(acc, sw[j + 2], v2);
             fma4(acc, sw[j + 3], v3);
         }
-        for (; j < n; j++) fma4(acc, sw[j], sy[j][c]);
+        for (; j < n; j++) fma4(acc, sw[j], load4(sy[j] + 4 * c));
         if (sh) {
             const float4 v = sh[c];
             acc.x = __fadd_rn(acc.x, v.x);
@@ -510,8 +523,9 @@ __global__ void set_pair_kernel(int* d, int a, int b) {
 }
 void launch_set_pair(int* d, int a, int b, cudaStream_t s) { set_pair_kernel<<<1, 1, 0, s>>>(d, a, b); }
 
-void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T, int K, int E,
-                    int n_out, const float* shared, float* out, cudaStream_t s) {
+template <typename Y>
+static void combine_typed(const Y* y, const int* order, const float* wtop, const int* pos_of, int T, int K, int E,
+                          int n_out, const float* shared, float* out, cudaStream_t s) {
     const bool vec = n_out % 4 == 0 && K <= kCombineMaxK && !((uintptr_t)y & 15) && !((uintptr_t)out & 15) &&
                      !((uintptr_t)shared & 15);
     if (vec) {
@@ -526,6 +540,15 @@ void launch_combine(const float* y, const int* order, const float* wtop, const i
     }
     dim3 grid((n_out + 255) / 256, T);
     combine_kernel<<<grid, 256, 0, s>>>(y, order, wtop, pos_of, T, K, E, n_out, shared, out);
+}
+
+void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T, int K, int E,
+                    int n_out, const float* shared, float* out, cudaStream_t s) {
+    combine_typed(y, order, wtop, pos_of, T, K, E, n_out, shared, out, s);
+}
+void launch_combine_half(const __half* y, const int* order, const float* wtop, const int* pos_of, int T, int K, int E,
+                         int n_out, const float* shared, float* out, cudaStream_t s) {
+    combine_typed(y, order, wtop, pos_of, T, K, E, n_out, shared, out, s);
 }
 
 // ------------------------------------------------------------------------------------------

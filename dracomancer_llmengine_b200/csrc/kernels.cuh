@@ -85,6 +85,9 @@ void launch_down_code(const ExpertTable& tab, int cd, const int* active, const i
 // then + shared[t][r] when shared != nullptr
 void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T,
                     int K, int E, int n_out, const float* shared, float* out, cudaStream_t s);
+// the same with fp16 expert output rows (the tensor-core path)
+void launch_combine_half(const __half* y, const int* order, const float* wtop, const int* pos_of, int T,
+                         int K, int E, int n_out, const float* shared, float* out, cudaStream_t s);
 // rows y[r] = dot(W row r, x) for r in [o0, o1), any supported code, one vector
 void launch_gemv_rows(int code, const uint8_t* W, const float* x, int n_in, int o0, int o1, float* y,
                       cudaStream_t s, int q6s);

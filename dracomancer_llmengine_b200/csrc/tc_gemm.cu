@@ -722,15 +722,23 @@ __global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
                     }
                 }
             } else {
+                // down: fp32 rows into y_out, or (act_out given) fp16 rows into act_out
                 const int orow = mt * 128 + quarter * 32 + lane;
                 for (int tb = 0; tb < ntok; tb += 16) {
                     uint32_t v[16];
                     ld_acc(acc + tb, v);
-                    float* dst = y_out + (size_t)(p0 + tb) * out_ld + orow;
                     const int nt = min(16, ntok - tb);
+                    if (act_out) {
+                        __half* dst = act_out + (size_t)(p0 + tb) * out_ld + orow;
 #pragma unroll
-                    for (int t = 0; t < 16; t++)
-                        if (t < nt) dst[(size_t)t * out_ld] = __uint_as_float(v[t]);
+                        for (int t = 0; t < 16; t++)
+                            if (t < nt) dst[(size_t)t * out_ld] = __float2half_rn(__uint_as_float(v[t]));
+                    } else {
+                        float* dst = y_out + (size_t)(p0 + tb) * out_ld + orow;
+#pragma unroll
+                        for (int t = 0; t < 16; t++)
+                            if (t < nt) dst[(size_t)t * out_ld] = __uint_as_float(v[t]);
+                    }
                 }
             }
             tc_fence_before();
@@ -950,16 +958,18 @@ int tc_gateup(const TcCall& c, const TcMaps& maps, const int4* items, const int*
     return e == cudaSuccess ? 0 : -3;
 }
 
-int tc_down(const TcCall& c, const TcMaps& maps, const int4* items, const int* n_items, float* y, int* err,
-            unsigned long long* stats, cudaStream_t s) {
+int tc_down(const TcCall& c, const TcMaps& maps, const int4* items, const int* n_items, void* y, bool half_out,
+            int* err, unsigned long long* stats, cudaStream_t s) {
     if (c.P <= 0) return 0;
     cudaError_t e;
+    __half* yh = half_out ? static_cast<__half*>(y) : nullptr;
+    float* yf = half_out ? nullptr : static_cast<float*>(y);
     if (c.cd == DRACO_CODE_Q4_K)
         e = launch_tc<1, DRACO_CODE_Q4_K>(maps.down, maps.down, c.ma, items, n_items, 148, c.nt, c.n_out, c.inter,
-                                          c.n_out, nullptr, y, err, stats, s);
+                                          c.n_out, yh, yf, err, stats, s);
     else
         e = launch_tc<1, DRACO_CODE_Q6_K>(maps.down, maps.down, c.ma, items, n_items, 148, c.nt, c.n_out, c.inter,
-                                          c.n_out, nullptr, y, err, stats, s);
+                                          c.n_out, yh, yf, err, stats, s);
     return e == cudaSuccess ? 0 : -3;
 }
 

@@ -44,8 +44,9 @@ void tc_gather(const TcCall& call, const float* X, const int* ilist, const int* 
 void tc_dense_items(const TcCall& call, int4* items_gu, int* n_gu, int4* items_dn, int* n_dn, cudaStream_t s);
 int tc_gateup(const TcCall& call, const TcMaps& maps, const int4* items, const int* n_items, __half* act_h, int* err,
               unsigned long long* stats, cudaStream_t s);
-int tc_down(const TcCall& call, const TcMaps& maps, const int4* items, const int* n_items, float* y, int* err,
-            unsigned long long* stats, cudaStream_t s);
+// y: fp32 rows, or fp16 rows when half_out
+int tc_down(const TcCall& call, const TcMaps& maps, const int4* items, const int* n_items, void* y, bool half_out,
+            int* err, unsigned long long* stats, cudaStream_t s);
 // wait-statistics sites per kernel (stats holds 2 * kTcStatSites counters: gate/up, down)
 constexpr int kTcStatSites = 15;
 // weight-row tiles per expert: gate/up tiles hold 64 rows of each matrix, down tiles 128 rows
