@@ -617,12 +617,11 @@ __global__ void __launch_bounds__(kMaxExperts) dispatch_scan_kernel(int* __restr
         st[e] += u;
         __syncthreads();
     }
-    const int base = sv[e] - c;   // exclusive offset of expert e
     if (e < E) {
         off[e + 1] = sv[e];
         if (c > 0) active[sa[e] - 1] = e;
     }
-    (void)base;   // the place kernel adds off[e] to the per-chunk prefix
+    // (the place kernel adds off[e] to the per-chunk prefix left in chunk_counts)
     if (e == 0) {
         off[0] = 0;
         *n_active = sa[kMaxExperts - 1];
