@@ -91,7 +91,7 @@ _SIGS = {
     "draco_b200_moe_forward": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, _vp, _vp], ct.c_int),
     "draco_b200_route": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, _vp], ct.c_int),
     "draco_b200_experts_forward": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, ct.c_int, ct.c_int, _vp,
-                                    ct.c_int, _vp], ct.c_int),
+                                    ct.c_int, ct.c_int, _vp], ct.c_int),
     "draco_b200_ep_plan": ([_vp, ct.c_int, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _vp, _vp, _vp, _vp], ct.c_int),
     "draco_b200_ep_pack": ([_vp, _vp, _vp, _vp, ct.c_int, _vp, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _vp, _vp,
                             _vp], ct.c_int),
@@ -100,8 +100,8 @@ _SIGS = {
     "draco_b200_ep_mem_open": ([_vp, ct.POINTER(ct.c_void_p)], ct.c_int),
     "draco_b200_ep_mem_close": ([_vp], ct.c_int),
     "draco_b200_ep_mem_free": ([_vp], ct.c_int),
-    "draco_b200_ep_push": ([_vp, _vp, _vp, _vp, ct.c_int, ct.c_int, _vp, ct.c_int, ct.c_int, ct.c_int, _vp, _vp,
-                            _vp], ct.c_int),
+    "draco_b200_ep_push": ([_vp, _vp, _vp, _vp, ct.c_int, ct.c_int, _vp, ct.c_int, ct.c_int, ct.c_int, _vp, ct.c_int,
+                            _vp, _vp], ct.c_int),
     "draco_b200_ep_barrier": ([_vp, _vp, _vp, ct.c_int, ct.c_int, _vp, _vp], ct.c_int),
     "draco_b200_ep_pull_combine": ([_vp, _vp, ct.c_int, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _vp, _vp, _vp],
                                    ct.c_int),

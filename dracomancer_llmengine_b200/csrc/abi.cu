@@ -702,6 +702,7 @@ struct LayerArgs {
     RouterParams rp{};
     const float* d_gi = nullptr; // router weights (device), null when routing is given
     bool no_routed = false;      // shared expert only
+    bool x_half = false;         // b.x holds fp16 rows
 };
 
 // routing supplied by the caller: rows of ld entries, expert ids minus e_base index the layer's
@@ -711,11 +712,13 @@ struct GivenRoute {
     const float* wtop = nullptr;
     int ld = 0;
     int e_base = 0;
+    bool x_half = false;   // X holds fp16 rows (device memory)
 };
 
 struct LayerBufs {
     RouteBufs rb{};
     float *x, *out, *act, *y, *act_sh, *y_sh;
+    float* x_ws = nullptr;          // the workspace's own activation rows
     int8_t* xq;
     float* xd;
     int16_t* xbs;
@@ -777,6 +780,7 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
     b.tc_err = (int*)(w + o_terr);
     b.item_tiles = (int*)(w + o_tiles);
     b.x = (float*)(w + o_x);
+    b.x_ws = b.x;
     b.out = (float*)(w + o_out);
     b.rb.logits = (float*)(w + o_lg);
     b.rb.order = (int*)(w + o_ord);
@@ -832,6 +836,14 @@ int dense_ffn(Ctx* c, Table* t, int T, const float* x, int ff, int n_in, int n_o
 // otherwise b.rb.order / b.rb.wtop already hold it.
 int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     RouteBufs& rb = b.rb;
+    bool xh = a.x_half;
+    if (xh && (!b.use_tc || (a.sh && !b.sh_tc))) {
+        // a CUDA-core path reads these rows: widen the fp16 rows to fp32 first
+        launch_half_to_float(reinterpret_cast<const __half*>(b.x), b.x_ws, (size_t)T * a.n_in, s);
+        g_launches += 1;
+        b.x = b.x_ws;
+        xh = false;
+    }
     if (a.no_routed) {
         CK(cudaMemsetAsync(rb.err, 0, sizeof(int), s));
         CK(cudaMemsetAsync(b.tc_err, 0, sizeof(int), s));
@@ -874,7 +886,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         const TcMaps& maps = *(const TcMaps*)a.tab->tc;
         if (rc == 0) {
             PhaseScope ps(kGather, s);
-            tc_gather(call, b.x, rb.ilist, rb.off + a.E, a.K, b.xs_h, s);
+            tc_gather(call, b.x, xh, rb.ilist, rb.off + a.E, a.K, b.xs_h, s);
         }
         if (rc == 0) {
             PhaseScope ps(kGateUp, s);
@@ -955,7 +967,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         const TcMaps& maps = *(const TcMaps*)a.sh->tc;
         if (rc == 0) {
             tc_dense_items(sc, b.items_sh_gu, b.n_items_sh, b.items_sh_dn, b.n_items_sh + 1, s);
-            tc_gather(sc, b.x, nullptr, nullptr, 1, b.xs_h, s);
+            tc_gather(sc, b.x, xh, nullptr, nullptr, 1, b.xs_h, s);
             rc = tc_gateup(sc, maps, b.items_sh_gu, b.n_items_sh, b.act_h, b.tc_err, nullptr, s);
         }
         if (rc == 0) rc = tc_down(sc, maps, b.items_sh_dn, b.n_items_sh + 1, b.y_sh, false, b.tc_err, nullptr, s);
@@ -1129,6 +1141,7 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
     a.rp.norm_w = norm_w;
     a.rp.w_scale = w_scale;
     a.no_routed = gr && !gr->order;
+    a.x_half = gr && gr->x_half;
     if (a.no_routed && !a.sh) {
         set_err("no routed experts and no shared expert: nothing to compute");
         return -1;
@@ -1138,6 +1151,10 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
     const bool dev_io = dev_kind(x);
     if (dev_io && ((uintptr_t)x & 15 || (uintptr_t)out & 15)) {
         set_err("device activations and outputs must be 16-byte aligned");
+        return -1;
+    }
+    if (a.x_half && !dev_io) {
+        set_err("fp16 activation rows must be device memory");
         return -1;
     }
     if (gr && gr->order && (dev_kind(gr->order) != dev_io || dev_kind(gr->wtop) != dev_io)) {
@@ -1195,7 +1212,7 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
             (uint64_t)a.rp.n_group_used, (uint64_t)a.rp.norm_w, (uint64_t)__float_as_uint_host(a.rp.w_scale),
             (uint64_t)gemm_path(), (uint64_t)g_act_mode, (uint64_t)b.use_tc, (uint64_t)(gr != nullptr),
             (uintptr_t)(gr ? gr->order : nullptr), (uintptr_t)(gr ? gr->wtop : nullptr), (uint64_t)(gr ? gr->ld : 0),
-            (uint64_t)(gr ? gr->e_base : 0)};
+            (uint64_t)(gr ? gr->e_base : 0), (uint64_t)a.x_half};
         const int rc = captured ? body() : graph_call(c, key, s, body);
         if (!captured) ws_release(c, s);
         return rc;
@@ -1560,8 +1577,8 @@ int draco_b200_moe_forward(const DracoMoeLayer* L, const float* X, int T, float*
                       (cudaStream_t)stream);
 }
 
-int draco_b200_experts_forward(const DracoMoeLayer* L, const float* X, int T, const int* order, const float* wtop,
-                               int ld, int first_expert, float* out, int with_shared, void* stream) {
+int draco_b200_experts_forward(const DracoMoeLayer* L, const void* X, int T, const int* order, const float* wtop,
+                               int ld, int first_expert, float* out, int with_shared, int x_fp16, void* stream) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (order && (!wtop || (ld != 0 && ld < L->n_used) || first_expert < 0)) {
         set_err("draco_b200_experts_forward: wtop missing, ld < n_used or first_expert < 0");
@@ -1572,13 +1589,14 @@ int draco_b200_experts_forward(const DracoMoeLayer* L, const float* X, int T, co
     gr.wtop = wtop;
     gr.ld = ld ? ld : L->n_used;
     gr.e_base = first_expert;
+    gr.x_half = x_fp16 != 0;
     const uint64_t sh3[3] = {(uint64_t)(uintptr_t)L->sh_gate, (uint64_t)(uintptr_t)L->sh_up,
                              (uint64_t)(uintptr_t)L->sh_down};
     const int shc3[3] = {L->sh_code_g, L->sh_code_u, L->sh_code_d};
     const bool has_sh = with_shared && L->sh_gate && L->sh_up && L->sh_down && L->sh_ff > 0;
-    return layer_call(X, T, L->exp_ptrs, L->exp_codes, L->gate_inp, L->probs_b, L->scoring, L->n_exp, L->n_used,
-                      L->n_group, L->n_group_used, L->norm_w, L->w_scale, L->inter, L->n_in, L->n_out,
-                      has_sh ? sh3 : nullptr, shc3, has_sh ? L->sh_ff : 0, out, nullptr, nullptr,
+    return layer_call(static_cast<const float*>(X), T, L->exp_ptrs, L->exp_codes, L->gate_inp, L->probs_b,
+                      L->scoring, L->n_exp, L->n_used, L->n_group, L->n_group_used, L->norm_w, L->w_scale, L->inter,
+                      L->n_in, L->n_out, has_sh ? sh3 : nullptr, shc3, has_sh ? L->sh_ff : 0, out, nullptr, nullptr,
                       (cudaStream_t)stream, &gr);
 }
 
@@ -1775,10 +1793,11 @@ int draco_b200_ep_mem_free(void* ptr) {
 }
 
 int draco_b200_ep_push(const float* X, const int* order, const float* wtop, const int* counts, int n_ranks, int rank,
-                       const int* src_tok, int block, int K, int H, float* const* dst_x, int* const* dst_meta,
-                       void* stream) {
+                       const int* src_tok, int block, int K, int H, void* const* dst_x, int x_fp16,
+                       int* const* dst_meta, void* stream) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (n_ranks < 1 || n_ranks > kEpMaxRanks || rank < 0 || rank >= n_ranks || H % 4 || K < 1 || block < 1) {
+    if (n_ranks < 1 || n_ranks > kEpMaxRanks || rank < 0 || rank >= n_ranks || H % (x_fp16 ? 8 : 4) || K < 1 ||
+        block < 1) {
         set_err("draco_b200_ep_push: need 0 <= rank < n_ranks <= %d, H %% 4 == 0, K >= 1, block >= 1", kEpMaxRanks);
         return -1;
     }
@@ -1787,7 +1806,7 @@ int draco_b200_ep_push(const float* X, const int* order, const float* wtop, cons
         return -1;
     }
     if (!ep_ptrs_ok({X, order, wtop, counts, src_tok, dst_x, dst_meta}, "draco_b200_ep_push")) return -1;
-    launch_ep_push(X, order, wtop, counts, n_ranks, rank, src_tok, block, K, H, dst_x, dst_meta,
+    launch_ep_push(X, order, wtop, counts, n_ranks, rank, src_tok, block, K, H, dst_x, x_fp16 != 0, dst_meta,
                    (cudaStream_t)stream);
     g_launches += 1;
     CK(cudaGetLastError());

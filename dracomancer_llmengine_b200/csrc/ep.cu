@@ -3,6 +3,7 @@
 // token sends its row once to every rank that owns at least one of its K experts, with its full
 // routing row (K global expert ids, K weights) beside it.  The owner computes the weighted sum of
 // its own experts for that row; the home rank adds the G partial rows in rank order.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -202,8 +203,8 @@ __device__ __forceinline__ uint64_t global_ns() {
 // scope before the kernel ends, so the barrier that follows publishes them.
 __global__ void ep_push_kernel(const float* __restrict__ X, const int* __restrict__ order,
                                const float* __restrict__ wtop, const int* __restrict__ counts, int G, int rank,
-                               const int* __restrict__ src_tok, int block, int K, int H, float* const* dst_x,
-                               int* const* dst_meta) {
+                               const int* __restrict__ src_tok, int block, int K, int H, void* const* dst_x,
+                               int x16, int* const* dst_meta) {
     const int lane = threadIdx.x & 31;
     const int wpb = blockDim.x >> 5;
     const int S = G * block;
@@ -220,8 +221,23 @@ __global__ void ep_push_kernel(const float* __restrict__ X, const int* __restric
         }
         const int t = src_tok[row];
         const float4* src = reinterpret_cast<const float4*>(X + (size_t)t * H);
-        float4* dst = reinterpret_cast<float4*>(dst_x[d] + drow * H);
-        for (int i = lane; i < H / 4; i += 32) dst[i] = src[i];
+        if (x16) {   // fp16 rows: half the bytes over the links; the owner's GEMM rounds to fp16 anyway
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(dst_x[d]) + drow * H);
+            for (int i = lane; i < H / 8; i += 32) {
+                const float4 a = src[2 * i], b = src[2 * i + 1];
+                const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+                const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+                uint4 o;
+                o.x = *reinterpret_cast<const uint32_t*>(&h0);
+                o.y = *reinterpret_cast<const uint32_t*>(&h1);
+                o.z = *reinterpret_cast<const uint32_t*>(&h2);
+                o.w = *reinterpret_cast<const uint32_t*>(&h3);
+                dst[i] = o;
+            }
+        } else {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(dst_x[d]) + drow * H);
+            for (int i = lane; i < H / 4; i += 32) dst[i] = src[i];
+        }
         for (int k = lane; k < K; k += 32) {
             meta[k] = order[(size_t)t * K + k];
             meta[K + k] = __float_as_int(wtop[(size_t)t * K + k]);
@@ -292,11 +308,12 @@ __global__ void ep_pull_combine_kernel(const float* const* src_partial, const in
 }  // namespace
 
 void launch_ep_push(const float* X, const int* order, const float* wtop, const int* counts, int G, int rank,
-                    const int* src_tok, int block, int K, int H, float* const* dst_x, int* const* dst_meta,
+                    const int* src_tok, int block, int K, int H, void* const* dst_x, int x16, int* const* dst_meta,
                     cudaStream_t s) {
     const int rows = G * block;
     const int blocks = std::max(1, std::min(148 * 4, (rows + 7) / 8));
-    ep_push_kernel<<<blocks, 256, 0, s>>>(X, order, wtop, counts, G, rank, src_tok, block, K, H, dst_x, dst_meta);
+    ep_push_kernel<<<blocks, 256, 0, s>>>(X, order, wtop, counts, G, rank, src_tok, block, K, H, dst_x, x16,
+                                          dst_meta);
 }
 
 void launch_ep_barrier(unsigned* const* peer_flags, unsigned* my_flags, unsigned* epoch_ctr, int G, int rank,

@@ -517,6 +517,15 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(
     }
 }
 
+__global__ void half_to_float_kernel(const __half* __restrict__ x, float* __restrict__ y, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = __half2float(x[i]);
+}
+void launch_half_to_float(const __half* x, float* y, size_t n, cudaStream_t s) {
+    const int blocks = (int)std::max<size_t>(1, std::min<size_t>(148 * 8, (n + 255) / 256));
+    half_to_float_kernel<<<blocks, 256, 0, s>>>(x, y, n);
+}
+
 __global__ void set_pair_kernel(int* d, int a, int b) {
     d[0] = a;
     d[1] = b;

@@ -85,6 +85,7 @@ void launch_down_code(const ExpertTable& tab, int cd, const int* active, const i
 // then + shared[t][r] when shared != nullptr
 void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T,
                     int K, int E, int n_out, const float* shared, float* out, cudaStream_t s);
+void launch_half_to_float(const __half* x, float* y, size_t n, cudaStream_t s);
 // the same with fp16 expert output rows (the tensor-core path)
 void launch_combine_half(const __half* y, const int* order, const float* wtop, const int* pos_of, int T,
                          int K, int E, int n_out, const float* shared, float* out, cudaStream_t s);
@@ -123,7 +124,7 @@ void launch_ep_combine(const float* back, const int* row_of, int T, int G, int H
 // of G peer pointers), a flag barrier over G ranks (bounded wait, 0x400 in *status), combine
 // loads from the owners' partial buffers
 void launch_ep_push(const float* X, const int* order, const float* wtop, const int* counts, int G, int rank,
-                    const int* src_tok, int block, int K, int H, float* const* dst_x, int* const* dst_meta,
+                    const int* src_tok, int block, int K, int H, void* const* dst_x, int x16, int* const* dst_meta,
                     cudaStream_t s);
 void launch_ep_barrier(unsigned* const* peer_flags, unsigned* my_flags, unsigned* epoch_ctr, int G, int rank,
                        int* status, cudaStream_t s);

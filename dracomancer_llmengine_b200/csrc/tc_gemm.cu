@@ -799,6 +799,20 @@ __global__ void gather_half_kernel(const float* __restrict__ X, const int* __res
     }
 }
 
+// the same from token rows that are already fp16: a row copy
+__global__ void gather_rows16_kernel(const __half* __restrict__ X, const int* __restrict__ ilist,
+                                     const int* __restrict__ n_valid, int tok_div, int P, int H,
+                                     __half* __restrict__ Xs) {
+    const int per_row = H / 8;
+    const int n = n_valid ? min(*n_valid, P) : P;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < (long)n * per_row;
+         i += (long)gridDim.x * blockDim.x) {
+        const int p = (int)(i / per_row), c8 = (int)(i % per_row) * 8;
+        const int t = ilist ? ilist[p] / tok_div : p;
+        *reinterpret_cast<uint4*>(Xs + (size_t)p * H + c8) = *reinterpret_cast<const uint4*>(X + (size_t)t * H + c8);
+    }
+}
+
 }  // namespace tc
 
 // ------------------------------------------------------------------------------ host side
@@ -940,9 +954,15 @@ void tc_dense_items(const TcCall& c, int4* items_gu, int* n_gu, int4* items_dn, 
                                              n_gu, items_dn, n_dn);
 }
 
-void tc_gather(const TcCall& c, const float* X, const int* ilist, const int* n_valid, int tok_div, __half* Xs,
-               cudaStream_t s) {
-    if (c.P > 0) tc::gather_half_kernel<<<148 * 8, 256, 0, s>>>(X, ilist, n_valid, tok_div, c.P, c.n_in, Xs);
+void tc_gather(const TcCall& c, const void* X, bool x_half, const int* ilist, const int* n_valid, int tok_div,
+               __half* Xs, cudaStream_t s) {
+    if (c.P <= 0) return;
+    if (x_half)
+        tc::gather_rows16_kernel<<<148 * 8, 256, 0, s>>>(static_cast<const __half*>(X), ilist, n_valid, tok_div, c.P,
+                                                         c.n_in, Xs);
+    else
+        tc::gather_half_kernel<<<148 * 8, 256, 0, s>>>(static_cast<const float*>(X), ilist, n_valid, tok_div, c.P,
+                                                       c.n_in, Xs);
 }
 
 int tc_gateup(const TcCall& c, const TcMaps& maps, const int4* items, const int* n_items, __half* act_h, int* err,

@@ -31,15 +31,16 @@ int tc_make_weight_maps(TcMaps* maps, const uint8_t* gate, const uint8_t* up, co
                         int cg, int cd, int inter, int n_in, int n_out);
 // The three launches of one call, for P sorted assignments (the item lists were built by the
 // dispatch scan with tc_token_tile / tc_tiles_*):
-//   tc_gather: Xs[p] = fp16(X[ilist[p] / tok_div]) for p < *n_valid (all P when n_valid is null)
+//   tc_gather: Xs[p] = fp16(X[ilist[p] / tok_div]) for p < *n_valid (all P when n_valid is null);
+//              X fp32 rows, or fp16 rows (x_half) copied as they are
 //   tc_gateup: act_h = fp16(silu(gate . Xs) * (up . Xs)) per item
 //   tc_down:   y = down . act_h per item (fp32)
 // err (device int) is nonzero after a bounded wait ran out; stats optionally collects wait
 // cycles (kTcStatSites per kernel).
 int tc_prepare(TcCall* call, int cg, int cd, int n_exp, int inter, int n_in, int n_out, int P, __half* Xs,
                __half* act_h);
-void tc_gather(const TcCall& call, const float* X, const int* ilist, const int* n_valid, int tok_div, __half* Xs,
-               cudaStream_t s);
+void tc_gather(const TcCall& call, const void* X, bool x_half, const int* ilist, const int* n_valid, int tok_div,
+               __half* Xs, cudaStream_t s);
 // item lists of a dense (shared-expert) call: one expert, call.P token rows in order
 void tc_dense_items(const TcCall& call, int4* items_gu, int* n_gu, int4* items_dn, int* n_dn, cudaStream_t s);
 int tc_gateup(const TcCall& call, const TcMaps& maps, const int4* items, const int* n_items, __half* act_h, int* err,

@@ -60,7 +60,8 @@ def slice_desc(full: DracoMoeLayer, first: int, count: int, keep: list) -> Draco
 def tensor_at(ptr: int, shape, dtype, device):
     """A torch tensor over existing device memory (no copy; the memory must outlive it)."""
     import torch
-    typestr = {torch.float32: "<f4", torch.int32: "<i4", torch.int64: "<i8", torch.uint32: "<u4"}[dtype]
+    typestr = {torch.float32: "<f4", torch.float16: "<f2", torch.int32: "<i4", torch.int64: "<i8",
+               torch.uint32: "<u4"}[dtype]
 
     class _Cai:
         pass
@@ -72,22 +73,25 @@ def tensor_at(ptr: int, shape, dtype, device):
 
 class PeerBuffers:
     """One rank's buffers of the peer-memory exchange, allocated by the library with CUDA IPC
-    handles: receive rows x [G*B, H] fp32, routing rows meta [G*B, 2K] int32, partial rows
-    [G*B, H] fp32 and a control block (flag words [16] u32 at byte 0, barrier epoch at 64,
-    status at 128).  `link` maps every rank's buffers and builds the device pointer arrays the
-    kernels take."""
+    handles: receive rows x [G*B, H] (fp16 when x_half: the owners' tensor-core GEMMs round
+    activations to fp16 in any case, so this halves the bytes on the links without changing a
+    result), routing rows meta [G*B, 2K] int32, partial rows [G*B, H] fp32 and a control block
+    (flag words [16] u32 at byte 0, barrier epoch at 64, status at 128).  `link` maps every
+    rank's buffers and builds the device pointer arrays the kernels take."""
     CTL = 256
 
-    def __init__(self, G, rank, B, H, K, device):
+    def __init__(self, G, rank, B, H, K, device, x_half=True):
         import torch
         self.L, self.G, self.rank, self.device = lib(), G, rank, device
-        sizes = {"x": G * B * H * 4, "meta": G * B * 2 * K * 4, "partial": G * B * H * 4, "ctl": self.CTL}
+        self.x_half = bool(x_half) and H % 8 == 0
+        xb = 2 if self.x_half else 4
+        sizes = {"x": G * B * H * xb, "meta": G * B * 2 * K * 4, "partial": G * B * H * 4, "ctl": self.CTL}
         self.own, self.handles, self.opened = {}, {}, []
         for name, n in sizes.items():
             p, h = ct.c_void_p(), (ct.c_char * 64)()
             _check(self.L.draco_b200_ep_mem_alloc(n, ct.byref(p), h), "draco_b200_ep_mem_alloc")
             self.own[name], self.handles[name] = p.value, bytes(h)
-        self.x = tensor_at(self.own["x"], (G * B, H), torch.float32, device)
+        self.x = tensor_at(self.own["x"], (G * B, H), torch.float16 if self.x_half else torch.float32, device)
         self.meta = tensor_at(self.own["meta"], (G * B, 2 * K), torch.int32, device)
         self.partial = tensor_at(self.own["partial"], (G * B, H), torch.float32, device)
         ctl = self.own["ctl"]
@@ -172,19 +176,21 @@ class DeviceOps:
 
     def shared(self, x, T, out):
         _check(self.L.draco_b200_experts_forward(ct.byref(self.local), x.data_ptr(), T, None, None, 0, 0,
-                                                 out.data_ptr(), 1, self._s()), "draco_b200_experts_forward")
+                                                 out.data_ptr(), 1, 0, self._s()), "draco_b200_experts_forward")
 
     def _experts(self, x, T, order_ptr, wtop_ptr, ld, with_shared, out):
+        x16 = 1 if x.dtype == self.torch.float16 else 0
         _check(self.L.draco_b200_experts_forward(ct.byref(self.local), x.data_ptr(), T, order_ptr, wtop_ptr, ld,
-                                                 self.first, out.data_ptr(), 1 if with_shared else 0, self._s()),
-               "draco_b200_experts_forward")
+                                                 self.first, out.data_ptr(), 1 if with_shared else 0, x16,
+                                                 self._s()), "draco_b200_experts_forward")
 
     def experts_routed(self, x, T, order, wtop, with_shared, out):
         """out[t] = sum_k wtop[t][k] * expert(x[t]) over the ids in this rank's slice (+ shared)."""
         self._experts(x, T, order.data_ptr(), wtop.data_ptr(), order.shape[1], with_shared, out)
 
     def experts_meta(self, x, R, meta, K, out):
-        """The same on received rows whose routing rows are {K ids, K weight bits} in meta [R, 2K]."""
+        """The same on received rows (fp32, or fp16 from the peer-memory exchange) whose routing
+        rows are {K ids, K weight bits} in meta [R, 2K]."""
         self._experts(x, R, meta.data_ptr(), meta.data_ptr() + 4 * K, 2 * K, False, out)
 
     def combine(self, back, row_of, T, G, H, sh, out):
@@ -194,8 +200,8 @@ class DeviceOps:
 
     def push(self, x, order, wtop, counts, G, rank, src_tok, block, K, H, pb: PeerBuffers):
         _check(self.L.draco_b200_ep_push(x.data_ptr(), order.data_ptr(), wtop.data_ptr(), counts.data_ptr(), G, rank,
-                                         src_tok.data_ptr(), block, K, H, pb.dst_x.data_ptr(), pb.dst_meta.data_ptr(),
-                                         self._s()), "draco_b200_ep_push")
+                                         src_tok.data_ptr(), block, K, H, pb.dst_x.data_ptr(), 1 if pb.x_half else 0,
+                                         pb.dst_meta.data_ptr(), self._s()), "draco_b200_ep_push")
 
     def barrier(self, G, rank, pb: PeerBuffers):
         _check(self.L.draco_b200_ep_barrier(pb.peer_flags.data_ptr(), pb.my_flags, pb.epoch, G, rank, pb.status,

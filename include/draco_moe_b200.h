@@ -158,10 +158,12 @@ int draco_b200_route(const DracoMoeLayer* L, const float* X, int T, int* order, 
  *            with_shared != 0 and L has one)
  * order == NULL: no routed experts, out = shared expert (L must have one).  Pointers are all
  * host (synchronous) or all device (asynchronous on stream when given).  gate_inp/probs_b of L
- * are not used. */
-int draco_b200_experts_forward(const DracoMoeLayer* L, const float* X, int T, const int* order,
+ * are not used.  x_fp16 != 0: X holds fp16 rows (device memory only); the tensor-core path
+ * reads them as they are (it rounds its activations to fp16 in any case), the CUDA-core paths
+ * widen them to fp32 first. */
+int draco_b200_experts_forward(const DracoMoeLayer* L, const void* X, int T, const int* order,
                                const float* wtop, int ld, int first_expert, float* out,
-                               int with_shared, void* stream);
+                               int with_shared, int x_fp16, void* stream);
 
 /* Expert-parallel token exchange over n_ranks ranks that split n_exp experts contiguously
  * (rank r owns [r*n_exp/n_ranks, (r+1)*n_exp/n_ranks)).  Device pointers, 16-byte aligned,
@@ -190,7 +192,8 @@ int draco_b200_ep_combine(const float* back, const int* row_of, int T, int n_ran
  *  ep_push: the dispatch of ep_pack with block > 0, written straight into the owners' receive
  *    buffers: row j of the block for rank d lands at row rank*block + j of dst_x[d] (H floats)
  *    and dst_meta[d] (2K ints); unused rows of the block get ids -1.  dst_x/dst_meta are device
- *    arrays of n_ranks pointers (this rank's own buffers at index rank).
+ *    arrays of n_ranks pointers (this rank's own buffers at index rank).  x_fp16 != 0: the rows
+ *    are stored as fp16 (H % 8 == 0).
  *  ep_barrier: every rank sets its word in each peer's flag array (peer_flags: device array of
  *    n_ranks pointers to the ranks' flag arrays of n_ranks words) to the next epoch (*epoch, a
  *    device counter) and waits until its own array my_flags holds that epoch from all ranks.
@@ -202,8 +205,8 @@ int draco_b200_ep_mem_open(const void* handle, void** ptr);
 int draco_b200_ep_mem_close(void* ptr);
 int draco_b200_ep_mem_free(void* ptr);
 int draco_b200_ep_push(const float* X, const int* order, const float* wtop, const int* counts, int n_ranks,
-                       int rank, const int* src_tok, int block, int K, int H, float* const* dst_x,
-                       int* const* dst_meta, void* stream);
+                       int rank, const int* src_tok, int block, int K, int H, void* const* dst_x,
+                       int x_fp16, int* const* dst_meta, void* stream);
 int draco_b200_ep_barrier(unsigned* const* peer_flags, unsigned* my_flags, unsigned* epoch, int n_ranks,
                           int rank, int* status, void* stream);
 int draco_b200_ep_pull_combine(const float* const* src_partial, const int* row_of, int T, int n_ranks,

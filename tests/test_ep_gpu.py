@@ -130,7 +130,7 @@ def test_experts_forward_given_routing(dlib, port, name, T):
     # whole expert set, routing given, shared on: the same output as the routed call
     out = np.empty_like(ref_out)
     assert dlib.draco_b200_experts_forward(ct.byref(full), X.ctypes.data, T, order.ctypes.data, wtop.ctypes.data,
-                                           0, 0, out.ctypes.data, 1, None) == 0, dm.last_error()
+                                           0, 0, out.ctypes.data, 1, 0, None) == 0, dm.last_error()
     assert np.array_equal(out.view(np.uint32), ref_out.view(np.uint32))
     # routing rows with a stride (device buffers, asynchronous), summed over four expert slices
     dev = torch.device("cuda")
@@ -145,12 +145,23 @@ def test_experts_forward_given_routing(dlib, port, name, T):
         d = slice_desc(full, r * e_loc, e_loc, keep)
         part = torch.empty((T, layer.hidden), device=dev)
         assert dlib.draco_b200_experts_forward(ct.byref(d), d_x.data_ptr(), T, d_meta.data_ptr(),
-                                               d_meta.data_ptr() + 4 * K, 2 * K, r * e_loc, part.data_ptr(), 0,
+                                               d_meta.data_ptr() + 4 * K, 2 * K, r * e_loc, part.data_ptr(), 0, 0,
                                                _s()) == 0, dm.last_error()
         total += part.cpu().numpy()
     sh = torch.empty((T, layer.hidden), device=dev)
-    assert dlib.draco_b200_experts_forward(ct.byref(full), d_x.data_ptr(), T, None, None, 0, 0, sh.data_ptr(), 1,
+    assert dlib.draco_b200_experts_forward(ct.byref(full), d_x.data_ptr(), T, None, None, 0, 0, sh.data_ptr(), 1, 0,
                                            _s()) == 0, dm.last_error()
+    # fp16 activation rows give the same bits as fp32 rows holding the same values: the
+    # tensor-core path (T = 200) reads them as they are, the CUDA-core path (T = 3) widens them
+    d_meta_o, d_meta_w = d_meta.data_ptr(), d_meta.data_ptr() + 4 * K
+    o32 = torch.empty((T, layer.hidden), device=dev)
+    o16 = torch.empty((T, layer.hidden), device=dev)
+    x16 = d_x.half()
+    for xx, oo, flag in ((d_x.half().float(), o32, 0), (x16, o16, 1)):
+        assert dlib.draco_b200_experts_forward(ct.byref(full), xx.data_ptr(), T, d_meta_o, d_meta_w, 2 * K, 0,
+                                               oo.data_ptr(), 1, flag, _s()) == 0, dm.last_error()
+    torch.cuda.synchronize()
+    assert np.array_equal(o16.cpu().numpy().view(np.uint32), o32.cpu().numpy().view(np.uint32))
     sh_h = sh.cpu().numpy()
     sh_ref = port.shared_add(layer, X, np.zeros_like(ref_out))
     assert rel(sh_h, sh_ref) < REL_L2_TOL
