@@ -1,12 +1,13 @@
-"""Benchmark of the MoE FFN layer (BASELINE.json metric: MoE layer tok/s, with HBM GB/s and
-TFLOP/s against the B200 roofline).
+"""Benchmark of the MoE FFN layer (metric: MoE layer tok/s, with HBM GB/s and TFLOP/s against the
+B200 roofline).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl draco|reference]
 
 One step = one MoE layer forward (routing, grouped expert gate/up/down, combine, shared expert
 when the layer has one) over the configuration's token batch, synthetic seeded weights and
-activations (dracomancer_llmengine_b200.synth).  Default workload: configs[1] of BASELINE.json,
-chunked prefill of 512 tokens through the H2048/E128/top-8/F768 Q4_K+Q6_K layer on one B200.
+activations (dracomancer_llmengine_b200.synth).  Default workload: the second benchmark
+configuration, chunked prefill of 512 tokens through the H2048/E128/top-8/F768 Q4_K+Q6_K layer on
+one B200.
 
   value  device-resident throughput: inputs already in HBM, CUDA events on the launching
          stream (a dedicated non-default stream), weights (392 MB) larger than L2 so no flush
