@@ -286,7 +286,12 @@ def main():
         with torch.cuda.stream(stream):
             ep = ExpertParallelMoE(layer, T, exchange=args.exchange, device=dev)
 
+    graph = None
+
     def fwd():
+        if graph is not None:
+            graph.replay()
+            return
         if ep is not None:
             ep.forward(X, out)
             return
@@ -306,6 +311,11 @@ def main():
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
             fwd()
+        if ep is not None and args.exchange == "p2p":
+            # the expert-parallel step as one CUDA graph (no collective, no host round trip in it)
+            graph = ep.capture(X, out)
+            for _ in range(2):
+                fwd()
     torch.cuda.synchronize()
     experts = None
     if ep is not None:
@@ -338,11 +348,13 @@ def main():
     # phase times (and the dominant kernel's) from a second pass of the same steps with the
     # library's per-phase CUDA events on, so the events do not inflate the timed steps
     dm.profile(True)
+    g_saved, graph = graph, None   # per-phase events need the eager calls
     with torch.cuda.stream(stream):
         for i in range(args.steps):
             if flush is not None:
                 flush_l2()
             fwd()
+    graph = g_saved
     torch.cuda.synchronize()
     prof = dm.profile_read()
     dm.profile(False)
@@ -361,7 +373,7 @@ def main():
         if ep is not None:
             with torch.cuda.stream(stream):
                 X.copy_(Xp, non_blocking=True)
-                ep.forward(X, out)
+                fwd()
                 Op.copy_(out, non_blocking=True)
             stream.synchronize()
             return
@@ -416,6 +428,7 @@ def main():
         print(json.dumps(line), flush=True)
     if ep is not None:
         ep.check()
+        graph = None
         ep.close()
     if dist:
         dist.barrier()

@@ -280,10 +280,28 @@ class ExpertParallelMoE:
                 for k in ("send_x", "send_meta", "recv_x", "recv_meta", "partial", "back", "rcounts"):
                     b[k] = None
                 self.peer = PeerBuffers(G, self.rank, B, H, K, o.device)
-                if hasattr(self.comm, "all_gather_object"):
+                if G == 1:
+                    self.peer.link([dict(self.peer.own)])
+                elif hasattr(self.comm, "all_gather_object"):
                     self.peer.open_peers(self.comm.all_gather_object(self.peer.handles))
         self._bufs = b
         return b
+
+    def capture(self, x, out):
+        """A CUDA graph of forward(x, out) for fixed buffers x and out (the peer-memory exchange:
+        no collective library call and no host round trip in the step), after one eager call
+        that sizes every workspace.  Returns the torch.cuda.CUDAGraph; replay() runs the step on
+        the current contents of x.  Graphs cannot hold the host synchronisation of the "compact"
+        exchange or the NCCL collectives of "fixed" and "replicated" here."""
+        import torch
+        if self.exchange != "p2p" or self.layout != "a2a":
+            raise ValueError("capture needs the peer-memory exchange")
+        self.forward(x, out)
+        torch.cuda.current_stream().synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=torch.cuda.current_stream()):
+            self.forward(x, out)
+        return g
 
     def check(self):
         """Raise if a barrier of the peer-memory exchange gave up waiting (status read back)."""

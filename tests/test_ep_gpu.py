@@ -217,6 +217,32 @@ def test_ep_p2p_emulated_matches_fixed_exchange(port, name, G, T):
     assert rel(res["p2p"], port.layer_forward(layer, X)) < REL_L2_TOL
 
 
+def test_ep_p2p_graph_replay_matches_eager(port):
+    """The whole peer-memory step (routing, plan, push, barriers, routed experts, shared expert,
+    pull) captured in one CUDA graph gives the eager step's bits, also after new inputs."""
+    layer = synth.make_layer(**LAYERS["softmax_e64_shared"])
+    dev = torch.device("cuda")
+    T = 64
+    ep = ExpertParallelMoE(layer, T, comm=types.SimpleNamespace(world=1, rank=0), ops=DeviceOps(layer, 0, 1, dev),
+                           exchange="p2p")
+    x = torch.from_numpy(synth.make_tokens(layer, T, 600, False)).to(dev)
+    out = torch.empty((T, layer.hidden), device=dev)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        g = ep.capture(x, out)
+        for seed in (601, 602):
+            x.copy_(torch.from_numpy(synth.make_tokens(layer, T, seed, False)))
+            g.replay()
+            got = out.clone()
+            want = ep.forward(x, torch.empty_like(out)).clone()
+    torch.cuda.synchronize()
+    ep.check()
+    assert np.array_equal(got.cpu().numpy().view(np.uint32), want.cpu().numpy().view(np.uint32))
+    assert rel(want.cpu().numpy(), port.layer_forward(layer, x.cpu().numpy())) < REL_L2_TOL
+    del g
+    ep.close()
+
+
 def test_ep_barrier_one_rank_and_bounded_wait(dlib):
     """The flag barrier: alone it passes at once and counts epochs; with a second rank that never
     arrives (a flag nothing sets) it gives up after its time limit, reports 0x400 and the device
