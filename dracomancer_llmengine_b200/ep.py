@@ -299,7 +299,9 @@ class ExpertParallelMoE:
         self.forward(x, out)
         torch.cuda.current_stream().synchronize()
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=torch.cuda.current_stream()):
+        # thread-local capture: other threads of the process (a process group's watchdog) keep
+        # using CUDA while this one captures
+        with torch.cuda.graph(g, stream=torch.cuda.current_stream(), capture_error_mode="thread_local"):
             self.forward(x, out)
         return g
 
