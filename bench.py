@@ -315,6 +315,11 @@ def main():
             # the expert-parallel step as one CUDA graph (no collective, no host round trip in it)
             try:
                 graph = ep.capture(X, out)
+                eager = out.clone()           # capture ran one eager step first
+                graph.replay()
+                stream.synchronize()
+                if not torch.equal(out, eager):
+                    raise RuntimeError("graph replay differs from the eager step")
             except Exception as exc:   # keep the eager step
                 print(f"rank {rank}: graph capture failed ({exc}); timing eager steps", file=sys.stderr)
                 graph = None
