@@ -70,27 +70,33 @@ __global__ void __launch_bounds__(32 * TY) router_logits_kernel(const float* __r
 // Rows are padded to 132 floats so the rows a warp reads at one k fall in distinct bank
 // groups.  Needs H % 4 == 0 and 16-byte aligned X and W.
 namespace rl {
-constexpr int KC = 128, LD = KC + 4, TT = 8, TE = 32, NTH = 128;
-constexpr int NV = (TT + TE) * (KC / 4);   // 16-byte copies per chunk
-constexpr int PER = NV / NTH;
+constexpr int KC = 128, LD = KC + 4, TT = 8;
+// NW warps per block cover TE = 8 NW experts
+template <int NW>
+struct Shape {
+    static constexpr int TE = 8 * NW, NTH = 32 * NW;
+    static constexpr int NV = (TT + TE) * (KC / 4);   // 16-byte copies per chunk
+    static constexpr int PER = NV / NTH;
+    static_assert(NV % NTH == 0, "copies per thread");
+};
 // ring depth: 3 chunks when each chunk carries enough work (many tokens), 8 for decode-sized
 // batches, where a chunk is only ~512 cycles of add chain against ~2 us of cold HBM latency
-template <int NS>
+template <int NS, int NW>
 constexpr int smem_bytes() {
-    return NS * (TT + TE) * LD * 4;
+    return NS * (TT + Shape<NW>::TE) * LD * 4;
 }
-static_assert(NV % NTH == 0, "copies per thread");
 }
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
                  "l"(src), "r"(src_bytes)
                  : "memory");
 }
-template <int NS>
-__global__ void __launch_bounds__(rl::NTH) router_logits_v2(const float* __restrict__ X, const float* __restrict__ W,
+template <int NS, int NW>
+__global__ void __launch_bounds__(32 * NW) router_logits_v2(const float* __restrict__ X, const float* __restrict__ W,
                                                             int T, int E, int H, float* __restrict__ logits,
                                                             int* __restrict__ zero_err) {
     using namespace rl;
+    constexpr int TE = Shape<NW>::TE, NTH = Shape<NW>::NTH, PER = Shape<NW>::PER;
     if (zero_err && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *zero_err = 0;
     extern __shared__ __align__(16) float rl_smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -309,15 +315,18 @@ void launch_router_logits(const float* X, const float* W, int T, int E, int H, f
             launch_router_tile<8, 2, 8, 3>(X, W, T, E, H, logits, s, zero_err);
             return;
         }
-        dim3 grid((T + 7) / 8, (E + 31) / 32);
         if (T <= 16) {
-            constexpr int sm = rl::smem_bytes<8>();
-            cudaFuncSetAttribute(router_logits_v2<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-            router_logits_v2<8><<<grid, rl::NTH, sm, s>>>(X, W, T, E, H, logits, zero_err);
+            dim3 grid((T + 7) / 8, (E + 31) / 32);
+            constexpr int sm = rl::smem_bytes<8, 4>();
+            cudaFuncSetAttribute(router_logits_v2<8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+            router_logits_v2<8, 4><<<grid, 128, sm, s>>>(X, W, T, E, H, logits, zero_err);
         } else {
-            constexpr int sm = rl::smem_bytes<3>();
-            cudaFuncSetAttribute(router_logits_v2<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-            router_logits_v2<3><<<grid, rl::NTH, sm, s>>>(X, W, T, E, H, logits, zero_err);
+            // 8 tokens x 16 experts a block: twice the blocks of 32-expert tiles, so mid-sized
+            // batches (a few hundred tokens) put more warps on each SM
+            dim3 grid((T + 7) / 8, (E + 15) / 16);
+            constexpr int sm = rl::smem_bytes<3, 2>();
+            cudaFuncSetAttribute(router_logits_v2<3, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+            router_logits_v2<3, 2><<<grid, 64, sm, s>>>(X, W, T, E, H, logits, zero_err);
         }
         return;
     }
