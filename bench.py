@@ -323,6 +323,8 @@ def main():
             except Exception as exc:   # keep the eager step
                 print(f"rank {rank}: graph capture failed ({exc}); timing eager steps", file=sys.stderr)
                 graph = None
+                torch.cuda.synchronize()
+                ep.peer.status_t.zero_()   # the eager steps that follow report their own waits
             for _ in range(2):
                 fwd()
     torch.cuda.synchronize()
