@@ -355,6 +355,8 @@ def main():
             ev[i][1].record(stream)
         torch.cuda.synchronize()
     launches = L.draco_b200_launch_count() - launches0
+    if graph is not None:   # replays bypass the host-side counter: the captured step's kernels
+        launches = ep.launches_per_step * args.steps
     step_ms = [a.elapsed_time(b) for a, b in ev]
     # phase times (and the dominant kernel's) from a second pass of the same steps with the
     # library's per-phase CUDA events on, so the events do not inflate the timed steps

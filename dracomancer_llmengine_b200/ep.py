@@ -296,7 +296,10 @@ class ExpertParallelMoE:
         import torch
         if self.exchange != "p2p" or self.layout != "a2a":
             raise ValueError("capture needs the peer-memory exchange")
+        n0 = lib().draco_b200_launch_count()
         self.forward(x, out)
+        # the library's kernels in one step (a replay launches the same ones without the host)
+        self.launches_per_step = int(lib().draco_b200_launch_count() - n0)
         torch.cuda.current_stream().synchronize()
         g = torch.cuda.CUDAGraph()
         # thread-local capture: other threads of the process (a process group's watchdog) keep

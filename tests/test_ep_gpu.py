@@ -230,6 +230,7 @@ def test_ep_p2p_graph_replay_matches_eager(port):
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
         g = ep.capture(x, out)
+        assert ep.launches_per_step >= 8   # route, plan, push, barriers, expert GEMMs, pull
         for seed in (601, 602):
             x.copy_(torch.from_numpy(synth.make_tokens(layer, T, seed, False)))
             g.replay()
