@@ -81,6 +81,15 @@ extern "C" int draco_b200_moe_tok_noalloc(const float* X, const int* order, cons
         (cg != DRACO_CODE_Q8_0 && n_in % 256) || (cu != DRACO_CODE_Q8_0 && n_in % 256) ||
         (cd != DRACO_CODE_Q8_0 && inter % 256))
         return fail(-1, "row length not a multiple of the block size");
+    // the row decoders read Q4_K superblocks with 4-byte loads from 16-byte aligned blocks and
+    // Q6_K / Q8_0 blocks with 2-byte loads: a misaligned table entry is refused here, before
+    // anything runs, instead of faulting on the device
+    for (int e = 0; e < n_exp; e++)
+        for (int k = 0; k < 3; k++) {
+            const uint64_t a = ep_dev[3 * e + k];
+            const uint64_t align = ec[3 * e + k] == DRACO_CODE_Q4_K ? 16 : 2;
+            if (a == 0 || a % align) return fail(-1, "weight address null or misaligned for its format");
+        }
     const size_t need = scratch_bytes(T, n_used, inter, n_out, n_exp);
     if (need > kNoAllocScratchBytes) {
         fprintf(stderr,

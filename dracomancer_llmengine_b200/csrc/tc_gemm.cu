@@ -718,7 +718,7 @@ __global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
                         const float g = is_up ? other : mine_e, u = is_up ? mine_o : other;
                         const int col = tb + c + (is_up ? 1 : 0);
                         if (col < ntok)
-                            act_out[(size_t)(p0 + col) * out_ld + orow] = __float2half_rn(g / (1.f + __expf(-g)) * u);
+                            act_out[(size_t)(p0 + col) * out_ld + orow] = __float2half_rn(silu_mul(g, u));
                     }
                 }
             } else {

@@ -273,6 +273,24 @@ void orc_route_sigmoid(const float* x, const float* gate_inp, const float* probs
     free(sel);
 }
 
+/* Routing of T token rows at once: the per-token routers above, one token per OpenMP thread
+ * (each token's routing is independent, so the threads change nothing in the results).
+ * scoring 0 = orc_route_softmax, 1 = orc_route_sigmoid. */
+void orc_route_batch(int scoring, const float* X, int T, const float* gate_inp, const float* probs_b,
+                     int n_exp, int n_used, int n_group, int n_group_used, int norm_w, float w_scale,
+                     int n_in, int* idx, float* w) {
+    #pragma omp parallel for schedule(dynamic, 4)
+    for (int t = 0; t < T; t++) {
+        const float* x = X + (size_t)t * n_in;
+        if (scoring == 0)
+            orc_route_softmax(x, gate_inp, n_exp, n_used, n_in, idx + (size_t)t * n_used,
+                              w + (size_t)t * n_used, NULL);
+        else
+            orc_route_sigmoid(x, gate_inp, probs_b, n_exp, n_used, n_group, n_group_used, norm_w,
+                              w_scale, n_in, idx + (size_t)t * n_used, w + (size_t)t * n_used, NULL);
+    }
+}
+
 static inline float silu_mul(float g, float u) { return (g / (1.f + expf(-g))) * u; }
 
 void orc_moe_experts(const float* x, const uint64_t* p3, const int* c3, const float* wtop,
@@ -380,6 +398,14 @@ void orc_shared_add(const float* x, const uint8_t* gw, const uint8_t* uw, const 
     free(g);
     free(u);
     free(y);
+}
+
+/* orc_shared_add for T token rows (one OpenMP thread per token; rows are independent) */
+void orc_shared_add_batch(const float* X, int T, const uint8_t* gw, const uint8_t* uw, const uint8_t* dw,
+                          int cg, int cu, int cd, int sh_ff, int n_in, int n_out, float* out) {
+    #pragma omp parallel for schedule(dynamic, 1)
+    for (int t = 0; t < T; t++)
+        orc_shared_add(X + (size_t)t * n_in, gw, uw, dw, cg, cu, cd, sh_ff, n_in, n_out, out + (size_t)t * n_out);
 }
 
 void orc_moe_tok(const float* X, const int* order, const float* wtop, const uint64_t* ep,

@@ -38,6 +38,11 @@ void orc_route_softmax(const float* x, const float* gate_inp, int n_exp, int n_u
 void orc_route_sigmoid(const float* x, const float* gate_inp, const float* probs_b, int n_exp,
                        int n_used, int n_group, int n_group_used, int norm_w, float w_scale,
                        int n_in, int* idx, float* w, float* probs_out);
+/* the two routers over T token rows [T][n_in] (one OpenMP thread per token); scoring 0 softmax,
+ * 1 sigmoid; idx/w [T][n_used] */
+void orc_route_batch(int scoring, const float* X, int T, const float* gate_inp, const float* probs_b,
+                     int n_exp, int n_used, int n_group, int n_group_used, int norm_w, float w_scale,
+                     int n_in, int* idx, float* w);
 /* stable top-k (ties -> lower index)                   (src/m6_layer.c:808-821) */
 void orc_topk(const float* v, int n, int k, int* out);
 
@@ -57,6 +62,10 @@ void orc_granite_shexp(const float* x, const uint64_t* shp, const int* shc, int 
                        float* out);
 void orc_shared_add(const float* x, const uint8_t* g, const uint8_t* u, const uint8_t* d,
                     int cg, int cu, int cd, int sh_ff, int n_in, int n_out, float* out);
+
+/* orc_shared_add over T token rows (one OpenMP thread per token) */
+void orc_shared_add_batch(const float* X, int T, const uint8_t* g, const uint8_t* u, const uint8_t* d,
+                          int cg, int cu, int cd, int sh_ff, int n_in, int n_out, float* out);
 
 /* chunked prefill: stable counting sort by expert, per-expert gate/up/SwiGLU/down, per-token
  * combine in k order                                    (src/m6_moe_tok.c:44-161) */

@@ -71,6 +71,8 @@ class Port:
         L.orc_route_sigmoid.argtypes = [_f, _f, _f, ct.c_int, ct.c_int, ct.c_int, ct.c_int,
                                         ct.c_int, ct.c_float, ct.c_int, _i, _f, _f]
         L.orc_route_sigmoid.restype = None
+        L.orc_route_batch.argtypes = [ct.c_int, _f, ct.c_int, _f, _f] + [ct.c_int] * 5 + [ct.c_float, ct.c_int, _i, _f]
+        L.orc_route_batch.restype = None
         L.orc_granite_moe.argtypes = [_f, _u64, _i, _f] + [ct.c_int] * 5 + [_f]
         L.orc_granite_moe.restype = None
         L.orc_bailing_moe.argtypes = [_f, _u64, _i, _f, _f] + [ct.c_int] * 5 + [ct.c_float] + [ct.c_int] * 3 + [_f]
@@ -79,6 +81,8 @@ class Port:
         L.orc_granite_shexp.restype = None
         L.orc_shared_add.argtypes = [_f, _u8, _u8, _u8] + [ct.c_int] * 6 + [_f]
         L.orc_shared_add.restype = None
+        L.orc_shared_add_batch.argtypes = [_f, ct.c_int, _u8, _u8, _u8] + [ct.c_int] * 6 + [_f]
+        L.orc_shared_add_batch.restype = None
         L.orc_moe_tok.argtypes = [_f, _i, _f, _u64, _i] + [ct.c_int] * 6 + [_f]
         L.orc_moe_tok.restype = None
         L.orc_q8k_quantize.argtypes = [_f, ct.c_int, _f, _i8, _i16]
@@ -111,21 +115,18 @@ class Port:
 
     # -- routers --
     def route(self, layer, x):
-        """(idx int32[T, K], w fp32[T, K]) for every token row of x, C-router semantics."""
+        """(idx int32[T, K], w fp32[T, K]) for every token row of x, C-router semantics (one
+        OpenMP thread per token)."""
         x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
         T = x.shape[0]
         idx = np.zeros((T, layer.n_used), np.int32)
         w = np.zeros((T, layer.n_used), np.float32)
         gi = np.ascontiguousarray(layer.gate_inp, np.float32)
-        for t in range(T):
-            if layer.scoring == "softmax":
-                self.L.orc_route_softmax(pf(x[t]), pf(gi), layer.n_exp, layer.n_used, layer.hidden,
-                                         pi(idx[t]), pf(w[t]), None)
-            else:
-                pb = pf(layer.probs_b) if layer.probs_b is not None else None
-                self.L.orc_route_sigmoid(pf(x[t]), pf(gi), pb, layer.n_exp, layer.n_used,
-                                         layer.n_group, layer.n_group_used, layer.norm_w,
-                                         ct.c_float(layer.w_scale), layer.hidden, pi(idx[t]), pf(w[t]), None)
+        sig = layer.scoring != "softmax"
+        pb = pf(layer.probs_b) if sig and layer.probs_b is not None else None
+        self.L.orc_route_batch(1 if sig else 0, pf(x), T, pf(gi), pb, layer.n_exp, layer.n_used,
+                               layer.n_group if sig else 1, layer.n_group_used, layer.norm_w,
+                               ct.c_float(layer.w_scale if sig else 0.0), layer.hidden, pi(idx), pf(w))
         return idx, w
 
     # -- layers --
@@ -148,12 +149,13 @@ class Port:
         return out
 
     def shared_add(self, layer, x, out):
+        """out[t] += ungated shared expert(x[t]) for every row (one OpenMP thread per row)."""
         x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
-        for t in range(x.shape[0]):
-            self.L.orc_shared_add(pf(x[t]), layer.sh_gate.ctypes.data_as(_u8),
-                                  layer.sh_up.ctypes.data_as(_u8), layer.sh_down.ctypes.data_as(_u8),
-                                  layer.code_gu, layer.code_gu, layer.code_d, layer.shared_inter,
-                                  layer.hidden, layer.hidden, pf(out[t]))
+        assert out.flags.c_contiguous and out.dtype == np.float32
+        self.L.orc_shared_add_batch(pf(x), x.shape[0], layer.sh_gate.ctypes.data_as(_u8),
+                                    layer.sh_up.ctypes.data_as(_u8), layer.sh_down.ctypes.data_as(_u8),
+                                    layer.code_gu, layer.code_gu, layer.code_d, layer.shared_inter,
+                                    layer.hidden, layer.hidden, pf(out))
         return out
 
     def moe_tok(self, layer, X, order, wtop):
@@ -275,6 +277,27 @@ class Ref:
                            X.ctypes.data, order.ctypes.data, wtop.ctypes.data,
                            ep.ctypes.data, ec.ctypes.data, T, K, F, H, H, layer.n_exp,
                            out.ctypes.data, work.ctypes.data, iwork.ctypes.data)
+        return out
+
+    def shared_add(self, layer, X, out):
+        """out[t] += the layer's ungated shared expert on X[t], computed by the reference's own
+        m6_moe_tok with the shared expert as the only expert (order 0, weight 1: the combine's
+        fused multiply-add then adds y exactly); the reference adds it in src/m6_engine.c:346."""
+        X = np.ascontiguousarray(X, np.float32)
+        T = X.shape[0]
+        F, H = layer.shared_inter, layer.hidden
+        ep = np.array([layer.sh_gate.ctypes.data, layer.sh_up.ctypes.data, layer.sh_down.ctypes.data], np.uint64)
+        ec = np.array([layer.code_gu, layer.code_gu, layer.code_d], np.int32)
+        order = np.zeros(T, np.int32)
+        wtop = np.ones(T, np.float32)
+        y = np.zeros((T, H), np.float32)
+        work = np.empty(T * (H + 3 * F + H), np.float32)
+        iwork = np.empty(T * 2 + 2, np.int32)
+        wbuf = np.zeros(self.nth * 8208 * max(1, (max(H, F) + 8207) // 8208), np.float32)
+        self.MT.m6_moe_tok(self.dq_fp, self.ga_fp, wbuf.ctypes.data, X.ctypes.data, order.ctypes.data,
+                           wtop.ctypes.data, ep.ctypes.data, ec.ctypes.data, T, 1, F, H, H, 1,
+                           y.ctypes.data, work.ctypes.data, iwork.ctypes.data)
+        out += y
         return out
 
     def gemvn(self, code, x, x_stride, W, idx, per, n_out_e, n_in):
