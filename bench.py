@@ -500,18 +500,25 @@ def run_workload(name, args, ctx, headline):
         e2e_s = float(t.item())
     e2e_val = tokens_step * steps / e2e_s
 
-    # ---- roofline of the dominant kernel (gate/up grouped GEMM) ----
+    # ---- roofline of the dominant kernel: the gate/up grouped GEMM, or the fused decode layer ----
     hbm, bf16, src = peaks()
-    gu_ms = prof["gateup"][0] / max(prof["gateup"][1], 1)
-    gu_gbs = work["gateup_bytes"] / (gu_ms / 1e3) / 1e9
-    gu_tfs = work["gateup_flops"] / (gu_ms / 1e3) / 1e12
+    fused = prof.get("fused", (0.0, 0))[1] > 0
+    if fused:   # one kernel does the whole layer: its bytes are the layer's
+        gu_ms = prof["fused"][0] / prof["fused"][1]
+        kbytes, kflops, kname = work["bytes"], work["flops"], "fused decode layer (routing through combine, one launch)"
+    else:
+        gu_ms = prof["gateup"][0] / max(prof["gateup"][1], 1)
+        kbytes, kflops, kname = work["gateup_bytes"], work["gateup_flops"], "gateup (grouped dequant GEMM, gate+up+SwiGLU)"
+    gu_ms = max(gu_ms, 1e-9)
+    gu_gbs = kbytes / (gu_ms / 1e3) / 1e9
+    gu_tfs = kflops / (gu_ms / 1e3) / 1e12
     tensor_bound = name in ("cfg4_ling_prefill", "cfg5_k2_prefill_zipf")
-    roof = {"kernel": "gateup (grouped dequant GEMM, gate+up+SwiGLU)", "bound": "tensor" if tensor_bound else "hbm",
+    roof = {"kernel": kname, "bound": "tensor" if tensor_bound else "hbm",
             "achieved": gu_tfs if tensor_bound else gu_gbs, "peak": bf16 if tensor_bound else hbm,
             "unit": "TFLOP/s" if tensor_bound else "GB/s",
             "frac": (gu_tfs / bf16) if tensor_bound else (gu_gbs / hbm),
             "traffic": profiled_traffic(name) if world == 1 else None,
-            "algorithmic_bytes": work["gateup_bytes"], "algorithmic_flops": work["gateup_flops"],
+            "algorithmic_bytes": kbytes, "algorithmic_flops": kflops,
             "peak_source": src + (" (cuBLAS bf16 burst; the kernel runs fp16 operands)" if tensor_bound else
                                   " (copy bandwidth)"),
             "kernel_ms": gu_ms, "kernel_gbs": gu_gbs, "kernel_tflops": gu_tfs,

@@ -107,6 +107,8 @@ _SIGS = {
                                    ct.c_int),
     "draco_b200_set_act_mode": ([ct.c_int], ct.c_int),
     "draco_b200_set_gemm_path": ([ct.c_int], ct.c_int),
+    "draco_b200_set_fused_decode": ([ct.c_int], ct.c_int),
+    "draco_b200_test_fused_barrier_extra": ([ct.c_int], ct.c_int),
     "draco_b200_profile": ([ct.c_int], ct.c_int),
     "draco_b200_profile_read": ([ct.POINTER(ct.c_double), ct.POINTER(ct.c_long), ct.c_int], ct.c_int),
     "draco_b200_launch_count": ([], ct.c_long),
@@ -139,7 +141,7 @@ def lib() -> ct.CDLL:
     return _LIB
 
 
-PHASES = ("route", "dispatch", "gateup", "down", "shared", "combine", "gather")
+PHASES = ("route", "dispatch", "gateup", "down", "shared", "combine", "gather", "fused")
 
 
 def profile(enable: bool) -> None:

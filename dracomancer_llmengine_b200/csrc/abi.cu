@@ -58,7 +58,7 @@ long g_launches = 0;          // kernels this library launched (all devices)
 
 // Optional per-phase device timing: CUDA events recorded around each phase on the launching
 // stream, resolved when read.
-enum Phase { kRoute = 0, kDispatch, kGateUp, kDown, kShared, kCombine, kGather, kPhases };
+enum Phase { kRoute = 0, kDispatch, kGateUp, kDown, kShared, kCombine, kGather, kFused, kPhases };
 bool g_prof = false;
 struct PendingEv {
     int phase;
@@ -728,8 +728,22 @@ struct LayerBufs {
     int* item_tiles = nullptr;     // dispatch scratch for the item lists
     int4 *items_sh_gu = nullptr, *items_sh_dn = nullptr;   // shared expert on the tensor-core path
     int* n_items_sh = nullptr;
+    int* fd_ctl = nullptr;         // fused decode: 2 grid barrier words, routing status, GEMV status
     bool use_tc = false, sh_tc = false;
 };
+
+// the fused single-launch decode layer (DRACO_B200_FUSED_DECODE=0 or draco_b200_set_fused_decode
+// turn it off); g_fd_extra: test hook, grid barrier arrivals the fused kernel waits for beyond
+// its own blocks (a block that never arrives)
+int g_fused_decode = -1;
+int g_fd_extra = 0;
+bool fused_decode_enabled() {
+    if (g_fused_decode < 0) {
+        const char* e = getenv("DRACO_B200_FUSED_DECODE");
+        g_fused_decode = e ? (atoi(e) != 0) : 1;
+    }
+    return g_fused_decode != 0;
+}
 
 bool want_tc(const LayerArgs& a, int T) {
     const int mode = gemm_path();
@@ -738,7 +752,8 @@ bool want_tc(const LayerArgs& a, int T) {
     return T * a.K >= tc_min_assignments();
 }
 
-int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
+// extra_bytes > 0: that many more bytes for the caller at *extra_off
+int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, size_t extra_bytes = 0, size_t* extra_off = nullptr) {
     const size_t n = (size_t)T * a.K;
     Carver cv;
     const size_t o_x = cv.take<float>((size_t)T * a.n_in), o_out = cv.take<float>((size_t)T * a.n_out);
@@ -767,11 +782,14 @@ int carve_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b) {
     const size_t o_sgu = cv.take<int4>(b.sh_tc ? sh_tiles * tc_tiles_gateup(a.sh_ff) : 0);
     const size_t o_sdn = cv.take<int4>(b.sh_tc ? sh_tiles * tc_tiles_down(a.n_out) : 0);
     const size_t o_nsh = cv.take<int>(2);
+    const size_t o_fd = cv.take<int>(4);
+    if (extra_bytes) *extra_off = cv.take<char>(extra_bytes);
     if (int rc = ensure_ws(c, cv.off)) return rc;
     char* w = c->ws;
     b.items_sh_gu = (int4*)(w + o_sgu);
     b.items_sh_dn = (int4*)(w + o_sdn);
     b.n_items_sh = (int*)(w + o_nsh);
+    b.fd_ctl = (int*)(w + o_fd);
     b.xs_h = (__half*)(w + o_xs);
     b.act_h = (__half*)(w + o_ah);
     b.items_gu = (int4*)(w + o_igu);
@@ -843,6 +861,79 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         g_launches += 1;
         b.x = b.x_ws;
         xh = false;
+    }
+    // decode batches: the whole layer (routing, experts, combine, shared expert) in one launch
+    const bool sh_ok = !a.sh || (a.sh->aligned16 && a.sh->cg == a.tab->cg && a.sh->cu == a.tab->cu &&
+                                 a.sh->cd == a.tab->cd && a.sh->q6s == a.tab->q6s &&
+                                 dec_supported(a.sh->cg, a.sh->cu, a.sh->cd, a.sh_ff, a.n_in, a.n_out, a.sh->q6s));
+    if (!a.no_routed && !xh && !b.use_tc && g_act_mode == 0 && fused_decode_enabled() && T <= 8 && T * a.K <= 64 &&
+        a.tab->aligned16 && a.tab->cg == a.tab->cu && sh_ok &&
+        dec_supported(a.tab->cg, a.tab->cu, a.tab->cd, a.inter, a.n_in, a.n_out, a.tab->q6s)) {
+        FusedDecodeArgs f{};
+        f.tab = ExpertTable{a.tab->d_w};
+        if (a.sh) {
+            f.sh_g = a.sh->base[0];
+            f.sh_u = a.sh->base[1];
+            f.sh_d = a.sh->base[2];
+            f.sh_ff = a.sh_ff;
+        }
+        f.W = a.d_gi;
+        f.rp = a.rp;   // scoring etc. (used only when the router runs here)
+        f.rp.n_exp = a.E;
+        f.rp.n_used = a.K;
+        f.rp.n_in = a.n_in;
+        f.X = b.x;
+        f.T = T;
+        f.F = a.inter;
+        f.n_out = a.n_out;
+        f.out = b.out;
+        f.order = rb.order;
+        f.wtop = rb.wtop;
+        f.logits = rb.logits;
+        f.act = b.act;
+        f.act_sh = b.act_sh;
+        f.bar = reinterpret_cast<unsigned*>(b.fd_ctl);
+        f.route_err = b.fd_ctl + 2;
+        f.status = b.fd_ctl + 3;
+        f.q6s = a.tab->q6s;
+        f.bar_extra = g_fd_extra;
+        static unsigned long long* fd_stamps = nullptr;   // DRACO_B200_FD_STATS=1: phase timestamps
+        if (!fd_stamps && env_flag("DRACO_B200_FD_STATS")) cudaMallocManaged(&fd_stamps, sizeof(unsigned long long) * 8 * 4096);
+        f.stamps = fd_stamps;
+        CK(cudaMemsetAsync(b.fd_ctl, 0, 4 * sizeof(int), s));
+        int rc;
+        {
+            PhaseScope ps(kFused, s);
+            rc = launch_fused_decode(f, a.tab->cg, a.tab->cu, a.tab->cd, s);
+        }
+        if (rc == 0) {
+            rb.err = f.route_err;   // the status words the synchronous calls read back
+            b.tc_err = f.status;
+            g_launches += 1;
+            if (fd_stamps) {
+                // per phase: median and max over the blocks of the time since the block started
+                cudaStreamSynchronize(s);
+                int G = 0;
+                while (G < 4096 && fd_stamps[(size_t)G * 8] != 0) G++;
+                fprintf(stderr, "[fused decode stats] blocks=%d", G);
+                static const char* nm[7] = {"start", "A", "bar1", "S", "B", "bar2", "C"};
+                for (int i = 1; i < 7; i++) {
+                    std::vector<double> v;
+                    for (int g = 0; g < G; g++)
+                        if (fd_stamps[(size_t)g * 8 + i]) v.push_back((fd_stamps[(size_t)g * 8 + i] - fd_stamps[(size_t)g * 8]) * 1e-3);
+                    std::sort(v.begin(), v.end());
+                    if (!v.empty()) fprintf(stderr, " %s=%.1f/%.1fus", nm[i], v[v.size() / 2], v.back());
+                }
+                fprintf(stderr, "\n");
+                memset(fd_stamps, 0, sizeof(unsigned long long) * 8 * 4096);
+            }
+            return 0;
+        }
+        if (rc < 0) {
+            set_err("fused decode launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+            return -3;
+        }
+        // not applicable on this device: the separate kernels below
     }
     if (a.no_routed) {
         CK(cudaMemsetAsync(rb.err, 0, sizeof(int), s));
@@ -1378,6 +1469,178 @@ void m6_moe_tok(m6_dequant_fn DQ, m6_gemm_auto_fn GA, float* gwbuf, const float*
         fail_void("m6_moe_tok", dev_kind(out) ? nullptr : out, (size_t)(T > 0 && n_out > 0 ? (size_t)T * n_out : 0));
 }
 
+// ---- caller-routed single-token variants (src/m6_layer.c:520-690): the table holds exactly the
+// n_exp selected experts, wtop their weights; out = sum_j wtop[j] * expert_j(x0), j ascending
+static int moe_batch_impl(const float* x0, const uint64_t* ptrs, const int* codes, const float* wtop, int n_exp,
+                          int inter, int n_in, int n_out, float* out) {
+    if (n_exp <= 0 || n_exp > 64) {
+        set_err("m6_moe_batch: 1 <= n_exp <= 64 selected experts expected, got %d", n_exp);
+        return -1;
+    }
+    int order[64];
+    for (int j = 0; j < n_exp; j++) order[j] = j;
+    return moe_tok_impl(x0, order, wtop, ptrs, codes, 1, n_exp, inter, n_in, n_out, n_exp, out);
+}
+
+void m6_moe_batch(const float* x0, const uint64_t* ptrs, const int* codes, const float* wtop, int n_exp, float* out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (moe_batch_impl(x0, ptrs, codes, wtop, n_exp, 512, 2048, 2048, out)) fail_void("m6_moe_batch", out, 2048);
+}
+
+void m6_moe_batch2(const float* x0, const uint64_t* ptrs, const int* codes, const float* wtop, int n_exp,
+                   const uint64_t* sh_ptrs, const int* sh_codes, const float* sh_gate_inp, float* scratch,
+                   float* out) {
+    (void)scratch;
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = moe_batch_impl(x0, ptrs, codes, wtop, n_exp, 512, 2048, 2048, out);
+    // + sigmoid(x0 . sh_gate_inp) * shared expert; without a gate row the reference's gate is 0
+    if (rc == 0 && sh_gate_inp && sh_ptrs && sh_codes) {
+        const uint64_t shp[4] = {sh_ptrs[0], sh_ptrs[1], sh_ptrs[2], (uint64_t)(uintptr_t)sh_gate_inp};
+        const int shc[4] = {sh_codes[0], sh_codes[1], sh_codes[2], DRACO_CODE_F32};
+        std::vector<float> g(2048);
+        rc = shexp_impl(x0, shp, shc, nullptr, nullptr, g.data(), 512, 2048);
+        if (rc == 0)
+            for (int i = 0; i < 2048; i++) out[i] += g[i];
+    }
+    if (rc) fail_void("m6_moe_batch2", out, 2048);
+}
+
+void m6_moe_batch3(const float* x0, const uint64_t* ptrs, const int* codes, const float* wtop, int n_exp, int inter,
+                   int n_in, int n_out, float* out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (moe_batch_impl(x0, ptrs, codes, wtop, n_exp, inter, n_in, n_out, out))
+        fail_void("m6_moe_batch3", out, (size_t)(n_out > 0 ? n_out : 0));
+}
+
+void m6_moe_batch4(const float* x0, const uint64_t* ptrs, const int* codes, const float* wtop, int n_exp, int inter,
+                   int n_in, int n_out, float* scratch, float* out) {
+    (void)scratch;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (moe_batch_impl(x0, ptrs, codes, wtop, n_exp, inter, n_in, n_out, out))
+        fail_void("m6_moe_batch4", out, (size_t)(n_out > 0 ? n_out : 0));
+}
+
+// ---- top-1 MoE with a learned router MLP (src/m6_engine.c:795-835) ----
+static int zaya_impl(const float* xn, const M6ZayaMoeP* p, float* out) {
+    const int H = p->hidden, RH = p->hidden2, F = p->inter, NE = p->nexp;
+    if (H <= 0 || RH <= 0 || F <= 0 || NE <= 0 || NE > 512 || p->nclass <= 0 || p->nclass > 1024) {
+        set_err("m6_zaya_moe_op: unsupported shape hidden=%d hidden2=%d inter=%d nexp=%d nclass=%d", H, RH, F, NE,
+                p->nclass);
+        return -1;
+    }
+    auto f16or32 = [](int c) { return c == 9 || c == 7; };
+    if (!f16or32(p->cdown) || !f16or32(p->cfc1) || !f16or32(p->cfc2) || !f16or32(p->cout)) {
+        set_err("m6_zaya_moe_op: router matrices must be F32 (9) or F16 (7)");
+        return -1;
+    }
+    Ctx* c = get_ctx();
+    if (!c) return -3;
+    const double t0 = now_s();
+    const int cg = p->exp_cg[0], cd = p->exp_cd[0];
+    const size_t rbg = row_bytes(cg, H);
+    std::vector<uint64_t> ep(3 * (size_t)NE);
+    std::vector<int> ec(3 * (size_t)NE);
+    for (int e = 0; e < NE; e++) {
+        if (p->exp_cg[e] != cg || p->exp_cd[e] != cd) {
+            set_err("m6_zaya_moe_op: experts with different formats are unsupported");
+            return -1;
+        }
+        // the fused gate|up matrix of 2*inter rows: gate rows first, then up
+        ep[3 * e] = p->exp_gp[e];
+        ep[3 * e + 1] = p->exp_gp[e] + (uint64_t)F * rbg;
+        ep[3 * e + 2] = p->exp_dp[e];
+        ec[3 * e] = ec[3 * e + 1] = cg;
+        ec[3 * e + 2] = cd;
+    }
+    auto esz = [](int code) { return code == 9 ? 4 : 2; };
+    ZayaRouterArgs z{};
+    LayerArgs a;
+    a.E = NE;
+    a.K = 1;
+    a.inter = F;
+    a.n_in = H;
+    a.n_out = H;
+    unsigned long gen0 = 0;
+    for (int attempt = 0; attempt < 3; attempt++) {
+        gen0 = c->gen;
+        // the whole fused gate|up tensors first (gate and up halves then resolve inside them):
+        // one range when the experts are stacked (base + e * per), else one per expert
+        if (cg != DRACO_CODE_Q6_K) {
+            const uint64_t base = p->exp_gp[0], per = NE > 1 ? p->exp_gp[1] - base : 0;
+            bool stacked = NE > 1 && p->exp_gp[1] > base && per >= 2 * (uint64_t)F * rbg;
+            for (int e = 2; stacked && e < NE; e++) stacked = p->exp_gp[e] == base + per * (uint64_t)e;
+            if (stacked) {
+                if (!dev_range(c, (const void*)(uintptr_t)base, per * (NE - 1) + 2 * (size_t)F * rbg)) return -1;
+            } else {
+                for (int e = 0; e < NE; e++)
+                    if (!dev_range(c, (const void*)(uintptr_t)p->exp_gp[e], 2 * (size_t)F * rbg)) return -1;
+            }
+        }
+        z.wdown = dev_range(c, p->wdown, (size_t)RH * H * esz(p->cdown));
+        z.wfc1 = dev_range(c, p->wfc1, (size_t)RH * RH * esz(p->cfc1));
+        z.wfc2 = dev_range(c, p->wfc2, (size_t)RH * RH * esz(p->cfc2));
+        z.wout = dev_range(c, p->wout, (size_t)p->nclass * RH * esz(p->cout));
+        z.bdown = (const float*)dev_range(c, p->bdown, sizeof(float) * RH);
+        z.bfc1 = (const float*)dev_range(c, p->bfc1, sizeof(float) * RH);
+        z.bfc2 = (const float*)dev_range(c, p->bfc2, sizeof(float) * RH);
+        z.rnorm = (const float*)dev_range(c, p->rnorm, sizeof(float) * RH);
+        z.bal = (const float*)dev_range(c, p->bal, sizeof(float) * p->nclass);
+        z.eda_scale = p->eda_scale ? (const float*)dev_range(c, p->eda_scale, sizeof(float) * RH) : nullptr;
+        if (!z.wdown || !z.wfc1 || !z.wfc2 || !z.wout || !z.bdown || !z.bfc1 || !z.bfc2 || !z.rnorm || !z.bal ||
+            (p->eda_scale && !z.eda_scale))
+            return -1;
+        a.tab = get_table(c, ep.data(), ec.data(), NE, F, H, H, (uintptr_t)p->exp_gp);
+        if (!a.tab) return -1;
+        if (c->gen == gen0) break;
+    }
+    if (c->gen != gen0) {
+        set_err("weight ranges keep changing under the call");
+        return -1;
+    }
+    LayerBufs b;
+    size_t o_z = 0;   // router scratch: state in, state out, rh
+    if (int rc = carve_layer(c, a, 1, b, 3 * align_up(sizeof(float) * RH, 256), &o_z)) return rc;
+    float* d_si = (float*)(c->ws + o_z);
+    float* d_so = (float*)(c->ws + o_z + align_up(sizeof(float) * RH, 256));
+    cudaStream_t s = c->stream;
+    CK(cudaMemcpyAsync(b.x, xn, sizeof(float) * H, cudaMemcpyHostToDevice, s));
+    if (p->eda_scale) CK(cudaMemcpyAsync(d_si, p->rh_state, sizeof(float) * RH, cudaMemcpyHostToDevice, s));
+    z.cdown = p->cdown;
+    z.cfc1 = p->cfc1;
+    z.cfc2 = p->cfc2;
+    z.cout = p->cout;
+    z.x = b.x;
+    z.state_in = d_si;
+    z.state_out = d_so;
+    z.rh = (float*)(c->ws + o_z + 2 * align_up(sizeof(float) * RH, 256));
+    z.H = H;
+    z.RH = RH;
+    z.nclass = p->nclass;
+    z.nexp = NE;
+    z.iskip = p->iskip;
+    z.order = b.rb.order;
+    z.wtop = b.rb.wtop;
+    if (launch_zaya_router(z, s)) {
+        set_err("m6_zaya_moe_op: router launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return -3;
+    }
+    g_launches += 2;
+    if (int rc = run_layer(c, a, 1, b, s)) return rc;
+    CK(cudaMemcpyAsync(out, b.out, sizeof(float) * H, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(p->rh_state, d_so, sizeof(float) * RH, cudaMemcpyDeviceToHost, s));
+    CK(cudaMemsetAsync(b.rb.err, 0, sizeof(int), s));   // routing came from the router MLP
+    if (int rc = check_route_err(c, b, s)) return rc;
+    m6_prof_t[23] += now_s() - t0;
+    m6_prof_n[23]++;
+    return 0;
+}
+
+void m6_zaya_moe_op(const float* xn, void* pv, float* out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const M6ZayaMoeP* p = (const M6ZayaMoeP*)pv;
+    if (!p || zaya_impl(xn, p, out)) fail_void("m6_zaya_moe_op", out, p && p->hidden > 0 ? (size_t)p->hidden : 0);
+}
+
 static int gemvn_impl(int code, const float* x, long x_stride, const uint8_t* W, const int* idx, long per,
                       int n_out_e, int n_in, int n_exp, float* y) {
     const int nb = n_in / 256;
@@ -1859,6 +2122,26 @@ int draco_b200_set_gemm_path(int mode) {
     std::lock_guard<std::mutex> lk(g_mu);
     const int o = gemm_path();
     if (mode >= 0 && mode <= 2) g_gemm_path = mode;
+    return o;
+}
+
+int draco_b200_set_fused_decode(int on) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int o = fused_decode_enabled() ? 1 : 0;
+    if (on == 0 || on == 1) {
+        g_fused_decode = on;
+        if (Ctx* c = get_ctx()) drop_graphs(c);   // captured calls hold the previous choice
+    }
+    return o;
+}
+
+int draco_b200_test_fused_barrier_extra(int n) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int o = g_fd_extra;
+    if (n >= 0) {
+        g_fd_extra = n;
+        if (Ctx* c = get_ctx()) drop_graphs(c);
+    }
     return o;
 }
 

@@ -13,6 +13,9 @@
 // (lane partials + tree), so results match the reference to rounding, not bit for bit.
 #include "kernels.cuh"
 #include "mbar.cuh"
+#include "select.cuh"
+
+#include <algorithm>
 
 namespace draco {
 namespace {
@@ -108,11 +111,13 @@ __device__ __forceinline__ void decode8(const uint8_t* blk, const float2* tab, i
     }
 }
 
-template <int CODE>
+// L2ONLY: the rows were written by other blocks of the same launch: load through L2 only
+template <int CODE, bool L2ONLY = false>
 __device__ __forceinline__ void load_x8(const float* __restrict__ x, int sb, int lane, float v[8]) {
     const float* b = x + sb * 256 + x_pos<CODE>(lane);
-    const float4 a = *reinterpret_cast<const float4*>(b);
-    const float4 c = *reinterpret_cast<const float4*>(b + x_gap<CODE>());
+    const float4 a = L2ONLY ? __ldcg(reinterpret_cast<const float4*>(b)) : *reinterpret_cast<const float4*>(b);
+    const float4 c = L2ONLY ? __ldcg(reinterpret_cast<const float4*>(b + x_gap<CODE>()))
+                            : *reinterpret_cast<const float4*>(b + x_gap<CODE>());
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
 }
@@ -148,7 +153,7 @@ __device__ __forceinline__ void build_scales(const uint8_t* tile, int rows, int 
 }
 
 // dot products of the warp's rpw rows (of up to two matrices) with NT token rows
-template <int CG, int CU, bool TWO, int NT>
+template <int CG, int CU, bool TWO, int NT, bool L2ONLY = false>
 __device__ __forceinline__ void rows_dot(const uint8_t* sg, const float2* tg, const uint8_t* su, const float2* tu,
                                          uint32_t rbg, uint32_t rbu, int bg, int bu, int nb, int r0, int rpw,
                                          const float* const (&xr)[2], int lane, float (&ag)[4][2], float (&au)[4][2]) {
@@ -160,8 +165,8 @@ __device__ __forceinline__ void rows_dot(const uint8_t* sg, const float2* tg, co
         float xg[NT][8], xu[NT][8];
 #pragma unroll
         for (int j = 0; j < NT; j++) {
-            load_x8<CG>(xr[j], sb, lane, xg[j]);
-            if (TWO && CG != CU) load_x8<CU>(xr[j], sb, lane, xu[j]);
+            load_x8<CG, L2ONLY>(xr[j], sb, lane, xg[j]);
+            if (TWO && CG != CU) load_x8<CU, L2ONLY>(xr[j], sb, lane, xu[j]);
         }
 #pragma unroll
         for (int r = 0; r < 4; r++) {
@@ -299,6 +304,443 @@ int tile_rows(int rows, uint32_t row_bytes_) {
     return rows % rt ? 0 : rt;
 }
 
+// ------------------------------------------------------------------------------------------
+// Fused decode layer: the whole MoE layer of a small token batch (T <= 8, T*K <= 64) in ONE
+// cooperative launch of one or two blocks per SM:
+//   phase A  router logits: the T*E exact-order chains (k ascending, rounded product then
+//            rounded add, src/m6_layer.c:775-783) spread over the blocks, one lane per chain,
+//            router rows and token rows streamed through a shared-memory ring by bulk copies;
+//   -- grid barrier 1 --
+//   phase S  every block selects the routing of all T tokens itself from the logits (the
+//            router's warp-level selection, bit-exact) and builds the active expert list;
+//   phase B  gate/up + SwiGLU tiles of (active expert, row tile), plus the shared expert's;
+//   -- grid barrier 2 (compute warps only: the producer warp is already streaming phase C's
+//            weight tiles, which do not depend on the activations) --
+//   phase C  down tiles of every active expert for a row tile, the expert rows y kept in shared
+//            memory, then the k-ascending fused combine (+ shared expert) of that row tile.
+// One producer warp issues the bulk copies of every job (router chunk, gate+up tile, down tile)
+// into a ring of slots; four compute warps decode and reduce (the dec_* kernels' row code).
+// Every wait is bounded: an mbarrier wait gives up after 2 s, a grid barrier after 1 s; a block
+// that gives up raises a status bit (0x200 copy, 0x1000 grid barrier), stops, and waits for its
+// own copies in flight before it exits.
+// ------------------------------------------------------------------------------------------
+constexpr int kFdMaxTokens = 8;
+constexpr int kFdMaxAssign = 64;
+constexpr int kFdCompute = 4;
+constexpr int kFdThreads = 32 * (kFdCompute + 1);
+constexpr int kFdKC = 128;                 // router k-chunk (floats)
+constexpr int kFdRS = kFdKC + 4;           // padded row stride of a chunk in shared memory
+constexpr int kFdMaxSlots = 4;
+constexpr uint64_t kFdGridWaitNs = 1000000000ull;
+
+__device__ __forceinline__ void fd_compute_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kFdCompute) : "memory"); }
+
+// grid barrier over all blocks (called by one thread); false on timeout
+__device__ __forceinline__ bool fd_grid_arrive_wait(unsigned* ctr, unsigned target) {
+    __threadfence();
+    atomicAdd(ctr, 1u);
+    const uint64_t t0 = sync::global_ns();
+    for (uint32_t i = 0;; i++) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+        if (v >= target) break;
+        if ((i & 15) == 15 && sync::global_ns() - t0 > kFdGridWaitNs) return false;
+    }
+    __threadfence();
+    return true;
+}
+
+template <int CODE>
+__device__ __forceinline__ void fd_scales(const uint8_t* tile, int rows, int nb, int bb, float2* tab, int tid,
+                                          int nth) {
+    for (int idx = tid; idx < rows * nb; idx += nth)
+        superblock_scales<CODE>(tile + (size_t)idx * bb, tab + (size_t)idx * scale_groups<CODE>());
+}
+
+// optional phase timestamps (DRACO_B200_FD_STATS): thread 0 of each block
+__device__ __forceinline__ void fd_stamp(const FusedDecodeArgs& a, int i) {
+    if (a.stamps && threadIdx.x == 0) a.stamps[(size_t)blockIdx.x * 8 + i] = sync::global_ns();
+}
+
+template <int CG, int CU, int CD, int NS>
+__global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArgs a) {
+    extern __shared__ __align__(128) uint8_t dsm[];
+    __shared__ uint64_t full[kFdMaxSlots], empty[kFdMaxSlots];
+    // s_cabort: written by compute threads (and thread 0 at the grid barriers) and read by them
+    // only after a barrier, so their decisions stay uniform; s_pabort: the producer's own
+    __shared__ volatile int s_cabort, s_pabort;
+    __shared__ int s_n_act, s_qc;
+    __shared__ int s_first[kFdMaxAssign];
+    const int E = a.rp.n_exp, K = a.rp.n_used, H = a.rp.n_in, T = a.T, F = a.F;
+    const int NA = T * K;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, b = blockIdx.x;
+    const int S = a.n_slots;
+    const bool sh = a.sh_ff > 0;
+    uint8_t* ring = dsm;
+    float* V = reinterpret_cast<float*>(dsm + (size_t)S * a.slot_bytes);      // [5][E]
+    float* gsm = V + (kFdCompute + 1) * E;                                      // [5][64]
+    int* s_order = reinterpret_cast<int*>(gsm + (kFdCompute + 1) * 64);          // [64]
+    float* s_wtop = reinterpret_cast<float*>(s_order + kFdMaxAssign);            // [64]
+    int* act_e = reinterpret_cast<int*>(s_wtop + kFdMaxAssign);                  // [64]
+    int* act_cnt = act_e + kFdMaxAssign;                                         // [64]
+    int* act_asg = act_cnt + kFdMaxAssign;                                       // [64][8]
+    float* ys = reinterpret_cast<float*>(act_asg + kFdMaxAssign * kFdMaxTokens);  // [(64+8)][rt_c]
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; i++) {
+            sync::mbar_init(&full[i], 1);
+            sync::mbar_init(&empty[i], 1);
+        }
+        sync::fence_init();
+        s_cabort = 0;
+        s_pabort = 0;
+        s_qc = 0;
+    }
+    __syncthreads();
+    fd_stamp(a, 0);
+    const bool producer = warp == kFdCompute;
+    const int ctid = threadIdx.x;   // compute thread id (warps 0..3)
+    uint32_t q = 0;                 // jobs issued (producer lane 0) / consumed (compute threads)
+
+    // producer (lane 0 of the producer warp): the next slot, nullptr after a failed wait or
+    // when the compute warps stopped
+    auto claim = [&]() -> uint8_t* {
+        const int sl = q % S;
+        if (s_cabort || s_pabort) return nullptr;
+        if (q >= (uint32_t)S && !sync::mbar_wait(&empty[sl], ((q / S) & 1) ^ 1)) {
+            atomicOr(a.status, 0x200);
+            s_pabort = 1;
+            return nullptr;
+        }
+        return ring + (size_t)sl * a.slot_bytes;
+    };
+    // compute threads: job q's slot, nullptr (uniformly) after a failed wait
+    auto take = [&]() -> uint8_t* {
+        const int sl = q % S;
+        if (!sync::mbar_wait(&full[sl], (q / S) & 1)) {
+            atomicOr(a.status, 0x200);
+            s_cabort = 1;
+        }
+        fd_compute_sync();
+        if (s_cabort) return nullptr;
+        return ring + (size_t)sl * a.slot_bytes;
+    };
+    auto release = [&]() {
+        fd_compute_sync();
+        if (ctid == 0)
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sync::smem_addr(&empty[q % S])) : "memory");
+        q++;
+    };
+
+    // ---------------------------------------------------------------- phase A: router logits
+    const int C = T * E;
+    const int nch = (a.W && b < C) ? (C - 1 - b) / G + 1 : 0;
+    const int n_chunks = H / kFdKC;
+    if (nch > 0) {
+        if (producer) {
+            if (lane == 0)
+                for (int ch = 0; ch < n_chunks; ch++) {
+                    uint8_t* dst = claim();
+                    if (!dst) break;
+                    const int sl = q % S;
+                    sync::mbar_expect_tx(&full[sl], (uint32_t)(nch + T) * kFdKC * 4);
+                    for (int i = 0; i < nch; i++) {
+                        const int e = (b + G * i) % E;
+                        sync::bulk_load(dst + (size_t)i * kFdRS * 4, a.W + (size_t)e * H + (size_t)ch * kFdKC,
+                                        kFdKC * 4, &full[sl]);
+                    }
+                    for (int t = 0; t < T; t++)
+                        sync::bulk_load(dst + (size_t)(nch + t) * kFdRS * 4, a.X + (size_t)t * H + (size_t)ch * kFdKC,
+                                        kFdKC * 4, &full[sl]);
+                    q++;
+                }
+        } else {
+            float acc = 0.f;
+            const int c = b + G * lane;
+            const int ct = c / E;
+            bool done = true;
+            for (int ch = 0; ch < n_chunks; ch++) {
+                const uint8_t* src = take();
+                if (!src) {
+                    done = false;
+                    break;
+                }
+                if (warp == 0 && lane < nch) {
+                    const float4* w4 = reinterpret_cast<const float4*>(src + (size_t)lane * kFdRS * 4);
+                    const float4* x4 = reinterpret_cast<const float4*>(src + (size_t)(nch + ct) * kFdRS * 4);
+#pragma unroll 8
+                    for (int k = 0; k < kFdKC / 4; k++) {
+                        const float4 w = w4[k], x = x4[k];
+                        acc = __fadd_rn(acc, __fmul_rn(x.x, w.x));
+                        acc = __fadd_rn(acc, __fmul_rn(x.y, w.y));
+                        acc = __fadd_rn(acc, __fmul_rn(x.z, w.z));
+                        acc = __fadd_rn(acc, __fmul_rn(x.w, w.w));
+                    }
+                }
+                release();
+            }
+            if (done && warp == 0 && lane < nch) a.logits[(size_t)ct * E + c % E] = acc;
+        }
+    }
+    // ---------------------------------------------------------------- grid barrier 1
+    __syncthreads();
+    fd_stamp(a, 1);
+    if (a.W && threadIdx.x == 0) {
+        if (s_cabort || s_pabort || !fd_grid_arrive_wait(a.bar, (unsigned)(G + a.bar_extra))) {
+            if (!s_cabort && !s_pabort) atomicOr(a.status, 0x1000);
+            s_cabort = 1;
+        }
+    }
+    __syncthreads();
+    bool ok = !s_cabort && !s_pabort;   // uniform over the block from here
+    fd_stamp(a, 2);
+    // ---------------------------------------------------------------- phase S: routing
+    if (ok) {
+        if (a.W) {
+            for (int t = warp; t < T; t += kFdCompute + 1) {
+                float* Vw = V + (size_t)warp * E;
+                for (int e = lane; e < E; e += 32) Vw[e] = __ldcg(a.logits + (size_t)t * E + e);
+                __syncwarp();
+                select_token<NS>(a.rp, Vw, s_order + t * K, s_wtop + t * K, a.route_err, Vw, gsm + warp * 64);
+                __syncwarp();
+            }
+        } else {
+            for (int i = threadIdx.x; i < NA; i += blockDim.x) {
+                s_order[i] = a.order[i];
+                s_wtop[i] = a.wtop[i];
+            }
+        }
+    }
+    __syncthreads();
+    if (ok && a.W && b == 0)
+        for (int i = threadIdx.x; i < NA; i += blockDim.x) {
+            a.order[i] = s_order[i];
+            a.wtop[i] = s_wtop[i];
+        }
+    // active experts ascending; per active expert its assignments in order (token ascending)
+    if (threadIdx.x < NA) {
+        const int i = threadIdx.x, e = ok ? s_order[i] : -1;
+        bool first = e >= 0 && e < E;
+        for (int j = 0; j < i && first; j++) first = s_order[j] != e;
+        s_first[i] = first;
+    }
+    __syncthreads();
+    if (threadIdx.x < NA && ok) {
+        const int i = threadIdx.x, e = s_order[i];
+        if (e >= 0 && e < E) {
+            int rank = 0, pos = 0, cnt = 0;
+            for (int j = 0; j < NA; j++) {
+                const int ej = s_order[j];
+                if (s_first[j] && ej < e) rank++;
+                if (ej == e) {
+                    cnt++;
+                    if (j < i) pos++;
+                }
+            }
+            if (s_first[i]) {
+                act_e[rank] = e;
+                act_cnt[rank] = cnt;
+            }
+            act_asg[rank * kFdMaxTokens + pos] = i;
+        }
+    }
+    if (threadIdx.x == 0) {
+        int n = 0;
+        for (int i = 0; i < NA; i++) n += s_first[i];
+        s_n_act = n;
+    }
+    __syncthreads();
+    fd_stamp(a, 3);
+    const int n_act = ok ? s_n_act : 0;
+    // ---------------------------------------------------------------- phases B and C
+    const int nb = H / 256, nbd = F / 256, nbds = sh ? a.sh_ff / 256 : 0;
+    const int bg = superblock_bytes(CG, a.q6s), bu = superblock_bytes(CU, a.q6s), bd = superblock_bytes(CD, a.q6s);
+    const uint32_t rbg = (uint32_t)(nb * bg), rbu = (uint32_t)(nb * bu);
+    const uint32_t rbd = (uint32_t)(nbd * bd), rbds = (uint32_t)(nbds * bd);
+    const int rt_b = a.rt_b, rt_c = a.rt_c;
+    const int tiles_f = F / rt_b, tiles_fs = sh ? a.sh_ff / rt_b : 0;
+    const int items_b = ok ? n_act * tiles_f + tiles_fs : 0;
+    const int items_c = ok ? a.n_out / rt_c : 0;
+    const int exp_c = n_act + (sh ? 1 : 0);
+    if (producer) {
+        // B jobs then C jobs, back to back (C's weight tiles do not wait for the activations)
+        if (lane == 0) {
+            bool go = true;
+            for (int j = b; j < items_b && go; j += G) {
+                uint8_t* dst = claim();
+                if (!dst) {
+                    go = false;
+                    break;
+                }
+                const uint8_t *g, *u;
+                if (j < n_act * tiles_f) {
+                    const int e = act_e[j / tiles_f];
+                    const size_t r0 = (size_t)(j % tiles_f) * rt_b;
+                    g = a.tab.w[3 * e] + r0 * rbg;
+                    u = a.tab.w[3 * e + 1] + r0 * rbu;
+                } else {
+                    const size_t r0 = (size_t)(j - n_act * tiles_f) * rt_b;
+                    g = a.sh_g + r0 * rbg;
+                    u = a.sh_u + r0 * rbu;
+                }
+                const int sl = q % S;
+                sync::mbar_expect_tx(&full[sl], (uint32_t)rt_b * (rbg + rbu));
+                sync::bulk_load(dst, g, rt_b * rbg, &full[sl]);
+                sync::bulk_load(dst + rt_b * rbg, u, rt_b * rbu, &full[sl]);
+                q++;
+            }
+            for (int j = b; j < items_c && go; j += G) {
+                for (int x = 0; x < exp_c; x++) {
+                    uint8_t* dst = claim();
+                    if (!dst) {
+                        go = false;
+                        break;
+                    }
+                    const bool shx = x == n_act;
+                    const uint32_t rb = shx ? rbds : rbd;
+                    const uint8_t* src = shx ? a.sh_d : a.tab.w[3 * act_e[x] + 2];
+                    const int sl = q % S;
+                    sync::mbar_expect_tx(&full[sl], (uint32_t)rt_c * rb);
+                    sync::bulk_load(dst, src + (size_t)j * rt_c * rb, rt_c * rb, &full[sl]);
+                    q++;
+                }
+            }
+        }
+    } else {
+        const int rpw = rt_b / kFdCompute, r0 = warp * rpw;
+        for (int j = b; j < items_b && ok; j += G) {
+            uint8_t* tile = take();
+            if (!tile) {
+                ok = false;
+                break;
+            }
+            const bool shx = j >= n_act * tiles_f;
+            const int ax = shx ? 0 : j / tiles_f;
+            const int tile_r = shx ? j - n_act * tiles_f : j % tiles_f;
+            const int cnt = shx ? T : act_cnt[ax];
+            uint8_t* sg = tile;
+            uint8_t* su = tile + rt_b * rbg;
+            float2* tg = reinterpret_cast<float2*>(tile + rt_b * (rbg + rbu));
+            float2* tu = tg + rt_b * nb * scale_groups<CG>();
+            fd_scales<CG>(sg, rt_b, nb, bg, tg, ctid, 32 * kFdCompute);
+            fd_scales<CU>(su, rt_b, nb, bu, tu, ctid, 32 * kFdCompute);
+            fd_compute_sync();
+            for (int tc = 0; tc < cnt; tc += 2) {
+                const int nt = min(2, cnt - tc);
+                const float* xr[2];
+                int slot[2];
+#pragma unroll
+                for (int jj = 0; jj < 2; jj++) {
+                    const int m = tc + min(jj, nt - 1);
+                    const int i = shx ? m : act_asg[ax * kFdMaxTokens + m];
+                    slot[jj] = i;
+                    xr[jj] = a.X + (size_t)(shx ? i : i / K) * H;
+                }
+                float ag[4][2], au[4][2];
+                if (nt == 2) rows_dot<CG, CU, true, 2>(sg, tg, su, tu, rbg, rbu, bg, bu, nb, r0, rpw, xr, lane, ag, au);
+                else rows_dot<CG, CU, true, 1>(sg, tg, su, tu, rbg, rbu, bg, bu, nb, r0, rpw, xr, lane, ag, au);
+#pragma unroll
+                for (int r = 0; r < 4; r++) {
+                    if (r < rpw) {
+#pragma unroll
+                        for (int jj = 0; jj < 2; jj++) {
+                            if (jj < nt) {
+                                const float gv = warp_sum(ag[r][jj]), uv = warp_sum(au[r][jj]);
+                                const int row = tile_r * rt_b + r0 + r;
+                                if (lane == 0) {
+                                    if (shx) a.act_sh[(size_t)slot[jj] * a.sh_ff + row] = silu_mul(gv, uv);
+                                    else a.act[(size_t)slot[jj] * F + row] = silu_mul(gv, uv);
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            release();
+        }
+        // ------------------------------------------------------------ grid barrier 2
+        fd_compute_sync();
+        fd_stamp(a, 4);
+        if (ctid == 0) {
+            if (!ok || !fd_grid_arrive_wait(a.bar + 1, (unsigned)(G + a.bar_extra))) {
+                if (ok) atomicOr(a.status, 0x1000);
+                s_cabort = 1;
+            }
+        }
+        fd_compute_sync();
+        fd_stamp(a, 5);
+        ok = !s_cabort;
+        const int rpc = rt_c / kFdCompute, c0 = warp * rpc;
+        for (int j = b; j < items_c && ok; j += G) {
+            for (int x = 0; x < exp_c; x++) {
+                uint8_t* tile = take();
+                if (!tile) {
+                    ok = false;
+                    break;
+                }
+                const bool shx = x == n_act;
+                const int cnt = shx ? T : act_cnt[x];
+                const int nbx = shx ? nbds : nbd;
+                const uint32_t rb = shx ? rbds : rbd;
+                float2* td = reinterpret_cast<float2*>(tile + rt_c * rb);
+                fd_scales<CD>(tile, rt_c, nbx, bd, td, ctid, 32 * kFdCompute);
+                fd_compute_sync();
+                for (int tc = 0; tc < cnt; tc += 2) {
+                    const int nt = min(2, cnt - tc);
+                    const float* xr[2];
+                    int slot[2];
+#pragma unroll
+                    for (int jj = 0; jj < 2; jj++) {
+                        const int m = tc + min(jj, nt - 1);
+                        const int i = shx ? m : act_asg[x * kFdMaxTokens + m];
+                        slot[jj] = shx ? NA + i : i;
+                        xr[jj] = shx ? a.act_sh + (size_t)i * a.sh_ff : a.act + (size_t)i * F;
+                    }
+                    float ad[4][2], unused[4][2];
+                    if (nt == 2)
+                        rows_dot<CD, CD, false, 2, true>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0, rpc, xr,
+                                                         lane, ad, unused);
+                    else
+                        rows_dot<CD, CD, false, 1, true>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0, rpc, xr,
+                                                         lane, ad, unused);
+#pragma unroll
+                    for (int r = 0; r < 4; r++) {
+                        if (r < rpc) {
+#pragma unroll
+                            for (int jj = 0; jj < 2; jj++) {
+                                if (jj < nt) {
+                                    const float v = warp_sum(ad[r][jj]);
+                                    if (lane == 0) ys[slot[jj] * rt_c + c0 + r] = v;
+                                }
+                            }
+                        }
+                    }
+                }
+                release();
+            }
+            if (!ok) break;
+            // combine this row tile: k ascending fused multiply-adds, then the shared expert
+            for (int c = ctid; c < T * rt_c; c += 32 * kFdCompute) {
+                const int t = c / rt_c, r = c % rt_c;
+                float acc = 0.f;
+                for (int k = 0; k < K; k++) {
+                    const int i = t * K + k, e = s_order[i];
+                    if (e >= 0 && e < E) acc = fmaf(s_wtop[i], ys[i * rt_c + r], acc);
+                }
+                if (sh) acc = __fadd_rn(acc, ys[(NA + t) * rt_c + r]);
+                a.out[(size_t)t * a.n_out + (size_t)j * rt_c + r] = acc;
+            }
+            fd_compute_sync();
+        }
+        if (ctid == 0) s_qc = (int)q;
+        fd_stamp(a, 6);
+    }
+    __syncthreads();
+    // copies issued but not consumed (after a failure) land before the block exits
+    if (producer && lane == 0)
+        for (uint32_t r = (uint32_t)s_qc; r < q; r++) sync::mbar_wait(&full[r % S], (r / S) & 1);
+}
+
 }  // namespace
 
 bool dec_supported(int cg, int cu, int cd, int inter, int n_in, int n_out, int q6s) {
@@ -355,6 +797,103 @@ int launch_dec_down(const ExpertTable& tab, int cd, const int* active, const int
                                                                           n_out, rt, y, q6s, status);
     }
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+
+int launch_fused_decode(FusedDecodeArgs a, int cg, int cu, int cd, cudaStream_t s) {
+    const int E = a.rp.n_exp, K = a.rp.n_used, H = a.rp.n_in, T = a.T;
+    if (T < 1 || T > kFdMaxTokens || T * K > kFdMaxAssign || E > 512 || cg != cu) return 1;
+    if (H % 256 || a.F % 256 || (a.sh_ff && a.sh_ff % 256) || a.n_out % 4) return 1;
+    auto ok_code = [](int c) { return c == DRACO_CODE_Q4_K || c == DRACO_CODE_Q6_K; };
+    if (!ok_code(cg) || !ok_code(cd)) return 1;
+    if (a.q6s != kQ6Padded && (cg == DRACO_CODE_Q6_K || cd == DRACO_CODE_Q6_K)) return 1;
+    int dev = 0, sms = 0, coop = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) ||
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) || !coop) {
+        cudaGetLastError();
+        return 1;
+    }
+    const int nb = H / 256, nbd = a.F / 256, nbds = a.sh_ff / 256;
+    const size_t rbg = (size_t)nb * superblock_bytes(cg, a.q6s), rbu = (size_t)nb * superblock_bytes(cu, a.q6s);
+    const size_t rbd = (size_t)nbd * superblock_bytes(cd, a.q6s), rbds = (size_t)nbds * superblock_bytes(cd, a.q6s);
+    auto slot_b = [&](int rt) { return (size_t)rt * (rbg + rbu) + (size_t)rt * nb * (groups_of(cg) + groups_of(cu)) * 8; };
+    auto slot_c = [&](int rt) {
+        return std::max((size_t)rt * rbd + (size_t)rt * nbd * groups_of(cd) * 8,
+                        a.sh_ff ? (size_t)rt * rbds + (size_t)rt * nbds * groups_of(cd) * 8 : (size_t)0);
+    };
+    const int n_act_est = std::min(T * K, E);
+    auto plan = [&](int G, int& rt_b, int& rt_c, size_t& slot) {
+        // the largest tile with at least one item per block, else the smallest
+        static const int cand[4] = {16, 12, 8, 4};
+        rt_b = rt_c = 0;
+        for (int r : cand)
+            if (a.F % r == 0 && a.sh_ff % r == 0 && slot_b(r) <= 56u * 1024) {
+                rt_b = r;
+                if (n_act_est * (a.F / r) >= G) break;
+            }
+        for (int r : cand)
+            if (a.n_out % r == 0 && slot_c(r) <= 56u * 1024) {
+                rt_c = r;
+                if (a.n_out / r >= G) break;
+            }
+        if (!rt_b || !rt_c) return false;
+        const int nch_max = (T * E + G - 1) / G;
+        if (nch_max > 32) return false;
+        const size_t stage_a = (size_t)(nch_max + T) * kFdRS * 4;
+        slot = std::max({slot_b(rt_b), slot_c(rt_c), stage_a});
+        slot = (slot + 127) / 128 * 128;
+        return true;
+    };
+    const size_t extra = ((size_t)(kFdCompute + 1) * E + (kFdCompute + 1) * 64) * 4 + 2 * kFdMaxAssign * 4 +
+                         (2 * kFdMaxAssign + kFdMaxAssign * kFdMaxTokens) * 4 +
+                         (size_t)(kFdMaxAssign + kFdMaxTokens) * 16 * 4;
+    const void* kern = nullptr;
+    const int ns = E <= 128 ? 4 : E <= 256 ? 8 : 16;
+    constexpr int Q4 = DRACO_CODE_Q4_K, Q6 = DRACO_CODE_Q6_K;
+#define DRACO_FD_PICK(A, D)                                                                  \
+    if (cg == A && cd == D)                                                                  \
+        kern = ns == 4   ? (const void*)fused_decode_kernel<A, A, D, 4>                      \
+               : ns == 8 ? (const void*)fused_decode_kernel<A, A, D, 8>                      \
+                         : (const void*)fused_decode_kernel<A, A, D, 16>;
+    DRACO_FD_PICK(Q4, Q6)
+    DRACO_FD_PICK(Q4, Q4)
+    DRACO_FD_PICK(Q6, Q6)
+    DRACO_FD_PICK(Q6, Q4)
+#undef DRACO_FD_PICK
+    if (!kern) return 1;
+    // blocks per SM from the occupancy of the planned shared memory (2 when it fits)
+    int rt_b = 0, rt_c = 0, slots = kFdMaxSlots, G = 0;
+    size_t slot = 0, total = 0;
+    for (int bps = 2; bps >= 1 && !G; bps--) {
+        if (!plan(sms * bps, rt_b, rt_c, slot)) continue;
+        for (slots = kFdMaxSlots; slots >= 2; slots--) {
+            total = slots * slot + extra;
+            if (total * bps <= 220u * 1024) break;
+        }
+        if (slots < 2) continue;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess) {
+            cudaGetLastError();
+            return 1;
+        }
+        int occ = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kFdThreads, total) != cudaSuccess) {
+            cudaGetLastError();
+            return 1;
+        }
+        if (occ >= bps) G = sms * bps;
+    }
+    if (!G) return 1;
+    a.rt_b = rt_b;
+    a.rt_c = rt_c;
+    a.slot_bytes = (int)slot;
+    a.n_slots = slots;
+    void* args[] = {&a};
+    const cudaError_t e = cudaLaunchCooperativeKernel(kern, G, kFdThreads, args, total, s);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return e == cudaErrorCooperativeLaunchTooLarge ? 1 : -3;
+    }
+    return 0;
 }
 
 }  // namespace draco

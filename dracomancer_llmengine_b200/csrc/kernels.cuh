@@ -68,6 +68,53 @@ int launch_dec_gateup(const ExpertTable& tab, int cg, int cu, const int* active,
 int launch_dec_down(const ExpertTable& tab, int cd, const int* active, const int* n_active, int n_active_max,
                     const int* off, const float* act, int inter, int n_out, float* y, int q6s, int* status,
                     cudaStream_t s);
+// The whole decode layer of a small batch (T <= 8 tokens, T*K <= 64) in one cooperative
+// launch (decode.cu): router logits (exact order), selection, gate/up + SwiGLU, down, combine,
+// shared expert.  Device pointers throughout; `bar` (2 words) must be zero at launch.
+struct FusedDecodeArgs {
+    ExpertTable tab;
+    const uint8_t* sh_g;        // shared expert matrices (same formats as the routed ones) or null
+    const uint8_t* sh_u;
+    const uint8_t* sh_d;
+    int sh_ff;                  // 0: no shared expert
+    const float* W;             // router [E][n_in]; nullptr: routing given in order/wtop
+    RouterParams rp;
+    const float* X;             // [T][n_in]
+    int T, F, n_out;
+    float* out;                 // [T][n_out]
+    int* order;                 // [T][K]: written (router) or read (given routing)
+    float* wtop;
+    float* logits;              // [T][E] scratch
+    float* act;                 // [T*K][F] scratch
+    float* act_sh;              // [T][sh_ff] scratch
+    unsigned* bar;              // [2] grid barrier counters
+    int* status;                // 0x200 staged copy wait ran out, 0x1000 grid barrier wait ran out
+    int* route_err;             // the routing status word (select)
+    int q6s;
+    int bar_extra;              // test hook: arrivals awaited beyond the grid (0 in use)
+    unsigned long long* stamps; // optional [grid][8] %globaltimer at the phase boundaries (or null)
+    int rt_b, rt_c, slot_bytes, n_slots;   // set by the launcher
+};
+// 0 launched; 1 not applicable (the caller runs the separate kernels); -3 launch error
+int launch_fused_decode(FusedDecodeArgs a, int cg, int cu, int cd, cudaStream_t s);
+
+// Router MLP of the top-1 learned-router MoE op (zaya.cu, src/m6_engine.c:795-835): device
+// pointers; router matrices F32 (code 9) or F16 (7); writes the routing of the one token
+// (order[0] = expert or -1, wtop[0]) and the new recurrent state.
+struct ZayaRouterArgs {
+    const void *wdown, *wfc1, *wfc2, *wout;
+    int cdown, cfc1, cfc2, cout;
+    const float *bdown, *bfc1, *bfc2, *rnorm, *eda_scale, *bal;
+    const float* x;             // [H]
+    const float* state_in;      // [RH] (read when eda_scale is given)
+    float* state_out;           // [RH]
+    float* rh;                  // [RH] scratch
+    int H, RH, nclass, nexp, iskip;
+    int* order;
+    float* wtop;
+};
+int launch_zaya_router(const ZayaRouterArgs& a, cudaStream_t s);
+
 // d[0] = a, d[1] = b (small device-side constants, stream ordered and graph capturable)
 void launch_set_pair(int* d, int a, int b, cudaStream_t s);
 

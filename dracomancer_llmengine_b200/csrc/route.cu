@@ -6,6 +6,7 @@
 // exp is the host C library's (common.cuh), sums run sequentially in expert order, ties go
 // to the lower expert index.
 #include "kernels.cuh"
+#include "select.cuh"
 
 namespace draco {
 
@@ -337,25 +338,6 @@ void launch_router_logits(const float* X, const float* W, int T, int E, int H, f
 // ------------------------------------------------------------------------------------------
 // Selection: one warp per token.
 // ------------------------------------------------------------------------------------------
-constexpr int kMaxExperts = 512;   // the reference's fixed arrays (src/m6_layer.c:774,791)
-constexpr int kMaxUsed = 64;       // (src/m6_layer.c:860-862)
-constexpr int kMaxGroups = 64;     // (src/m6_layer.c:843,852)
-constexpr int kSelWarps = 4;
-
-// (v2, i2) beats (v1, i1): larger value, or equal value at a lower valid index.  Invalid
-// candidates carry i = -1 and never beat a valid one.
-__device__ __forceinline__ bool beats(float v2, int i2, float v1, int i1) {
-    if (i2 < 0) return false;
-    if (i1 < 0) return true;
-    return v2 > v1 || (v2 == v1 && i2 < i1);
-}
-
-// One warp per token.  Lane l holds experts l + 32 j (j < NS) in registers with a bitmask of
-// those still selectable; each of the K rounds takes every lane's best candidate and a 5-step
-// shuffle argmax over (score, expert, prob).  The order of comparisons gives exactly the
-// reference's scan (src/m6_layer.c:860-870): the largest score wins, the lowest expert index
-// among equal scores, and only scores above the -1e30 floor count (NaN never does).  The softmax
-// denominator and the weight sum are taken sequentially in the reference's order.
 template <int NS>
 __global__ void __launch_bounds__(32 * kSelWarps) router_select_kernel(RouterParams p, int T,
                                                                       const float* __restrict__ logits,
@@ -364,188 +346,11 @@ __global__ void __launch_bounds__(32 * kSelWarps) router_select_kernel(RouterPar
                                                                       int* __restrict__ err) {
     __shared__ __align__(16) float s_v[kSelWarps][kMaxExperts];
     __shared__ float s_gs[kSelWarps][kMaxGroups];
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int w = threadIdx.x >> 5;
     const int t = blockIdx.x * kSelWarps + w;
     if (t >= T) return;
-    const int E = p.n_exp, K = p.n_used;
-    const float* lg = logits + (size_t)t * E;
-    float* V = s_v[w];
-    float S[NS], P[NS];
-    if (p.scoring == 0) {
-        // max-subtracted softmax (src/m6_layer.c:784-789)
-        float mx = -1e30f;
-#pragma unroll
-        for (int j = 0; j < NS; j++) {
-            const int e = lane + 32 * j;
-            S[j] = e < E ? lg[e] : 0.f;
-            if (e < E && S[j] > mx) mx = S[j];
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, mx, o);
-            mx = ov > mx ? ov : mx;
-        }
-#pragma unroll
-        for (int j = 0; j < NS; j++) {
-            const int e = lane + 32 * j;
-            P[j] = host_expf(__fsub_rn(S[j], mx));
-            if (e < E) V[e] = P[j];
-        }
-        __syncwarp();
-        float s = 0.f;
-        if (lane == 0) {
-            int e = 0;
-            for (; e + 4 <= E; e += 4) {
-                const float4 q = *reinterpret_cast<const float4*>(V + e);
-                s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, q.x), q.y), q.z), q.w);
-            }
-            for (; e < E; e++) s = __fadd_rn(s, V[e]);
-        }
-        s = __shfl_sync(0xffffffffu, s, 0);
-        const float inv = __fdiv_rn(1.0f, s);
-#pragma unroll
-        for (int j = 0; j < NS; j++) {
-            P[j] = __fmul_rn(P[j], inv);
-            S[j] = P[j];
-        }
-    } else {
-        // sigmoid scores; bias only steers the selection (src/m6_layer.c:833-840)
-#pragma unroll
-        for (int j = 0; j < NS; j++) {
-            const int e = lane + 32 * j;
-            const float l = e < E ? lg[e] : 0.f;
-            P[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, host_expf(-l)));
-            S[j] = __fadd_rn(P[j], p.probs_b && e < E ? p.probs_b[e] : 0.0f);
-        }
-        if (p.n_group > 1) {
-            // group score = sum of the group's two largest (src/m6_layer.c:841-859), then the
-            // n_group_used best groups by the same strict-greater scan
-#pragma unroll
-            for (int j = 0; j < NS; j++)
-                if (lane + 32 * j < E) V[lane + 32 * j] = S[j];
-            __syncwarp();
-            const int per = E / p.n_group;
-            for (int g = lane; g < p.n_group; g += 32) {
-                float m1 = -1e30f, m2 = -1e30f;
-                for (int i = 0; i < per; i++) {
-                    const float v = V[g * per + i];
-                    if (v > m1) {
-                        m2 = m1;
-                        m1 = v;
-                    } else if (v > m2) {
-                        m2 = v;
-                    }
-                }
-                s_gs[w][g] = __fadd_rn(m1, m2);
-            }
-            __syncwarp();
-            uint32_t gavail = 0, gsel = 0;   // groups lane, lane + 32
-            float G[2];
-#pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const int g = lane + 32 * j;
-                G[j] = g < p.n_group ? s_gs[w][g] : 0.f;
-                if (g < p.n_group) gavail |= 1u << j;
-            }
-            for (int r = 0; r < p.n_group_used; r++) {
-                float bv = -1e30f;
-                int bi = -1;
-#pragma unroll
-                for (int j = 0; j < 2; j++)
-                    if ((gavail >> j & 1) && G[j] > bv) {
-                        bv = G[j];
-                        bi = lane + 32 * j;
-                    }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    if (beats(ov, oi, bv, bi)) {
-                        bv = ov;
-                        bi = oi;
-                    }
-                }
-                if (bi < 0) {
-                    if (lane == 0) atomicOr(err, 1);
-                    break;
-                }
-                if ((bi & 31) == lane) {
-                    gavail &= ~(1u << (bi >> 5));
-                    gsel |= 1u << (bi >> 5);
-                }
-            }
-            // every lane learns the chosen groups
-            const unsigned long long chosen =
-                (unsigned long long)__ballot_sync(0xffffffffu, gsel & 1) |
-                ((unsigned long long)__ballot_sync(0xffffffffu, gsel >> 1 & 1) << 32);
-#pragma unroll
-            for (int j = 0; j < NS; j++) {
-                const int e = lane + 32 * j;
-                if (e < E && !(chosen >> (e / per) & 1)) S[j] = -1e30f;
-            }
-        }
-    }
-    uint32_t avail = 0;
-#pragma unroll
-    for (int j = 0; j < NS; j++)
-        if (lane + 32 * j < E) avail |= 1u << j;
-    // lane l keeps result l (and l + 32 when K > 32)
-    static_assert(kMaxUsed <= 64, "two results per lane");
-    int my_i0 = -1, my_i1 = -1;
-    float my_p0 = 0.f, my_p1 = 0.f;
-    for (int r = 0; r < K; r++) {
-        float bv = -1e30f, bp = 0.f;
-        int bi = -1;
-#pragma unroll
-        for (int j = 0; j < NS; j++)
-            if ((avail >> j & 1) && S[j] > bv) {
-                bv = S[j];
-                bp = P[j];
-                bi = lane + 32 * j;
-            }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
-            if (beats(ov, oi, bv, bi)) {
-                bv = ov;
-                bi = oi;
-                bp = op;
-            }
-        }
-        if (bi < 0) {
-            if (lane == 0) atomicOr(err, 2);
-        } else if ((bi & 31) == lane) {
-            avail &= ~(1u << (bi >> 5));
-        }
-        if ((r & 31) == lane) {
-            if (r < 32) {
-                my_i0 = bi;
-                my_p0 = bi >= 0 ? bp : 0.f;
-            } else {
-                my_i1 = bi;
-                my_p1 = bi >= 0 ? bp : 0.f;
-            }
-        }
-    }
-    // weights (src/m6_layer.c:871-880): sum in selection order, then per-lane division
-    float s = 0.f;
-    for (int j = 0; j < K; j++) s = __fadd_rn(s, __shfl_sync(0xffffffffu, j < 32 ? my_p0 : my_p1, j & 31));
-    const bool renorm = p.scoring == 0 || p.norm_w;
-    if (s < 6.103515625e-5f) s = 6.103515625e-5f;
-    const bool scale = p.scoring != 0 && p.w_scale != 0.f && p.w_scale != 1.f;
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const int j = lane + 32 * h;
-        if (j < K) {
-            float wl = h ? my_p1 : my_p0;
-            if (renorm) wl = __fdiv_rn(wl, s);
-            if (scale) wl = __fmul_rn(wl, p.w_scale);
-            order[(size_t)t * K + j] = h ? my_i1 : my_i0;
-            wtop[(size_t)t * K + j] = wl;
-        }
-    }
+    select_token<NS>(p, logits + (size_t)t * p.n_exp, order + (size_t)t * p.n_used, wtop + (size_t)t * p.n_used, err,
+                     s_v[w], s_gs[w]);
 }
 
 void launch_router_select(const RouterParams& p, int T, RouteBufs& b, cudaStream_t s) {

@@ -314,18 +314,28 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// ---------------------------------------------------------------- dequantisation (fp32 -> fp16)
-// float 2 + q/64 from a byte q (0..63) placed in bits 16..23 under exponent byte 0x40: one PRMT
-__device__ __forceinline__ float q_as_float(uint32_t bytes4, int i) {
-    // selector nibbles (low to high): y.b0, y.b0, x.b_i, y.b3 -> bytes (0, 0, q, 0x40)
-    const uint32_t sel = 0x7044u | ((uint32_t)i << 8);
-    return __uint_as_float(__byte_perm(bytes4, 0x40000000u, sel));
+// ---------------------------------------------------------------- dequantisation (-> fp16)
+// Operand K order.  A dequant thread turns one 32-bit word of packed codes into fp16 pairs with
+// one LOP3 per pair: the two values of a pair are bytes 0 and 2 (or 1 and 3) of the word, i.e.
+// K positions 4w + {0, 2} and 4w + {1, 3}.  Both operands of the MMAs therefore hold K in the
+// order "positions 1 and 2 of every group of 4 swapped": the weights by construction here, the
+// activations by the gather (gather_*_kernel) and by the gate/up epilogue, which writes the
+// down GEMM's activation rows.  A dot product does not depend on the order of its terms'
+// pairing, so the result is that of the natural order (up to fp32 accumulation order).
+__host__ __device__ __forceinline__ int kperm(int i) { return (i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1); }
+
+__device__ __forceinline__ uint32_t lop_or_mask(uint32_t a, uint32_t mask, uint32_t bits) {
+    // (a & mask) | bits in one LOP3
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(bits));
+    return r;
 }
-// value = scale * q - offset computed as fma(2 + q/64, 64 * scale, -(128 * scale + offset))
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&h);
 }
+__device__ __forceinline__ __half2 u2h2(uint32_t u) { return *reinterpret_cast<const __half2*>(&u); }
+__device__ __forceinline__ uint32_t h22u(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
 
 // Q4_K 6-bit scale/min of sub-block j (0..7) from the 12 scale bytes held in three words
 // (s0 = bytes 0-3, s1 = 4-7, s2 = 8-11; src/m5_kern_scalar.c:39-46), without indexing memory
@@ -341,18 +351,39 @@ __device__ __forceinline__ void q4k_sm_words(uint32_t s0, uint32_t s1, uint32_t 
     }
 }
 
-// Q4_K: 64 values [64*kc, 64*kc+64) of one superblock row -> 32 packed fp16 pairs
+// Per-sub-block constants of the Q4_K decode in fp16x2 arithmetic.  The reference's value is
+// w = d*sc*q - dmin*m (src/m5_kern_scalar.c:73-83).  With H = 1024 + 16q (the nibble placed in
+// mantissa bits 4-7 under exponent 10):
+//   I = fma(H, sc/16, -72 sc) = sc*(q - 8)          exact (integer |I| <= 504)
+//   w = fma(I, d, C),  C = fp16(8 d sc - dmin m)       one rounding of d*sc*(q-8) + C
+// Centring q on 8 leaves C small wherever the sub-block's values are centred (the min term is
+// about 8 scale steps), so w is the fp16 rounding of the exact value up to C's own rounding.
+struct Q4Sub {
+    __half2 sc16, off, d, c;
+};
+__device__ __forceinline__ Q4Sub q4_sub(float d, float dmin, int sc, int mn) {
+    Q4Sub r;
+    r.sc16 = __float2half2_rn((float)sc * 0.0625f);
+    r.off = __float2half2_rn((float)(-72 * sc));
+    r.d = __float2half2_rn(d);
+    r.c = __float2half2_rn(__fsub_rn(8.f * d * (float)sc, dmin * (float)mn));
+    return r;
+}
+__device__ __forceinline__ uint32_t q4_pair(uint32_t hbits, const Q4Sub& k) {
+    const __half2 i = __hfma2(u2h2(hbits), k.sc16, k.off);
+    return h22u(__hfma2(i, k.d, k.c));
+}
+
+// Q4_K: 64 values [64*kc, 64*kc+64) of one superblock row -> 32 fp16 pairs (kperm order)
 __device__ __forceinline__ void deq_q4k(const uint8_t* blk, int kc, uint32_t (&out)[32]) {
     const uint4 hd = *reinterpret_cast<const uint4*>(blk);
     const float d = h2f((uint16_t)(hd.x & 0xffff)), dmin = h2f((uint16_t)(hd.x >> 16));
     int sc0, m0, sc1, m1;
     q4k_sm_words(hd.y, hd.z, hd.w, 2 * kc, sc0, m0);
     q4k_sm_words(hd.y, hd.z, hd.w, 2 * kc + 1, sc1, m1);
-    const float ds0 = d * (float)sc0, dm0 = dmin * (float)m0;
-    const float ds1 = d * (float)sc1, dm1 = dmin * (float)m1;
-    const float a0 = 64.f * ds0, b0 = -(128.f * ds0 + dm0);
-    const float a1 = 64.f * ds1, b1 = -(128.f * ds1 + dm1);
+    const Q4Sub k0 = q4_sub(d, dmin, sc0, m0), k1 = q4_sub(d, dmin, sc1, m1);
     const uint4* qv = reinterpret_cast<const uint4*>(blk + 16 + 32 * kc);
+    constexpr uint32_t kMask = 0x00F000F0u, kMagic = 0x64006400u;
 #pragma unroll
     for (int h = 0; h < 2; h++) {
         const uint4 q = qv[h];
@@ -360,12 +391,12 @@ __device__ __forceinline__ void deq_q4k(const uint8_t* blk, int kc, uint32_t (&o
         for (int c = 0; c < 4; c++) {
             const uint32_t word = c == 0 ? q.x : c == 1 ? q.y : c == 2 ? q.z : q.w;
             const int w = 4 * h + c;
-            const uint32_t lo = word & 0x0F0F0F0Fu, hi = (word >> 4) & 0x0F0F0F0Fu;
-            // low nibbles: values 4w..4w+3 of sub-block 2kc; high nibbles: of sub-block 2kc+1
-            out[2 * w] = pack2(fmaf(q_as_float(lo, 0), a0, b0), fmaf(q_as_float(lo, 1), a0, b0));
-            out[2 * w + 1] = pack2(fmaf(q_as_float(lo, 2), a0, b0), fmaf(q_as_float(lo, 3), a0, b0));
-            out[16 + 2 * w] = pack2(fmaf(q_as_float(hi, 0), a1, b1), fmaf(q_as_float(hi, 1), a1, b1));
-            out[16 + 2 * w + 1] = pack2(fmaf(q_as_float(hi, 2), a1, b1), fmaf(q_as_float(hi, 3), a1, b1));
+            // low nibbles (sub-block 2kc) of bytes 0,2 and 1,3; high nibbles (2kc+1) likewise,
+            // each moved to bits 4-7 of its half
+            out[2 * w] = q4_pair(lop_or_mask(word << 4, kMask, kMagic), k0);
+            out[2 * w + 1] = q4_pair(lop_or_mask(word >> 4, kMask, kMagic), k0);
+            out[16 + 2 * w] = q4_pair(lop_or_mask(word, kMask, kMagic), k1);
+            out[16 + 2 * w + 1] = q4_pair(lop_or_mask(word >> 8, kMask, kMagic), k1);
         }
     }
 }
@@ -373,6 +404,9 @@ __device__ __forceinline__ void deq_q4k(const uint8_t* blk, int kc, uint32_t (&o
 // Q6_K (224-byte padded superblock): values p in [64*kc, 64*kc+64)
 //   ql byte (p>>7)*64 + (p&63), high nibble if (p>>6)&1; qh byte (p>>7)*32 + (p&31), shift
 //   ((p>>5)&3)*2; scale sc[p>>4]; w = d * sc * (q - 32)   (src/m5_kern_scalar.c:115-142)
+// fp16x2 arithmetic: H = 1024 + q (PRMT under the exponent byte 0x64), Q = H - 1056 = q - 32
+// exact; S = d*sc exact in fp32 is split S = S_hi + S_lo (both fp16) and w = fma(Q, S_hi,
+// Q*S_lo): the fp16 rounding of Q*S up to the tiny rounding of Q*S_lo.
 __device__ __forceinline__ void deq_q6k(const uint8_t* blk, int kc, uint32_t (&out)[32]) {
     const int h = kc >> 1, nhi = kc & 1;
     const uint4* qlv = reinterpret_cast<const uint4*>(blk + h * 64);
@@ -380,22 +414,28 @@ __device__ __forceinline__ void deq_q6k(const uint8_t* blk, int kc, uint32_t (&o
     const uint32_t scw = *reinterpret_cast<const uint32_t*>(blk + 192 + 4 * kc);
     const float d = h2f(*reinterpret_cast<const uint16_t*>(blk + 208));
     const int nsh = 4 * nhi;
+    const __half2 m1056 = __float2half2_rn(-1056.f);
     // 4 groups of 16 values: group g covers p = 64kc + 16g .. +16 with scale sc[4kc + g];
     // ql byte 16g + i of this half, qh byte 16(g & 1) + i, 2-bit field at (2 nhi + g/2) * 2
 #pragma unroll
     for (int g = 0; g < 4; g++) {
-        const float ds = d * (float)(int8_t)(scw >> (8 * g));
-        const float a = 64.f * ds, b = -(160.f * ds);
+        const float S = d * (float)(int8_t)(scw >> (8 * g));
+        const __half shi = __float2half_rn(S);
+        const __half2 s_hi = __half2half2(shi);
+        const __half2 s_lo = __float2half2_rn(__fsub_rn(S, __half2float(shi)));
         const uint4 l = qlv[g];
         const uint4 q2 = qhv[g & 1];
-        const int shift = (2 * nhi + (g >> 1)) * 2;
+        const int shift = (2 * nhi + (g >> 1)) * 2;   // field -> bits 4-5 of each byte
 #pragma unroll
         for (int w = 0; w < 4; w++) {
             const uint32_t lw = w == 0 ? l.x : w == 1 ? l.y : w == 2 ? l.z : l.w;
             const uint32_t hw = w == 0 ? q2.x : w == 1 ? q2.y : w == 2 ? q2.z : q2.w;
-            const uint32_t q6 = ((lw >> nsh) & 0x0F0F0F0Fu) | (((hw >> shift) & 0x03030303u) << 4);
-            out[8 * g + 2 * w] = pack2(fmaf(q_as_float(q6, 0), a, b), fmaf(q_as_float(q6, 1), a, b));
-            out[8 * g + 2 * w + 1] = pack2(fmaf(q_as_float(q6, 2), a, b), fmaf(q_as_float(q6, 3), a, b));
+            const uint32_t hs = shift >= 4 ? hw >> (shift - 4) : hw << (4 - shift);
+            const uint32_t q6 = lop_or_mask(lw >> nsh, 0x0F0F0F0Fu, hs & 0x30303030u);
+            const __half2 q02 = __hadd2(u2h2(__byte_perm(q6, 0x64646464u, 0x4240)), m1056);
+            const __half2 q13 = __hadd2(u2h2(__byte_perm(q6, 0x64646464u, 0x4341)), m1056);
+            out[8 * g + 2 * w] = h22u(__hfma2(q02, s_hi, __hmul2(q02, s_lo)));
+            out[8 * g + 2 * w + 1] = h22u(__hfma2(q13, s_hi, __hmul2(q13, s_lo)));
         }
     }
 }
@@ -718,7 +758,7 @@ __global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
                         const float g = is_up ? other : mine_e, u = is_up ? mine_o : other;
                         const int col = tb + c + (is_up ? 1 : 0);
                         if (col < ntok)
-                            act_out[(size_t)(p0 + col) * out_ld + orow] = __float2half_rn(silu_mul(g, u));
+                            act_out[(size_t)(p0 + col) * out_ld + kperm(orow)] = __float2half_rn(silu_mul(g, u));
                     }
                 }
             } else {
@@ -790,16 +830,16 @@ __global__ void gather_half_kernel(const float* __restrict__ X, const int* __res
         const int t = ilist ? ilist[p] / tok_div : p;
         const float4 a = *reinterpret_cast<const float4*>(X + (size_t)t * H + c8);
         const float4 b = *reinterpret_cast<const float4*>(X + (size_t)t * H + c8 + 4);
-        uint4 o;
-        o.x = pack2(a.x, a.y);
-        o.y = pack2(a.z, a.w);
-        o.z = pack2(b.x, b.y);
-        o.w = pack2(b.z, b.w);
+        uint4 o;   // kperm order: positions 1 and 2 of each group of 4 swapped
+        o.x = pack2(a.x, a.z);
+        o.y = pack2(a.y, a.w);
+        o.z = pack2(b.x, b.z);
+        o.w = pack2(b.y, b.w);
         *reinterpret_cast<uint4*>(Xs + (size_t)p * H + c8) = o;
     }
 }
 
-// the same from token rows that are already fp16: a row copy
+// the same from token rows that are already fp16
 __global__ void gather_rows16_kernel(const __half* __restrict__ X, const int* __restrict__ ilist,
                                      const int* __restrict__ n_valid, int tok_div, int P, int H,
                                      __half* __restrict__ Xs) {
@@ -809,7 +849,13 @@ __global__ void gather_rows16_kernel(const __half* __restrict__ X, const int* __
          i += (long)gridDim.x * blockDim.x) {
         const int p = (int)(i / per_row), c8 = (int)(i % per_row) * 8;
         const int t = ilist ? ilist[p] / tok_div : p;
-        *reinterpret_cast<uint4*>(Xs + (size_t)p * H + c8) = *reinterpret_cast<const uint4*>(X + (size_t)t * H + c8);
+        const uint4 a = *reinterpret_cast<const uint4*>(X + (size_t)t * H + c8);
+        uint4 o;   // kperm order
+        o.x = __byte_perm(a.x, a.y, 0x5410);
+        o.y = __byte_perm(a.x, a.y, 0x7632);
+        o.z = __byte_perm(a.z, a.w, 0x5410);
+        o.w = __byte_perm(a.z, a.w, 0x7632);
+        *reinterpret_cast<uint4*>(Xs + (size_t)p * H + c8) = o;
     }
 }
 

@@ -73,6 +73,44 @@ void m6_moe_tok(m6_dequant_fn DQ, m6_gemm_auto_fn GA, float* gwbuf, const float*
                 int n_used, int inter, int n_in, int n_out, int n_exp, float* out, float* work,
                 int* iwork);
 
+/* caller-routed experts of one token: the table ptrs/codes holds exactly the n_exp (<= 64)
+ * selected experts (gate, up, down each), wtop their weights; out = sum_j wtop[j] * expert_j(x0),
+ * j ascending.  m6_moe_batch/2 have the fixed shape inter 512, hidden 2048; m6_moe_batch2 adds
+ * sigmoid(x0 . sh_gate_inp) * shared expert (sh_ptrs/sh_codes: gate, up, down; no gate row:
+ * nothing added, as the reference's gate is then 0); scratch is accepted and unused.
+ * replaces src/m6_layer.c:522-537 (m6_moe_batch), :547-604 (m6_moe_batch2),
+ *          :606-634 (m6_moe_batch3), :656-690 (m6_moe_batch4) */
+void m6_moe_batch(const float* x0, const uint64_t* ptrs, const int* codes, const float* wtop, int n_exp,
+                  float* out);
+void m6_moe_batch2(const float* x0, const uint64_t* ptrs, const int* codes, const float* wtop, int n_exp,
+                   const uint64_t* sh_ptrs, const int* sh_codes, const float* sh_gate_inp, float* scratch,
+                   float* out);
+void m6_moe_batch3(const float* x0, const uint64_t* ptrs, const int* codes, const float* wtop, int n_exp,
+                   int inter, int n_in, int n_out, float* out);
+void m6_moe_batch4(const float* x0, const uint64_t* ptrs, const int* codes, const float* wtop, int n_exp,
+                   int inter, int n_in, int n_out, float* scratch, float* out);
+
+/* top-1 MoE with a learned router MLP (2-layer GELU MLP over a recurrent state, softmax over
+ * nclass classes + balancing biases; classes >= nexp or == iskip mean "no expert", output 0).
+ * Router matrices F32 (9) or F16 (7); experts: exp_gp[e] a fused [2*inter][hidden] gate|up
+ * matrix, exp_dp[e] the down matrix.  rh_state (host, [hidden2]) is read (with eda_scale) and
+ * overwritten with the new state, as in the reference.  Field order of src/m6_engine.c:781-793.
+ * replaces src/m6_engine.c:795-835 (m6_zaya_moe_op) */
+typedef struct M6ZayaMoeP {
+    const uint8_t *wdown, *wfc1, *wfc2, *wout;
+    int cdown, cfc1, cfc2, cout;
+    const float *bdown, *bfc1, *bfc2;
+    const float* rnorm;
+    const float* eda_scale;
+    const float* bal;
+    const uint64_t *exp_gp, *exp_dp;
+    const int *exp_cg, *exp_cd;
+    int nexp, nclass, inter, hidden, hidden2, iskip;
+    float* rh_state;
+    float* scratch;
+} M6ZayaMoeP;
+void m6_zaya_moe_op(const float* xn, void* pv, float* out);
+
 /* N selected experts' GEMV: y[e][o] = sum_i x_e[i] * W[idx[e]][o][i], x_e = x + e*x_stride.
  * Returns 0, -1 (shape), -3 (device error).
  * replaces src/m5/m5_batch8_k.c:80-114 (m5_gemvn_q4k) and :170-183 (m5_gemvn_q6k) */
@@ -233,6 +271,16 @@ int draco_b200_moe_tok_noalloc(const float* X, const int* order, const float* wt
  * previous mode. */
 int draco_b200_set_gemm_path(int mode);
 
+/* Fused decode layer on (1, the default) or off (0): batches of at most 8 tokens and 64
+ * token-expert assignments run the whole layer (router logits, selection, gate/up, down, combine,
+ * shared expert) as one cooperative kernel instead of separate launches.  DRACO_B200_FUSED_DECODE
+ * sets the initial value.  Returns the previous setting. */
+int draco_b200_set_fused_decode(int on);
+/* Test hook: the fused decode kernel's grid barriers wait for n arrivals beyond its own blocks
+ * (n > 0 models a block that never arrives: the bounded waits run out after about a second, the
+ * kernel reports code 0x1000 and the call returns -5).  Returns the previous value; 0 in use. */
+int draco_b200_test_fused_barrier_extra(int n);
+
 /* Activation mode for gate/up: 0 fp32 (reference semantics, default), 1 Q8_K (int8
  * activations, integer superblock dots).  Returns the previous mode. */
 int draco_b200_set_act_mode(int mode);
@@ -240,7 +288,9 @@ int draco_b200_set_act_mode(int mode);
 /* Per-phase device timing with CUDA events on the launching stream (enable != 0 turns it on
  * and clears the totals).  profile_read fills ms[i] (total milliseconds) and counts[i] for
  * phases 0 route, 1 dispatch, 2 gate/up, 3 down, 4 shared expert, 5 combine, 6 gather of the
- * fp16 token rows (tensor-core path); returns the number of phases. */
+ * fp16 token rows (tensor-core path), 7 the fused single-launch decode layer (batches of at most
+ * 8 tokens and 64 token-expert assignments: routing through combine in one kernel); returns
+ * the number of phases. */
 int draco_b200_profile(int enable);
 int draco_b200_profile_read(double* ms, long* counts, int n);
 /* Number of kernels this library has launched since it was loaded. */

@@ -219,6 +219,23 @@ void orc_route_softmax(const float* x, const float* gate_inp, int n_exp, int n_u
     free(p);
 }
 
+float orc_pairwise_sum(const float* a, int n) {
+    /* numpy's float32 add.reduce over a contiguous run of n <= 128 values */
+    if (n < 8) {
+        float r = 0.f;
+        for (int i = 0; i < n; i++) r += a[i];
+        return r;
+    }
+    float r[8];
+    for (int j = 0; j < 8; j++) r[j] = a[j];
+    int i = 8;
+    for (; i < n - (n % 8); i += 8)
+        for (int j = 0; j < 8; j++) r[j] += a[i + j];
+    float res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+    for (; i < n; i++) res += a[i];
+    return res;
+}
+
 void orc_route_sigmoid(const float* x, const float* gate_inp, const float* probs_b, int n_exp,
                        int n_used, int n_group, int n_group_used, int norm_w, float w_scale,
                        int n_in, int* idx, float* w, float* probs_out) {
@@ -262,7 +279,12 @@ void orc_route_sigmoid(const float* x, const float* gate_inp, const float* probs
         w[j] = p[idx[j]];
         s += w[j];
     }
-    if (norm_w) {
+    if (norm_w == 2) {
+        /* the numpy drivers (src/k2_engine.py:506-507): rw / rw.sum() * scale, no clamp, the sum
+         * in numpy's float32 pairwise order (8 running sums for n >= 8) */
+        s = orc_pairwise_sum(w, n_used);
+        for (int j = 0; j < n_used; j++) w[j] /= s;
+    } else if (norm_w) {
         if (s < 6.103515625e-5f) s = 6.103515625e-5f;
         for (int j = 0; j < n_used; j++) w[j] /= s;
     }

@@ -34,7 +34,9 @@ int orc_dequant_row(int code, const uint8_t* row, int n_in, float* out);
 void orc_route_softmax(const float* x, const float* gate_inp, int n_exp, int n_used, int n_in,
                        int* idx, float* w, float* probs_out);
 /* sigmoid router: +bias for selection, group-limited top-k, weights from the unbiased
- * sigmoid, optional renorm (clamp) and scale           (src/m6_layer.c:823-866) */
+ * sigmoid, optional renorm (clamp) and scale           (src/m6_layer.c:823-866)
+ * norm_w == 2: the numpy drivers' renormalisation instead (src/k2_engine.py:506-507): no clamp,
+ * numpy's pairwise sum order */
 void orc_route_sigmoid(const float* x, const float* gate_inp, const float* probs_b, int n_exp,
                        int n_used, int n_group, int n_group_used, int norm_w, float w_scale,
                        int n_in, int* idx, float* w, float* probs_out);
@@ -43,6 +45,8 @@ void orc_route_sigmoid(const float* x, const float* gate_inp, const float* probs
 void orc_route_batch(int scoring, const float* X, int T, const float* gate_inp, const float* probs_b,
                      int n_exp, int n_used, int n_group, int n_group_used, int norm_w, float w_scale,
                      int n_in, int* idx, float* w);
+/* numpy's float32 pairwise sum of n <= 128 contiguous values */
+float orc_pairwise_sum(const float* a, int n);
 /* stable top-k (ties -> lower index)                   (src/m6_layer.c:808-821) */
 void orc_topk(const float* v, int n, int k, int* out);
 

@@ -129,6 +129,26 @@ class Port:
                                ct.c_float(layer.w_scale if sig else 0.0), layer.hidden, pi(idx), pf(w))
         return idx, w
 
+    def route_probs(self, layer, x):
+        """(idx, w, probs fp32[T, E]) with the per-token C router (probs: the softmax or sigmoid
+        scores before selection)."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        T = x.shape[0]
+        idx = np.zeros((T, layer.n_used), np.int32)
+        w = np.zeros((T, layer.n_used), np.float32)
+        P = np.zeros((T, layer.n_exp), np.float32)
+        gi = np.ascontiguousarray(layer.gate_inp, np.float32)
+        pb = pf(layer.probs_b) if layer.probs_b is not None else None
+        for t in range(T):
+            if layer.scoring == "softmax":
+                self.L.orc_route_softmax(pf(x[t]), pf(gi), layer.n_exp, layer.n_used, layer.hidden,
+                                         pi(idx[t]), pf(w[t]), pf(P[t]))
+            else:
+                self.L.orc_route_sigmoid(pf(x[t]), pf(gi), pb, layer.n_exp, layer.n_used, layer.n_group,
+                                         layer.n_group_used, layer.norm_w, ct.c_float(layer.w_scale), layer.hidden,
+                                         pi(idx[t]), pf(w[t]), pf(P[t]))
+        return idx, w, P
+
     # -- layers --
     def decode(self, layer, x):
         """Routed experts for each token row independently (decode semantics, no shared expert)."""

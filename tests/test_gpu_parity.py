@@ -55,6 +55,11 @@ ROUTER_CASES = {
                               bias=True, zipf=True, seed=24),
     "softmax_k1": dict(hidden=512, n_exp=16, n_used=1, inter=256, seed=25),
     "sigmoid_nonorm": dict(hidden=512, n_exp=64, n_used=6, inter=256, scoring="sigmoid", bias=True, seed=26),
+    # the numpy K2 drivers' renormalisation (norm_w = 2: no clamp, numpy's pairwise sum order)
+    "sigmoid_k2_driver_renorm": dict(hidden=7168, n_exp=384, n_used=8, inter=256, scoring="sigmoid", w_scale=2.827,
+                                     bias=True, seed=28),
+    "sigmoid_k2_driver_renorm_k12": dict(hidden=512, n_exp=96, n_used=12, inter=256, scoring="sigmoid",
+                                         w_scale=2.5, bias=True, seed=29),
 }
 
 
@@ -65,6 +70,8 @@ def test_router_bitexact(dlib, port, name):
     layer = synth.make_layer(zipf=zipf, **c)
     if name == "sigmoid_nonorm":
         layer.norm_w = 0
+    if name.startswith("sigmoid_k2_driver"):
+        layer.norm_w = 2
     X = synth.make_tokens(layer, 48, c["seed"], zipf=zipf)
     o_gpu, w_gpu = dm.route(layer, X)
     o_ref, w_ref = port.route(layer, X)
