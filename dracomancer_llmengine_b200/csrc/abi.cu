@@ -235,6 +235,7 @@ struct Ctx {
     cudaEvent_t legacy_event = nullptr;   // orders the library stream after the legacy default stream
     cudaStream_t aux_stream = nullptr;    // second copy stream: large host->device copies run as two halves
     cudaEvent_t aux_fork = nullptr, aux_join = nullptr;
+    int* h_status = nullptr;              // page-locked [2]: status words read back by graph-replayed host calls
     // set once a call was captured into an application's CUDA graph: that graph keeps the
     // workspace addresses, so a workspace that is outgrown is retired instead of freed
     bool ws_captured = false;
@@ -291,7 +292,8 @@ Ctx* get_ctx() {
             cudaEventCreateWithFlags(&c->legacy_event, cudaEventDisableTiming) != cudaSuccess ||
             cudaStreamCreateWithFlags(&c->aux_stream, cudaStreamNonBlocking) != cudaSuccess ||
             cudaEventCreateWithFlags(&c->aux_fork, cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&c->aux_join, cudaEventDisableTiming) != cudaSuccess) {
+            cudaEventCreateWithFlags(&c->aux_join, cudaEventDisableTiming) != cudaSuccess ||
+            cudaMallocHost((void**)&c->h_status, 2 * sizeof(int)) != cudaSuccess) {
             set_err("CUDA context set-up failed: %s", cudaGetErrorString(cudaGetLastError()));
             delete c;
             return nullptr;
@@ -735,6 +737,15 @@ struct LayerBufs {
 // the fused single-launch decode layer (DRACO_B200_FUSED_DECODE=0 or draco_b200_set_fused_decode
 // turn it off); g_fd_extra: test hook, grid barrier arrivals the fused kernel waits for beyond
 // its own blocks (a block that never arrives)
+// graph replay of synchronous calls on page-locked host buffers (DRACO_B200_HOST_GRAPH=0: off)
+bool host_graph_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("DRACO_B200_HOST_GRAPH");
+        v = e ? (atoi(e) != 0) : 1;
+    }
+    return v != 0;
+}
 int g_fused_decode = -1;
 int g_fd_extra = 0;
 bool fused_decode_enabled() {
@@ -898,7 +909,11 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         f.q6s = a.tab->q6s;
         f.bar_extra = g_fd_extra;
         static unsigned long long* fd_stamps = nullptr;   // DRACO_B200_FD_STATS=1: phase timestamps
-        if (!fd_stamps && env_flag("DRACO_B200_FD_STATS")) cudaMallocManaged(&fd_stamps, sizeof(unsigned long long) * 8 * 4096);
+        if (!fd_stamps && env_flag("DRACO_B200_FD_STATS")) {
+            // device memory (a managed buffer would migrate to the host and back between calls)
+            cudaMalloc(&fd_stamps, sizeof(unsigned long long) * 64 * 4096);
+            cudaMemset(fd_stamps, 0, sizeof(unsigned long long) * 64 * 4096);
+        }
         f.stamps = fd_stamps;
         CK(cudaMemsetAsync(b.fd_ctl, 0, 4 * sizeof(int), s));
         int rc;
@@ -913,19 +928,27 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
             if (fd_stamps) {
                 // per phase: median and max over the blocks of the time since the block started
                 cudaStreamSynchronize(s);
+                std::vector<unsigned long long> hs((size_t)64 * 4096);
+                cudaMemcpy(hs.data(), fd_stamps, sizeof(unsigned long long) * hs.size(), cudaMemcpyDeviceToHost);
+                cudaMemset(fd_stamps, 0, sizeof(unsigned long long) * hs.size());
+                const unsigned long long* st = hs.data();
                 int G = 0;
-                while (G < 4096 && fd_stamps[(size_t)G * 8] != 0) G++;
+                while (G < 4096 && st[(size_t)G * 64] != 0) G++;
                 fprintf(stderr, "[fused decode stats] blocks=%d", G);
                 static const char* nm[7] = {"start", "A", "bar1", "S", "B", "bar2", "C"};
                 for (int i = 1; i < 7; i++) {
                     std::vector<double> v;
                     for (int g = 0; g < G; g++)
-                        if (fd_stamps[(size_t)g * 8 + i]) v.push_back((fd_stamps[(size_t)g * 8 + i] - fd_stamps[(size_t)g * 8]) * 1e-3);
+                        if (st[(size_t)g * 64 + i]) v.push_back((st[(size_t)g * 64 + i] - st[(size_t)g * 64]) * 1e-3);
                     std::sort(v.begin(), v.end());
                     if (!v.empty()) fprintf(stderr, " %s=%.1f/%.1fus", nm[i], v[v.size() / 2], v.back());
                 }
+                fprintf(stderr, "\n[fused decode jobs, block 0: issued/taken us]");
+                for (int j = 0; j < 24; j++) {
+                    const unsigned long long t0 = st[0], a = st[8 + j], b = st[32 + j];
+                    if (a || b) fprintf(stderr, " %d:%.1f/%.1f", j, a ? (a - t0) * 1e-3 : -1.0, b ? (b - t0) * 1e-3 : -1.0);
+                }
                 fprintf(stderr, "\n");
-                memset(fd_stamps, 0, sizeof(unsigned long long) * 8 * 4096);
             }
             return 0;
         }
@@ -1266,8 +1289,6 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
         b.x = const_cast<float*>(x);
         d_out = out;
         b.out = out;
-    } else {
-        if (int rc = h2d(c, b.x, x, sizeof(float) * (size_t)T * n_in, s)) return rc;
     }
     auto body = [&]() -> int {
         if (gr && gr->order) {
@@ -1307,6 +1328,49 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
         const int rc = captured ? body() : graph_call(c, key, s, body);
         if (!captured) ws_release(c, s);
         return rc;
+    }
+    // synchronous call on page-locked host buffers: the copies and the launches replay as one
+    // captured graph; the status words come back through the context's page-locked buffer
+    const bool host_graph = !dev_io && !captured && !gr && host_graph_enabled() && is_pinned_host(x) &&
+                            is_pinned_host(out) && (!order_out || is_pinned_host(order_out)) &&
+                            (!wtop_out || is_pinned_host(wtop_out));
+    if (host_graph) {
+        auto body_h = [&]() -> int {
+            if (int rc = h2d(c, b.x, x, sizeof(float) * (size_t)T * n_in, s)) return rc;
+            if (int rc = body()) return rc;
+            CK(cudaMemcpyAsync(out, d_out, sizeof(float) * (size_t)T * n_out, cudaMemcpyDeviceToHost, s));
+            if (order_out) CK(cudaMemcpyAsync(order_out, b.rb.order, sizeof(int) * T * n_used, cudaMemcpyDeviceToHost, s));
+            if (wtop_out) CK(cudaMemcpyAsync(wtop_out, b.rb.wtop, sizeof(float) * T * n_used, cudaMemcpyDeviceToHost, s));
+            CK(cudaMemcpyAsync(c->h_status, b.rb.err, sizeof(int), cudaMemcpyDeviceToHost, s));
+            CK(cudaMemcpyAsync(c->h_status + 1, b.tc_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+            return 0;
+        };
+        const std::vector<uint64_t> key = {
+            2, (uintptr_t)a.tab, (uintptr_t)a.sh, c->gen, (uintptr_t)c->ws, c->ws_cap, (uintptr_t)a.d_gi,
+            (uintptr_t)a.rp.probs_b, (uintptr_t)x, (uintptr_t)out, (uintptr_t)order_out, (uintptr_t)wtop_out,
+            (uint64_t)T, (uintptr_t)s, (uint64_t)n_exp, (uint64_t)n_used, (uint64_t)inter, (uint64_t)n_in,
+            (uint64_t)n_out, (uint64_t)a.sh_ff, (uint64_t)a.rp.scoring, (uint64_t)a.rp.n_group,
+            (uint64_t)a.rp.n_group_used, (uint64_t)a.rp.norm_w, (uint64_t)__float_as_uint_host(a.rp.w_scale),
+            (uint64_t)gemm_path(), (uint64_t)g_act_mode, (uint64_t)b.use_tc, (uint64_t)fused_decode_enabled()};
+        if (int rc = graph_call(c, key, s, body_h)) return rc;
+        ws_release(c, s);
+        CK(cudaStreamSynchronize(s));
+        const int h_err = c->h_status[0], h_tc = c->h_status[1];
+        if (h_tc) {
+            set_err("expert GEMM stopped after a bounded wait ran out (code 0x%x)", h_tc);
+            return -5;
+        }
+        if (h_err) {
+            set_err("routing found fewer eligible experts than n_used (group limit or non-finite scores), code %d",
+                    h_err);
+            return -2;
+        }
+        m6_prof_t[23] += now_s() - t0;
+        m6_prof_n[23]++;
+        return 0;
+    }
+    if (!dev_io) {
+        if (int rc = h2d(c, b.x, x, sizeof(float) * (size_t)T * n_in, s)) return rc;
     }
     if (int rc = body()) return rc;
     if (dev_io) {

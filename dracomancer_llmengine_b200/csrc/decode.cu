@@ -326,10 +326,8 @@ int tile_rows(int rows, uint32_t row_bytes_) {
 // ------------------------------------------------------------------------------------------
 constexpr int kFdMaxTokens = 8;
 constexpr int kFdMaxAssign = 64;
-constexpr int kFdCompute = 4;
+constexpr int kFdCompute = 16;            // compute warps (the producer warp is warp 16)
 constexpr int kFdThreads = 32 * (kFdCompute + 1);
-constexpr int kFdKC = 128;                 // router k-chunk (floats)
-constexpr int kFdRS = kFdKC + 4;           // padded row stride of a chunk in shared memory
 constexpr int kFdMaxSlots = 4;
 constexpr uint64_t kFdGridWaitNs = 1000000000ull;
 
@@ -357,9 +355,17 @@ __device__ __forceinline__ void fd_scales(const uint8_t* tile, int rows, int nb,
         superblock_scales<CODE>(tile + (size_t)idx * bb, tab + (size_t)idx * scale_groups<CODE>());
 }
 
+// rows of n floats from global memory into shared memory by the compute threads (float4 loads
+// through L2: the rows may have been written by other blocks of this launch)
+__device__ __forceinline__ void fd_stage_rows(float* dst, const float* src, size_t n, int tid) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (size_t i = tid; i < n / 4; i += 32 * kFdCompute) d4[i] = __ldcg(s4 + i);
+}
+
 // optional phase timestamps (DRACO_B200_FD_STATS): thread 0 of each block
 __device__ __forceinline__ void fd_stamp(const FusedDecodeArgs& a, int i) {
-    if (a.stamps && threadIdx.x == 0) a.stamps[(size_t)blockIdx.x * 8 + i] = sync::global_ns();
+    if (a.stamps && threadIdx.x == 0) a.stamps[(size_t)blockIdx.x * 64 + i] = sync::global_ns();
 }
 
 template <int CG, int CU, int CD, int NS>
@@ -378,9 +384,11 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
     const int S = a.n_slots;
     const bool sh = a.sh_ff > 0;
     uint8_t* ring = dsm;
-    float* V = reinterpret_cast<float*>(dsm + (size_t)S * a.slot_bytes);      // [5][E]
-    float* gsm = V + (kFdCompute + 1) * E;                                      // [5][64]
-    int* s_order = reinterpret_cast<int*>(gsm + (kFdCompute + 1) * 64);          // [64]
+    float* xs = reinterpret_cast<float*>(dsm + (size_t)S * a.slot_bytes);      // [xs_cap] token / act rows
+    const int ES = (E + 3) & ~3;                                                // 16-byte aligned rows
+    float* V = xs + a.xs_cap;                                                   // [8][ES] selection scratch
+    float* gsm = V + kFdMaxTokens * ES;                                         // [8][64]
+    int* s_order = reinterpret_cast<int*>(gsm + kFdMaxTokens * 64);              // [64]
     float* s_wtop = reinterpret_cast<float*>(s_order + kFdMaxAssign);            // [64]
     int* act_e = reinterpret_cast<int*>(s_wtop + kFdMaxAssign);                  // [64]
     int* act_cnt = act_e + kFdMaxAssign;                                         // [64]
@@ -412,6 +420,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             s_pabort = 1;
             return nullptr;
         }
+        if (a.stamps && q < 24) a.stamps[(size_t)blockIdx.x * 64 + 8 + q] = sync::global_ns();
         return ring + (size_t)sl * a.slot_bytes;
     };
     // compute threads: job q's slot, nullptr (uniformly) after a failed wait
@@ -422,6 +431,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             s_cabort = 1;
         }
         fd_compute_sync();
+        if (a.stamps && ctid == 0 && q < 24) a.stamps[(size_t)blockIdx.x * 64 + 32 + q] = sync::global_ns();
         if (s_cabort) return nullptr;
         return ring + (size_t)sl * a.slot_bytes;
     };
@@ -435,7 +445,8 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
     // ---------------------------------------------------------------- phase A: router logits
     const int C = T * E;
     const int nch = (a.W && b < C) ? (C - 1 - b) / G + 1 : 0;
-    const int n_chunks = H / kFdKC;
+    const int KC = a.kc, RS = a.kc + 4;
+    const int n_chunks = H / KC;
     if (nch > 0) {
         if (producer) {
             if (lane == 0)
@@ -443,15 +454,15 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                     uint8_t* dst = claim();
                     if (!dst) break;
                     const int sl = q % S;
-                    sync::mbar_expect_tx(&full[sl], (uint32_t)(nch + T) * kFdKC * 4);
+                    sync::mbar_expect_tx(&full[sl], (uint32_t)(nch + T) * KC * 4);
                     for (int i = 0; i < nch; i++) {
                         const int e = (b + G * i) % E;
-                        sync::bulk_load(dst + (size_t)i * kFdRS * 4, a.W + (size_t)e * H + (size_t)ch * kFdKC,
-                                        kFdKC * 4, &full[sl]);
+                        sync::bulk_load(dst + (size_t)i * RS * 4, a.W + (size_t)e * H + (size_t)ch * KC, KC * 4,
+                                        &full[sl]);
                     }
                     for (int t = 0; t < T; t++)
-                        sync::bulk_load(dst + (size_t)(nch + t) * kFdRS * 4, a.X + (size_t)t * H + (size_t)ch * kFdKC,
-                                        kFdKC * 4, &full[sl]);
+                        sync::bulk_load(dst + (size_t)(nch + t) * RS * 4, a.X + (size_t)t * H + (size_t)ch * KC,
+                                        KC * 4, &full[sl]);
                     q++;
                 }
         } else {
@@ -466,10 +477,10 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                     break;
                 }
                 if (warp == 0 && lane < nch) {
-                    const float4* w4 = reinterpret_cast<const float4*>(src + (size_t)lane * kFdRS * 4);
-                    const float4* x4 = reinterpret_cast<const float4*>(src + (size_t)(nch + ct) * kFdRS * 4);
+                    const float4* w4 = reinterpret_cast<const float4*>(src + (size_t)lane * RS * 4);
+                    const float4* x4 = reinterpret_cast<const float4*>(src + (size_t)(nch + ct) * RS * 4);
 #pragma unroll 8
-                    for (int k = 0; k < kFdKC / 4; k++) {
+                    for (int k = 0; k < KC / 4; k++) {
                         const float4 w = w4[k], x = x4[k];
                         acc = __fadd_rn(acc, __fmul_rn(x.x, w.x));
                         acc = __fadd_rn(acc, __fmul_rn(x.y, w.y));
@@ -497,8 +508,8 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
     // ---------------------------------------------------------------- phase S: routing
     if (ok) {
         if (a.W) {
-            for (int t = warp; t < T; t += kFdCompute + 1) {
-                float* Vw = V + (size_t)warp * E;
+            for (int t = warp; t < T && warp < kFdMaxTokens; t += kFdMaxTokens) {
+                float* Vw = V + (size_t)warp * ES;
                 for (int e = lane; e < E; e += 32) Vw[e] = __ldcg(a.logits + (size_t)t * E + e);
                 __syncwarp();
                 select_token<NS>(a.rp, Vw, s_order + t * K, s_wtop + t * K, a.route_err, Vw, gsm + warp * 64);
@@ -562,6 +573,10 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
     const int items_b = ok ? n_act * tiles_f + tiles_fs : 0;
     const int items_c = ok ? a.n_out / rt_c : 0;
     const int exp_c = n_act + (sh ? 1 : 0);
+    const int cg_sz = a.c_group;                           // experts per phase-C job
+    // bytes of one expert's down tile in a phase-C slot: data, then its scale table
+    const uint32_t tile_c = (uint32_t)rt_c * (rbd > rbds ? rbd : rbds) +
+                            (uint32_t)rt_c * (nbd > nbds ? nbd : nbds) * scale_groups<CD>() * 8;
     if (producer) {
         // B jobs then C jobs, back to back (C's weight tiles do not wait for the activations)
         if (lane == 0) {
@@ -590,24 +605,38 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                 q++;
             }
             for (int j = b; j < items_c && go; j += G) {
-                for (int x = 0; x < exp_c; x++) {
+                for (int x0 = 0; x0 < exp_c; x0 += cg_sz) {
                     uint8_t* dst = claim();
                     if (!dst) {
                         go = false;
                         break;
                     }
-                    const bool shx = x == n_act;
-                    const uint32_t rb = shx ? rbds : rbd;
-                    const uint8_t* src = shx ? a.sh_d : a.tab.w[3 * act_e[x] + 2];
+                    const int x1 = min(exp_c, x0 + cg_sz);
+                    uint32_t bytes = 0;
+                    for (int x = x0; x < x1; x++) bytes += (uint32_t)rt_c * (x == n_act ? rbds : rbd);
                     const int sl = q % S;
-                    sync::mbar_expect_tx(&full[sl], (uint32_t)rt_c * rb);
-                    sync::bulk_load(dst, src + (size_t)j * rt_c * rb, rt_c * rb, &full[sl]);
+                    sync::mbar_expect_tx(&full[sl], bytes);
+                    for (int x = x0; x < x1; x++) {
+                        const bool shx = x == n_act;
+                        const uint32_t rb = shx ? rbds : rbd;
+                        const uint8_t* src = shx ? a.sh_d : a.tab.w[3 * act_e[x] + 2];
+                        sync::bulk_load(dst + (size_t)(x - x0) * tile_c, src + (size_t)j * rt_c * rb, rt_c * rb,
+                                        &full[sl]);
+                    }
                     q++;
                 }
             }
         }
     } else {
-        const int rpw = rt_b / kFdCompute, r0 = warp * rpw;
+        // token rows in shared memory when they fit (one L2 round trip instead of one per superblock)
+        const bool x_in_smem = (size_t)T * H <= (size_t)a.xs_cap;
+        if (ok && x_in_smem) fd_stage_rows(xs, a.X, (size_t)T * H, ctid);
+        fd_compute_sync();
+        const float* xbase = x_in_smem ? xs : a.X;
+        // rows of a gate/up tile over the compute warps: warp w takes rows [w * rpw, +rpw)
+        const int rpw = (rt_b + kFdCompute - 1) / kFdCompute;
+        const int r0 = warp * rpw;
+        const int my_rows = max(0, min(rpw, rt_b - r0));
         for (int j = b; j < items_b && ok; j += G) {
             uint8_t* tile = take();
             if (!tile) {
@@ -625,7 +654,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             fd_scales<CG>(sg, rt_b, nb, bg, tg, ctid, 32 * kFdCompute);
             fd_scales<CU>(su, rt_b, nb, bu, tu, ctid, 32 * kFdCompute);
             fd_compute_sync();
-            for (int tc = 0; tc < cnt; tc += 2) {
+            for (int tc = 0; tc < cnt && my_rows > 0; tc += 2) {
                 const int nt = min(2, cnt - tc);
                 const float* xr[2];
                 int slot[2];
@@ -634,14 +663,14 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                     const int m = tc + min(jj, nt - 1);
                     const int i = shx ? m : act_asg[ax * kFdMaxTokens + m];
                     slot[jj] = i;
-                    xr[jj] = a.X + (size_t)(shx ? i : i / K) * H;
+                    xr[jj] = xbase + (size_t)(shx ? i : i / K) * H;
                 }
                 float ag[4][2], au[4][2];
-                if (nt == 2) rows_dot<CG, CU, true, 2>(sg, tg, su, tu, rbg, rbu, bg, bu, nb, r0, rpw, xr, lane, ag, au);
-                else rows_dot<CG, CU, true, 1>(sg, tg, su, tu, rbg, rbu, bg, bu, nb, r0, rpw, xr, lane, ag, au);
+                if (nt == 2) rows_dot<CG, CU, true, 2>(sg, tg, su, tu, rbg, rbu, bg, bu, nb, r0, my_rows, xr, lane, ag, au);
+                else rows_dot<CG, CU, true, 1>(sg, tg, su, tu, rbg, rbu, bg, bu, nb, r0, my_rows, xr, lane, ag, au);
 #pragma unroll
                 for (int r = 0; r < 4; r++) {
-                    if (r < rpw) {
+                    if (r < my_rows) {
 #pragma unroll
                         for (int jj = 0; jj < 2; jj++) {
                             if (jj < nt) {
@@ -670,47 +699,81 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
         fd_compute_sync();
         fd_stamp(a, 5);
         ok = !s_cabort;
-        const int rpc = rt_c / kFdCompute, c0 = warp * rpc;
+        // the activation rows of every assignment (and the shared expert's) in shared memory
+        const size_t act_n = (size_t)NA * F + (sh ? (size_t)T * a.sh_ff : 0);
+        const bool a_in_smem = items_c > 0 && act_n <= (size_t)a.xs_cap;
+        if (ok && a_in_smem) {
+            fd_stage_rows(xs, a.act, (size_t)NA * F, ctid);
+            if (sh) fd_stage_rows(xs + (size_t)NA * F, a.act_sh, (size_t)T * a.sh_ff, ctid);
+        }
+        fd_compute_sync();
+        const float* abase = a_in_smem ? xs : a.act;
+        const float* sbase = a_in_smem ? xs + (size_t)NA * F : a.act_sh;
+        // row-dot tasks of a down job over the compute warps: task = (tile in the group, rpc rows)
+        const int rpc = rt_c >= 8 ? 2 : 1;
+        const int tasks_per_tile = rt_c / rpc;
         for (int j = b; j < items_c && ok; j += G) {
-            for (int x = 0; x < exp_c; x++) {
-                uint8_t* tile = take();
-                if (!tile) {
+            for (int x0 = 0; x0 < exp_c && ok; x0 += cg_sz) {
+                uint8_t* slotp = take();
+                if (!slotp) {
                     ok = false;
                     break;
                 }
-                const bool shx = x == n_act;
-                const int cnt = shx ? T : act_cnt[x];
-                const int nbx = shx ? nbds : nbd;
-                const uint32_t rb = shx ? rbds : rbd;
-                float2* td = reinterpret_cast<float2*>(tile + rt_c * rb);
-                fd_scales<CD>(tile, rt_c, nbx, bd, td, ctid, 32 * kFdCompute);
+                const int x1 = min(exp_c, x0 + cg_sz);
+                for (int x = x0; x < x1; x++) {
+                    const bool shx = x == n_act;
+                    uint8_t* tile = slotp + (size_t)(x - x0) * tile_c;
+                    const int nbx = shx ? nbds : nbd;
+                    const uint32_t rb = shx ? rbds : rbd;
+                    fd_scales<CD>(tile, rt_c, nbx, bd, reinterpret_cast<float2*>(tile + rt_c * rb), ctid,
+                                  32 * kFdCompute);
+                }
                 fd_compute_sync();
-                for (int tc = 0; tc < cnt; tc += 2) {
-                    const int nt = min(2, cnt - tc);
-                    const float* xr[2];
-                    int slot[2];
+                for (int task = warp; task < (x1 - x0) * tasks_per_tile; task += kFdCompute) {
+                    const int x = x0 + task / tasks_per_tile;
+                    const int c0 = (task % tasks_per_tile) * rpc;
+                    const bool shx = x == n_act;
+                    uint8_t* tile = slotp + (size_t)(x - x0) * tile_c;
+                    const int cnt = shx ? T : act_cnt[x];
+                    const int nbx = shx ? nbds : nbd;
+                    const uint32_t rb = shx ? rbds : rbd;
+                    float2* td = reinterpret_cast<float2*>(tile + rt_c * rb);
+                    for (int tc = 0; tc < cnt; tc += 2) {
+                        const int nt = min(2, cnt - tc);
+                        const float* xr[2];
+                        int slot[2];
 #pragma unroll
-                    for (int jj = 0; jj < 2; jj++) {
-                        const int m = tc + min(jj, nt - 1);
-                        const int i = shx ? m : act_asg[x * kFdMaxTokens + m];
-                        slot[jj] = shx ? NA + i : i;
-                        xr[jj] = shx ? a.act_sh + (size_t)i * a.sh_ff : a.act + (size_t)i * F;
-                    }
-                    float ad[4][2], unused[4][2];
-                    if (nt == 2)
-                        rows_dot<CD, CD, false, 2, true>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0, rpc, xr,
-                                                         lane, ad, unused);
-                    else
-                        rows_dot<CD, CD, false, 1, true>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0, rpc, xr,
-                                                         lane, ad, unused);
+                        for (int jj = 0; jj < 2; jj++) {
+                            const int m = tc + min(jj, nt - 1);
+                            const int i = shx ? m : act_asg[x * kFdMaxTokens + m];
+                            slot[jj] = shx ? NA + i : i;
+                            xr[jj] = shx ? sbase + (size_t)i * a.sh_ff : abase + (size_t)i * F;
+                        }
+                        float ad[4][2], unused[4][2];
+                        if (a_in_smem) {
+                            if (nt == 2)
+                                rows_dot<CD, CD, false, 2>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0, rpc, xr,
+                                                           lane, ad, unused);
+                            else
+                                rows_dot<CD, CD, false, 1>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0, rpc, xr,
+                                                           lane, ad, unused);
+                        } else {
+                            if (nt == 2)
+                                rows_dot<CD, CD, false, 2, true>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0,
+                                                                 rpc, xr, lane, ad, unused);
+                            else
+                                rows_dot<CD, CD, false, 1, true>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0,
+                                                                 rpc, xr, lane, ad, unused);
+                        }
 #pragma unroll
-                    for (int r = 0; r < 4; r++) {
-                        if (r < rpc) {
+                        for (int r = 0; r < 4; r++) {
+                            if (r < rpc) {
 #pragma unroll
-                            for (int jj = 0; jj < 2; jj++) {
-                                if (jj < nt) {
-                                    const float v = warp_sum(ad[r][jj]);
-                                    if (lane == 0) ys[slot[jj] * rt_c + c0 + r] = v;
+                                for (int jj = 0; jj < 2; jj++) {
+                                    if (jj < nt) {
+                                        const float v = warp_sum(ad[r][jj]);
+                                        if (lane == 0) ys[slot[jj] * rt_c + c0 + r] = v;
+                                    }
                                 }
                             }
                         }
@@ -813,40 +876,58 @@ int launch_fused_decode(FusedDecodeArgs a, int cg, int cu, int cd, cudaStream_t 
         cudaGetLastError();
         return 1;
     }
+    const int G = sms;   // one block per SM
     const int nb = H / 256, nbd = a.F / 256, nbds = a.sh_ff / 256;
     const size_t rbg = (size_t)nb * superblock_bytes(cg, a.q6s), rbu = (size_t)nb * superblock_bytes(cu, a.q6s);
     const size_t rbd = (size_t)nbd * superblock_bytes(cd, a.q6s), rbds = (size_t)nbds * superblock_bytes(cd, a.q6s);
+    constexpr size_t kSlotMax = 64 * 1024;
     auto slot_b = [&](int rt) { return (size_t)rt * (rbg + rbu) + (size_t)rt * nb * (groups_of(cg) + groups_of(cu)) * 8; };
-    auto slot_c = [&](int rt) {
-        return std::max((size_t)rt * rbd + (size_t)rt * nbd * groups_of(cd) * 8,
-                        a.sh_ff ? (size_t)rt * rbds + (size_t)rt * nbds * groups_of(cd) * 8 : (size_t)0);
+    auto tile_c = [&](int rt) {
+        return (size_t)rt * std::max(rbd, rbds) + (size_t)rt * std::max(nbd, nbds) * groups_of(cd) * 8;
     };
-    const int n_act_est = std::min(T * K, E);
-    auto plan = [&](int G, int& rt_b, int& rt_c, size_t& slot) {
-        // the largest tile with at least one item per block, else the smallest
-        static const int cand[4] = {16, 12, 8, 4};
-        rt_b = rt_c = 0;
-        for (int r : cand)
-            if (a.F % r == 0 && a.sh_ff % r == 0 && slot_b(r) <= 56u * 1024) {
-                rt_b = r;
-                if (n_act_est * (a.F / r) >= G) break;
-            }
-        for (int r : cand)
-            if (a.n_out % r == 0 && slot_c(r) <= 56u * 1024) {
-                rt_c = r;
-                if (a.n_out / r >= G) break;
-            }
-        if (!rt_b || !rt_c) return false;
-        const int nch_max = (T * E + G - 1) / G;
-        if (nch_max > 32) return false;
-        const size_t stage_a = (size_t)(nch_max + T) * kFdRS * 4;
-        slot = std::max({slot_b(rt_b), slot_c(rt_c), stage_a});
-        slot = (slot + 127) / 128 * 128;
-        return true;
-    };
-    const size_t extra = ((size_t)(kFdCompute + 1) * E + (kFdCompute + 1) * 64) * 4 + 2 * kFdMaxAssign * 4 +
-                         (2 * kFdMaxAssign + kFdMaxAssign * kFdMaxTokens) * 4 +
-                         (size_t)(kFdMaxAssign + kFdMaxTokens) * 16 * 4;
+    const int n_act_max = std::min(T * K, E);
+    const int exp_c_max = n_act_max + (a.sh_ff ? 1 : 0);
+    // tile rows: the largest with at least one item per block, else the smallest that fits
+    static const int cand[4] = {16, 12, 8, 4};
+    int rt_b = 0, rt_c = 0;
+    for (int r : cand)
+        if (a.F % r == 0 && a.sh_ff % r == 0 && slot_b(r) <= kSlotMax) {
+            rt_b = r;
+            if (n_act_max * (a.F / r) >= G) break;
+        }
+    for (int r : cand)
+        if (a.n_out % r == 0 && tile_c(r) <= kSlotMax) {
+            rt_c = r;
+            if (a.n_out / r >= G) break;
+        }
+    if (!rt_b || !rt_c) return 1;
+    // experts per down job: as many tiles as a slot holds, split evenly over the jobs
+    const int gmax = std::max(1, (int)(kSlotMax / tile_c(rt_c)));
+    const int njobs = (exp_c_max + gmax - 1) / gmax;
+    const int c_group = (exp_c_max + njobs - 1) / njobs;
+    // router chunk: the longest of 512 / 256 / 128 values whose stage fits a slot
+    const int nch_max = (T * E + G - 1) / G;
+    if (nch_max > 32) return 1;
+    auto stage_a = [&](int kc) { return (size_t)(nch_max + T) * (kc + 4) * 4; };
+    const size_t slot_bc = std::max(slot_b(rt_b), (size_t)c_group * tile_c(rt_c));
+    int kc = 128;
+    for (int c : {512, 256})
+        if (H % c == 0 && stage_a(c) <= std::max(slot_bc, (size_t)8192)) {
+            kc = c;
+            break;
+        }
+    size_t slot = std::max(slot_bc, stage_a(kc));
+    slot = (slot + 127) / 128 * 128;
+    // token rows (phase B) / activation rows (phase C) staged in shared memory up to 64 KB
+    const size_t rows_b = (size_t)T * H, rows_c = (size_t)T * K * a.F + (size_t)T * a.sh_ff;
+    const int xs_cap = (int)std::min<size_t>(16384, std::max(rows_b, rows_c));
+    const size_t extra = (size_t)xs_cap * 4 + ((size_t)kFdMaxTokens * ((E + 3) & ~3) + kFdMaxTokens * 64) * 4 +
+                         2 * kFdMaxAssign * 4 + (2 * kFdMaxAssign + kFdMaxAssign * kFdMaxTokens) * 4 +
+                         (size_t)(kFdMaxAssign + kFdMaxTokens) * 16 * 4 + 256;
+    int slots = kFdMaxSlots;
+    while (slots > 2 && slots * slot + extra > 220u * 1024) slots--;
+    const size_t total = slots * slot + extra;
+    if (total > 220u * 1024) return 1;
     const void* kern = nullptr;
     const int ns = E <= 128 ? 4 : E <= 256 ? 8 : 16;
     constexpr int Q4 = DRACO_CODE_Q4_K, Q6 = DRACO_CODE_Q6_K;
@@ -861,32 +942,22 @@ int launch_fused_decode(FusedDecodeArgs a, int cg, int cu, int cd, cudaStream_t 
     DRACO_FD_PICK(Q6, Q4)
 #undef DRACO_FD_PICK
     if (!kern) return 1;
-    // blocks per SM from the occupancy of the planned shared memory (2 when it fits)
-    int rt_b = 0, rt_c = 0, slots = kFdMaxSlots, G = 0;
-    size_t slot = 0, total = 0;
-    for (int bps = 2; bps >= 1 && !G; bps--) {
-        if (!plan(sms * bps, rt_b, rt_c, slot)) continue;
-        for (slots = kFdMaxSlots; slots >= 2; slots--) {
-            total = slots * slot + extra;
-            if (total * bps <= 220u * 1024) break;
-        }
-        if (slots < 2) continue;
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess) {
-            cudaGetLastError();
-            return 1;
-        }
-        int occ = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kFdThreads, total) != cudaSuccess) {
-            cudaGetLastError();
-            return 1;
-        }
-        if (occ >= bps) G = sms * bps;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess) {
+        cudaGetLastError();
+        return 1;
     }
-    if (!G) return 1;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kFdThreads, total) != cudaSuccess || occ < 1) {
+        cudaGetLastError();
+        return 1;
+    }
     a.rt_b = rt_b;
     a.rt_c = rt_c;
     a.slot_bytes = (int)slot;
     a.n_slots = slots;
+    a.kc = kc;
+    a.c_group = c_group;
+    a.xs_cap = xs_cap;
     void* args[] = {&a};
     const cudaError_t e = cudaLaunchCooperativeKernel(kern, G, kFdThreads, args, total, s);
     if (e != cudaSuccess) {

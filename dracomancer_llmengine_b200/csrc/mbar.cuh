@@ -8,6 +8,11 @@ namespace draco {
 namespace sync {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s
+// try_wait may suspend the polling thread up to this long (0: poll with test_wait)
+#ifndef DRACO_MBAR_SUSPEND_NS
+#define DRACO_MBAR_SUSPEND_NS 1000
+#endif
+constexpr uint32_t kSuspendNs = DRACO_MBAR_SUSPEND_NS;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -22,11 +27,18 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 }
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity), "r"(1000u)
-        : "memory");
+    if (kSuspendNs == 0)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_addr(bar)), "r"(parity)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendNs)
+            : "memory");
     return ok != 0;
 }
 __device__ __forceinline__ uint64_t global_ns() {

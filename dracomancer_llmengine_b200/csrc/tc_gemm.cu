@@ -42,16 +42,26 @@
 #ifndef DRACO_TC_RAW_STAGES_Q6K
 #define DRACO_TC_RAW_STAGES_Q6K 3
 #endif
-// 64-token tiles (decode and lightly loaded experts): fewer activation stages (their rows come
-// from L2), deeper weight rings (measured: 1.6 % faster on the K2 decode shape, 1 % on cfg2)
+// 64-token tiles (decode and lightly loaded experts): 8 activation stages and 5 (Q4_K) / 3 (Q6_K)
+// weight stages.  The MMAs of a K step need both its A slot and its activation stage, and an
+// activation stage is reused only after the MMAs of the step it held finished, so with 4 stages
+// the activation TMA latency (rows from L2) held the MMA warps (per-site wait counters, cfg2)
 #ifndef DRACO_TC_B_STAGES_64
-#define DRACO_TC_B_STAGES_64 4
+#define DRACO_TC_B_STAGES_64 8
 #endif
 #ifndef DRACO_TC_RAW_STAGES_Q4K_64
-#define DRACO_TC_RAW_STAGES_Q4K_64 8
+#define DRACO_TC_RAW_STAGES_Q4K_64 5
 #endif
 #ifndef DRACO_TC_RAW_STAGES_Q6K_64
-#define DRACO_TC_RAW_STAGES_Q6K_64 5
+#define DRACO_TC_RAW_STAGES_Q6K_64 3
+#endif
+// 64-token tiles: MMA issuer warps (2: even and odd K steps into separate accumulators) and
+// A slots in TMEM (2 * issuers * 64 accumulator columns + 64 per slot <= 512)
+#ifndef DRACO_TC_ISSUERS_64
+#define DRACO_TC_ISSUERS_64 2
+#endif
+#ifndef DRACO_TC_SLOTS_64
+#define DRACO_TC_SLOTS_64 4
 #endif
 #ifndef DRACO_TC_SUSPEND_NS
 #define DRACO_TC_SUSPEND_NS 1000
@@ -67,11 +77,10 @@ constexpr int kBProdWarp = 18;                // TMA producer of the activation 
 constexpr int kEpiWarp0 = 19;                 // epilogue warpgroup: warps 19..22
 constexpr int kMmaWarp2 = 23;                 // second MMA issuer (odd K steps; 64-token tiles)
 constexpr int kMaxRawStages = 8;              // raw superblock-column stages
-constexpr int kSlots = 4;                     // A slots in TMEM (K steps decoded ahead of the MMAs)
+constexpr int kMaxSlots = 8;                  // A slots in TMEM (K steps decoded ahead of the MMAs), most
 constexpr int kDone = 8;                      // ring of per-step completion barriers (>= every stage count)
 constexpr int kMaxBStages = 8;                // activation stages
 constexpr int kTmemCols = 512;
-constexpr int kABase = 256;                   // A slots (64 columns each) start here
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // bounded waits give up after 2 s
 // try_wait may suspend the polling thread up to this long (0: poll with test_wait)
 constexpr uint32_t kSuspendNs = DRACO_TC_SUSPEND_NS;
@@ -361,12 +370,20 @@ __device__ __forceinline__ void q4k_sm_words(uint32_t s0, uint32_t s1, uint32_t 
 struct Q4Sub {
     __half2 sc16, off, d, c;
 };
-__device__ __forceinline__ Q4Sub q4_sub(float d, float dmin, int sc, int mn) {
+// small non-negative integer (< 2^23) to float without the conversion unit: 2^23 + v in the
+// mantissa, minus 2^23 (exact)
+__device__ __forceinline__ float small_int_f(int v) { return __int_as_float(0x4B000000 + v) - 8388608.f; }
+// d_bits: the superblock's fp16 d; d, dmin: as floats
+__device__ __forceinline__ Q4Sub q4_sub(uint32_t d_bits, float d, float dmin, int sc, int mn) {
     Q4Sub r;
-    r.sc16 = __float2half2_rn((float)sc * 0.0625f);
-    r.off = __float2half2_rn((float)(-72 * sc));
-    r.d = __float2half2_rn(d);
-    r.c = __float2half2_rn(__fsub_rn(8.f * d * (float)sc, dmin * (float)mn));
+    // sc / 16 exactly: fp16 1024 + sc (bits 0x6400 + sc) times 1/16 minus 64; both halves
+    const __half2 h = u2h2((0x6400u + (uint32_t)sc) * 0x00010001u);
+    r.sc16 = __hfma2(h, __float2half2_rn(0.0625f), __float2half2_rn(-64.f));
+    r.off = __hmul2(r.sc16, __float2half2_rn(-1152.f));   // -72 sc, exact
+    r.d = u2h2(d_bits * 0x00010001u);
+    const float scf = small_int_f(sc), mnf = small_int_f(mn);
+    const float cf = __fsub_rn(8.f * d * scf, dmin * mnf);
+    r.c = __floats2half2_rn(cf, cf);
     return r;
 }
 __device__ __forceinline__ uint32_t q4_pair(uint32_t hbits, const Q4Sub& k) {
@@ -381,7 +398,7 @@ __device__ __forceinline__ void deq_q4k(const uint8_t* blk, int kc, uint32_t (&o
     int sc0, m0, sc1, m1;
     q4k_sm_words(hd.y, hd.z, hd.w, 2 * kc, sc0, m0);
     q4k_sm_words(hd.y, hd.z, hd.w, 2 * kc + 1, sc1, m1);
-    const Q4Sub k0 = q4_sub(d, dmin, sc0, m0), k1 = q4_sub(d, dmin, sc1, m1);
+    const Q4Sub k0 = q4_sub(hd.x & 0xffffu, d, dmin, sc0, m0), k1 = q4_sub(hd.x & 0xffffu, d, dmin, sc1, m1);
     const uint4* qv = reinterpret_cast<const uint4*>(blk + 16 + 32 * kc);
     constexpr uint32_t kMask = 0x00F000F0u, kMagic = 0x64006400u;
 #pragma unroll
@@ -419,7 +436,8 @@ __device__ __forceinline__ void deq_q6k(const uint8_t* blk, int kc, uint32_t (&o
     // ql byte 16g + i of this half, qh byte 16(g & 1) + i, 2-bit field at (2 nhi + g/2) * 2
 #pragma unroll
     for (int g = 0; g < 4; g++) {
-        const float S = d * (float)(int8_t)(scw >> (8 * g));
+        // int8 scale to float without the conversion unit: (sc + 128) via the mantissa, minus 128
+        const float S = d * (small_int_f((int)((scw >> (8 * g)) & 0xffu) ^ 0x80) - 128.f);
         const __half shi = __float2half_rn(S);
         const __half2 s_hi = __half2half2(shi);
         const __half2 s_lo = __float2half2_rn(__fsub_rn(S, __half2float(shi)));
@@ -446,7 +464,10 @@ __device__ __forceinline__ void deq_q6k(const uint8_t* blk, int kc, uint32_t (&o
 // overheads (readiness test, commit) then overlap.
 template <int MODE, int CODE, int NT>
 struct Cfg {
-    static constexpr int kIssuers = NT == 64 ? 2 : 1;
+    static constexpr int kIssuers = NT == 64 ? DRACO_TC_ISSUERS_64 : 1;
+    // TMEM: 2 accumulator buffers (kIssuers x NT columns each), then the A slots of 64 columns
+    static constexpr int kABase = 2 * kIssuers * NT;
+    static constexpr int kSlots = NT == 64 ? DRACO_TC_SLOTS_64 : 4;
     static constexpr int kThreads = 32 * (NT == 64 ? 24 : 23);
     // TMEM columns of accumulator (buffer b, issuer i): b * kAccStride + i * NT
     static constexpr int kAccStride = kIssuers * NT;
@@ -463,7 +484,8 @@ struct Cfg {
     static constexpr int kBarOff = kBOffAligned + kBStages * kBStage;
     static constexpr int kSmem = kBarOff + 1024 + 1024;                    // barriers + alignment slack
     static_assert(kRawStages <= kMaxRawStages && kBStages <= kMaxBStages && kBStages <= kDone &&
-                      kSlots <= kDone && kSmem <= 232448,
+                      kSlots <= kDone && kSlots <= kMaxSlots && kABase + 64 * kSlots <= kTmemCols &&
+                      kSmem <= 232448,
                   "rings and shared memory");
 };
 
@@ -473,7 +495,7 @@ using ActMaps = TcActMaps;
 
 struct Bars {
     uint64_t raw_full[kMaxRawStages], raw_empty[kMaxRawStages];
-    uint64_t a_full[kSlots], b_full[kMaxBStages];
+    uint64_t a_full[kMaxSlots], b_full[kMaxBStages];
     uint64_t done[kDone];                      // done[q % 8]: MMAs of K step q finished
     uint64_t acc_full[2], acc_empty[2], drain[2];
     uint32_t tmem_base;
@@ -512,7 +534,7 @@ __global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
             mbar_init(&bars->raw_full[i], 1);
             mbar_init(&bars->raw_empty[i], kDeqWarps);
         }
-        for (int i = 0; i < kSlots; i++) mbar_init(&bars->a_full[i], kDeqWarps / 2);
+        for (int i = 0; i < C::kSlots; i++) mbar_init(&bars->a_full[i], kDeqWarps / 2);
         for (int i = 0; i < C::kBStages; i++) mbar_init(&bars->b_full[i], 1);
         for (int i = 0; i < kDone; i++) mbar_init(&bars->done[i], 1);
         for (int i = 0; i < 2; i++) {
@@ -621,13 +643,13 @@ __global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
             const uint32_t d_tm = tmem + buf * C::kAccStride + iss * NT;
             const int nsteps = 2 * nb;   // even, so a step's parity is the same in every item
             uint32_t qi = q + (C::kIssuers == 2 ? iss : 0);   // this issuer's first step
-            bool rdy = __all_sync(0xffffffffu, mbar_test2(&bars->a_full[qi % kSlots], (qi / kSlots) & 1,
+            bool rdy = __all_sync(0xffffffffu, mbar_test2(&bars->a_full[qi % C::kSlots], (qi / C::kSlots) & 1,
                                                           &bars->b_full[qi % C::kBStages], (qi / C::kBStages) & 1));
             for (int s2 = qi - q; s2 < nsteps; s2 += C::kIssuers, qi += C::kIssuers) {
-                const int sl = qi % kSlots, bs = qi % C::kBStages;
+                const int sl = qi % C::kSlots, bs = qi % C::kBStages;
                 if (!rdy) {
                     st.start();
-                    ok = warp_wait(&bars->a_full[sl], (qi / kSlots) & 1, abort_flag, err, 5);
+                    ok = warp_wait(&bars->a_full[sl], (qi / C::kSlots) & 1, abort_flag, err, 5);
                     st.stop(kStMmaAFull);
                     if (!ok) break;
                     st.start();
@@ -641,11 +663,11 @@ __global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
                 const uint32_t qn = qi + C::kIssuers;
                 if (s2 + C::kIssuers < nsteps)
                     rdy = __all_sync(0xffffffffu,
-                                     mbar_test2(&bars->a_full[qn % kSlots], (qn / kSlots) & 1,
+                                     mbar_test2(&bars->a_full[qn % C::kSlots], (qn / C::kSlots) & 1,
                                                 &bars->b_full[qn % C::kBStages], (qn / C::kBStages) & 1));
                 st.stop(kStMmaTest);
                 st.start();
-                const uint32_t a_tm = tmem + kABase + 64 * sl;
+                const uint32_t a_tm = tmem + C::kABase + 64 * sl;
                 const uint64_t bd = desc0 + (uint64_t)(bs * (C::kBStage >> 4));
                 const bool first = s2 < C::kIssuers;   // this accumulator's first step of the item
                 if (elect_one()) {
@@ -683,13 +705,13 @@ __global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
         for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
             for (int sb = 0; sb < nb; sb++, sq++) {
                 const uint32_t q = 2 * sq + (wg >> 1);   // this warpgroup's K step
-                const int rs = sq % C::kRawStages, sl = q % kSlots;
+                const int rs = sq % C::kRawStages, sl = q % C::kSlots;
                 st.start();
                 ok = warp_wait(&bars->raw_full[rs], (sq / C::kRawStages) & 1, abort_flag, err, 7);
                 st.stop(kStDeqRawFull);
                 if (!ok) break;
-                if (q >= (uint32_t)kSlots) {   // slot reused: step q - 4 finished
-                    const uint32_t r = q - kSlots;
+                if (q >= (uint32_t)C::kSlots) {   // slot reused: step q - 4 finished
+                    const uint32_t r = q - C::kSlots;
                     st.start();
                     ok = warp_wait(&bars->done[r % kDone], (r / kDone) & 1, abort_flag, err, 8);
                     st.stop(kStDeqAEmpty);
@@ -705,7 +727,7 @@ __global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars->raw_empty[rs]);
                 st.start();
-                tc_st32(tmem + lane_base + kABase + 64 * sl + 32 * (wg & 1), v);
+                tc_st32(tmem + lane_base + C::kABase + 64 * sl + 32 * (wg & 1), v);
                 tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -758,7 +780,12 @@ __global__ void __launch_bounds__(Cfg<MODE, CODE, NT>::kThreads, 1)
                         const float g = is_up ? other : mine_e, u = is_up ? mine_o : other;
                         const int col = tb + c + (is_up ? 1 : 0);
                         if (col < ntok)
-                            act_out[(size_t)(p0 + col) * out_ld + kperm(orow)] = __float2half_rn(silu_mul(g, u));
+                            // SwiGLU with the hardware exp: the value is rounded to fp16 next, and the
+                            // bit-exact libm exp (silu_mul) halved the gate/up kernel's speed (one
+                            // epilogue warpgroup per SM: cfg4 466 -> 230 us, cfg2 111 -> 90 us) at the
+                            // same layer rel-L2 (5.53e-4 both on cfg2)
+                            act_out[(size_t)(p0 + col) * out_ld + kperm(orow)] =
+                                __float2half_rn(g / (1.f + __expf(-g)) * u);
                     }
                 }
             } else {
