@@ -90,6 +90,11 @@ struct PhaseScope {
             cudaEventRecord(a, s);
         }
     }
+    // nothing ran in this scope (a launch that did not happen): record nothing
+    void drop() {
+        if (a) g_ev_pool.push_back(a);
+        a = nullptr;
+    }
     ~PhaseScope() {
         if (g_prof && a) {
             cudaEvent_t b = ev_get();
@@ -920,6 +925,7 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         {
             PhaseScope ps(kFused, s);
             rc = launch_fused_decode(f, a.tab->cg, a.tab->cu, a.tab->cd, s);
+            if (rc != 0) ps.drop();
         }
         if (rc == 0) {
             rb.err = f.route_err;   // the status words the synchronous calls read back
@@ -943,10 +949,17 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
                     std::sort(v.begin(), v.end());
                     if (!v.empty()) fprintf(stderr, " %s=%.1f/%.1fus", nm[i], v[v.size() / 2], v.back());
                 }
-                fprintf(stderr, "\n[fused decode jobs, block 0: issued/taken us]");
-                for (int j = 0; j < 24; j++) {
-                    const unsigned long long t0 = st[0], a = st[8 + j], b = st[32 + j];
-                    if (a || b) fprintf(stderr, " %d:%.1f/%.1f", j, a ? (a - t0) * 1e-3 : -1.0, b ? (b - t0) * 1e-3 : -1.0);
+                for (int blk : {0, G / 2}) {
+                    if (blk >= G) continue;
+                    const unsigned long long* sb = st + (size_t)blk * 64;
+                    fprintf(stderr, "\n[block %d per warp: first piece / B done / C done us]", blk);
+                    for (int w = 0; w < 16; w++)
+                        fprintf(stderr, " %d:%.1f/%.1f/%.1f", w, sb[8 + w] ? (sb[8 + w] - sb[0]) * 1e-3 : -1.0,
+                                sb[24 + w] ? (sb[24 + w] - sb[0]) * 1e-3 : -1.0,
+                                sb[40 + w] ? (sb[40 + w] - sb[0]) * 1e-3 : -1.0);
+                    fprintf(stderr, "\n[block %d warps 0/15: B wait/compute, C wait/compute us] %.1f/%.1f %.1f/%.1f | %.1f/%.1f %.1f/%.1f",
+                            blk, sb[56] * 1e-3, sb[57] * 1e-3, sb[58] * 1e-3, sb[59] * 1e-3, sb[60] * 1e-3, sb[61] * 1e-3,
+                            sb[62] * 1e-3, sb[63] * 1e-3);
                 }
                 fprintf(stderr, "\n");
             }

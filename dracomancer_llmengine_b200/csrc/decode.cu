@@ -16,6 +16,7 @@
 #include "select.cuh"
 
 #include <algorithm>
+#include <vector>
 
 namespace draco {
 namespace {
@@ -305,21 +306,239 @@ int tile_rows(int rows, uint32_t row_bytes_) {
 }
 
 // ------------------------------------------------------------------------------------------
+// Lane-direct superblock decode: the words one lane needs of one superblock loaded straight from
+// global memory (no staging, no scale table), decoded to the same 8 values as decode8 with the
+// same arithmetic (superblock_scales' expressions), so sums match the staged kernels bit for bit.
+// Q4_K: header (16 B, the same for all lanes) + the lane's qs word; Q6_K (224-byte layout): the
+// lane's ql and qh words + the 16 scales and d (the same for all lanes).
+// ------------------------------------------------------------------------------------------
+template <int CODE>
+struct LaneSB;
+template <>
+struct LaneSB<DRACO_CODE_Q4_K> {
+    uint4 hd;
+    uint32_t qs;
+};
+template <>
+struct LaneSB<DRACO_CODE_Q6_K> {
+    uint32_t ql, qh;
+    uint4 sc;
+    uint32_t d;
+};
+
+template <int CODE>
+__device__ __forceinline__ LaneSB<CODE> lane_load(const uint8_t* __restrict__ blk, int lane) {
+    LaneSB<CODE> r;
+    if constexpr (CODE == DRACO_CODE_Q4_K) {
+        r.hd = __ldg(reinterpret_cast<const uint4*>(blk));
+        r.qs = __ldg(reinterpret_cast<const uint32_t*>(blk + 16 + 4 * lane));
+    } else {
+        const int h = lane >> 4, i = lane & 15;
+        r.ql = __ldg(reinterpret_cast<const uint32_t*>(blk + 64 * h + 4 * i));
+        r.qh = __ldg(reinterpret_cast<const uint32_t*>(blk + 128 + 32 * h + 4 * (i & 7)));
+        r.sc = __ldg(reinterpret_cast<const uint4*>(blk + 192));
+        r.d = __ldg(reinterpret_cast<const uint32_t*>(blk + 208));
+    }
+    return r;
+}
+__device__ __forceinline__ int byte_of(const uint4& v, int idx) {   // signed byte idx (0..15)
+    const uint32_t w = (idx >> 2) == 0 ? v.x : (idx >> 2) == 1 ? v.y : (idx >> 2) == 2 ? v.z : v.w;
+    return (int)(int8_t)(w >> (8 * (idx & 3)));
+}
+
+template <int CODE>
+__device__ __forceinline__ void lane_decode(const LaneSB<CODE>& s, int lane, float w[8]) {
+    if constexpr (CODE == DRACO_CODE_Q4_K) {
+        const float d = h2f((uint16_t)(s.hd.x & 0xffff)), dmin = h2f((uint16_t)(s.hd.x >> 16));
+        const int g = lane >> 3;
+        int sc0, m0, sc1, m1;
+        q4k_scale_min(s.hd.y, s.hd.z, s.hd.w, 2 * g, sc0, m0);
+        q4k_scale_min(s.hd.y, s.hd.z, s.hd.w, 2 * g + 1, sc1, m1);
+        const float ds0 = d * (float)sc0, dm0 = dmin * (float)m0;
+        const float ds1 = d * (float)sc1, dm1 = dmin * (float)m1;
+        const float2 t0 = make_float2(64.f * ds0, -(128.f * ds0 + dm0));
+        const float2 t1 = make_float2(64.f * ds1, -(128.f * ds1 + dm1));
+        const uint32_t lo = s.qs & 0x0F0F0F0Fu, hi = (s.qs >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            w[k] = fmaf(code_float(lo, k), t0.x, t0.y);
+            w[4 + k] = fmaf(code_float(hi, k), t1.x, t1.y);
+        }
+    } else {
+        const int h = lane >> 4, i = lane & 15;
+        const float d = h2f((uint16_t)(s.d & 0xffff));
+        const float dsl = d * (float)byte_of(s.sc, 8 * h + (i >> 2));
+        const float dsh = d * (float)byte_of(s.sc, 8 * h + 4 + (i >> 2));
+        const float2 sl = make_float2(64.f * dsl, -160.f * dsl), sh = make_float2(64.f * dsh, -160.f * dsh);
+        const int s0 = 2 * (i >> 3);
+        const uint32_t q_lo = (s.ql & 0x0F0F0F0Fu) | (((s.qh >> s0) & 0x03030303u) << 4);
+        const uint32_t q_hi = ((s.ql >> 4) & 0x0F0F0F0Fu) | (((s.qh >> (s0 + 4)) & 0x03030303u) << 4);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            w[k] = fmaf(code_float(q_lo, k), sl.x, sl.y);
+            w[4 + k] = fmaf(code_float(q_hi, k), sh.x, sh.y);
+        }
+    }
+}
+
+// dot products of one weight row (nb superblocks of bb bytes, global memory) with nt <= 2 token
+// rows x (shared or global memory): lane partials in superblock order, then the warp sum (the
+// order of rows_dot); loads run four superblocks ahead
+template <int CODE, int NT>
+__device__ __forceinline__ void row_dot_direct(const uint8_t* __restrict__ row, int nb, int bb,
+                                               const float* const (&xr)[2], int lane, float (&acc)[2]) {
+#pragma unroll
+    for (int j = 0; j < 2; j++) acc[j] = 0.f;
+    constexpr int kAhead = 4;
+    LaneSB<CODE> buf[kAhead];
+#pragma unroll
+    for (int u = 0; u < kAhead; u++)
+        if (u < nb) buf[u] = lane_load<CODE>(row + (size_t)u * bb, lane);
+    for (int sb0 = 0; sb0 < nb; sb0 += kAhead) {
+#pragma unroll
+        for (int u = 0; u < kAhead; u++) {
+            const int sb = sb0 + u;
+            if (sb < nb) {
+                float w[8];
+                lane_decode<CODE>(buf[u], lane, w);
+                if (sb + kAhead < nb) buf[u] = lane_load<CODE>(row + (size_t)(sb + kAhead) * bb, lane);
+#pragma unroll
+                for (int j = 0; j < NT; j++) {
+                    float xv[8];
+                    load_x8<CODE>(xr[j], sb, lane, xv);
+#pragma unroll
+                    for (int k = 0; k < 8; k++) acc[j] = fmaf(w[k], xv[k], acc[j]);
+                }
+            }
+        }
+    }
+}
+
+// One staged weight row (nb superblocks of bb bytes, shared memory) with nt <= 2 token rows, the
+// superblock scales computed cooperatively: for a group of superblocks (4 of Q4_K, 2 of Q6_K)
+// every lane works out ONE (64 d sc, offset) pair -- lane L: Q4_K superblock L / 8, sub-block
+// L % 8; Q6_K superblock L / 16, scale L % 16 -- and the lanes that decode with it fetch it by
+// shuffle, instead of each lane unpacking its own scales for every superblock.  The pairs, the
+// decoded weights and the sums are those of lane_decode / decode8 (same expressions, same
+// order), so the results equal the other decode paths bit for bit.
+template <int CODE>
+__device__ __forceinline__ float2 coop_scale(const uint8_t* row, int nb, int bb, int sb0, int lane) {
+    if constexpr (CODE == DRACO_CODE_Q4_K) {
+        const int sb = sb0 + (lane >> 3), j = lane & 7;
+        if (sb >= nb) return make_float2(0.f, 0.f);
+        const uint4 hd = *reinterpret_cast<const uint4*>(row + (size_t)sb * bb);
+        const float d = h2f((uint16_t)(hd.x & 0xffff)), dmin = h2f((uint16_t)(hd.x >> 16));
+        const int t = 8 * (j & 3);
+        const int sc_lo = (hd.y >> t) & 63, m_lo = (hd.z >> t) & 63;
+        const int e2 = (hd.w >> t) & 0xff;
+        const int sc_hi = (e2 & 15) | (((hd.y >> (t + 6)) & 3) << 4);
+        const int m_hi = (e2 >> 4) | (((hd.z >> (t + 6)) & 3) << 4);
+        const int sc = j < 4 ? sc_lo : sc_hi, mn = j < 4 ? m_lo : m_hi;
+        const float ds = d * (float)sc, dm = dmin * (float)mn;
+        return make_float2(64.f * ds, -(128.f * ds + dm));
+    } else {
+        const int sb = sb0 + (lane >> 4);
+        if (sb >= nb) return make_float2(0.f, 0.f);
+        const uint8_t* blk = row + (size_t)sb * bb;
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(blk + 208));
+        const float ds = d * (float)reinterpret_cast<const int8_t*>(blk + 192)[lane & 15];
+        return make_float2(64.f * ds, -160.f * ds);
+    }
+}
+
+// R staged weight rows at once (independent sums that the scheduler interleaves), row r with
+// the token rows xr[r] (SAME_X: every row with xr[0], loaded once)
+template <int CODE, int NT, int R, bool SAME_X, bool L2ONLY = false>
+__device__ __forceinline__ void rows_dot_smem(const uint8_t* const (&rows)[R], int nb, int bb,
+                                              const float* const (&xr)[R][2], int lane, float (&acc)[R][2]) {
+    constexpr int G = CODE == DRACO_CODE_Q4_K ? 4 : 2;   // superblocks per scale group
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) acc[r][j] = 0.f;
+    // the lanes holding this lane's two pairs (superblock offset u adds u * 32 / G)
+    const int src_lo = CODE == DRACO_CODE_Q4_K ? 2 * (lane >> 3) : 8 * (lane >> 4) + ((lane & 15) >> 2);
+    const int src_hi = CODE == DRACO_CODE_Q4_K ? src_lo + 1 : src_lo + 4;
+    for (int sb0 = 0; sb0 < nb; sb0 += G) {
+        float2 ab[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) ab[r] = coop_scale<CODE>(rows[r], nb, bb, sb0, lane);
+#pragma unroll
+        for (int u = 0; u < G; u++) {
+            const int sb = sb0 + u;
+            float2 sl[R], sh[R];
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                sl[r] = make_float2(__shfl_sync(0xffffffffu, ab[r].x, src_lo + u * (32 / G)),
+                                    __shfl_sync(0xffffffffu, ab[r].y, src_lo + u * (32 / G)));
+                sh[r] = make_float2(__shfl_sync(0xffffffffu, ab[r].x, src_hi + u * (32 / G)),
+                                    __shfl_sync(0xffffffffu, ab[r].y, src_hi + u * (32 / G)));
+            }
+            if (sb < nb) {
+                float xs0[NT][8];
+                if (SAME_X) {
+#pragma unroll
+                    for (int j = 0; j < NT; j++) load_x8<CODE, L2ONLY>(xr[0][j], sb, lane, xs0[j]);
+                }
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    const uint8_t* blk = rows[r] + (size_t)sb * bb;
+                    uint32_t q_lo, q_hi;
+                    if constexpr (CODE == DRACO_CODE_Q4_K) {
+                        const uint32_t qs = *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * lane);
+                        q_lo = qs & 0x0F0F0F0Fu;
+                        q_hi = (qs >> 4) & 0x0F0F0F0Fu;
+                    } else {
+                        const int h = lane >> 4, i = lane & 15;
+                        const uint32_t ql = *reinterpret_cast<const uint32_t*>(blk + 64 * h + 4 * i);
+                        const uint32_t qh = *reinterpret_cast<const uint32_t*>(blk + 128 + 32 * h + 4 * (i & 7));
+                        const int s0 = 2 * (i >> 3);
+                        q_lo = (ql & 0x0F0F0F0Fu) | (((qh >> s0) & 0x03030303u) << 4);
+                        q_hi = ((ql >> 4) & 0x0F0F0F0Fu) | (((qh >> (s0 + 4)) & 0x03030303u) << 4);
+                    }
+                    float w[8];
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        w[k] = fmaf(code_float(q_lo, k), sl[r].x, sl[r].y);
+                        w[4 + k] = fmaf(code_float(q_hi, k), sh[r].x, sh[r].y);
+                    }
+#pragma unroll
+                    for (int j = 0; j < NT; j++) {
+                        float xv[8];
+                        if (SAME_X) {
+#pragma unroll
+                            for (int k = 0; k < 8; k++) xv[k] = xs0[j][k];
+                        } else {
+                            load_x8<CODE, L2ONLY>(xr[r][j], sb, lane, xv);
+                        }
+#pragma unroll
+                        for (int k = 0; k < 8; k++) acc[r][j] = fmaf(w[k], xv[k], acc[r][j]);
+                    }
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // Fused decode layer: the whole MoE layer of a small token batch (T <= 8, T*K <= 64) in ONE
-// cooperative launch of one or two blocks per SM:
+// cooperative launch of one block per SM:
 //   phase A  router logits: the T*E exact-order chains (k ascending, rounded product then
 //            rounded add, src/m6_layer.c:775-783) spread over the blocks, one lane per chain,
-//            router rows and token rows streamed through a shared-memory ring by bulk copies;
+//            router rows and token rows streamed by a producer warp through a shared-memory
+//            ring of bulk copies;
 //   -- grid barrier 1 --
 //   phase S  every block selects the routing of all T tokens itself from the logits (the
 //            router's warp-level selection, bit-exact) and builds the active expert list;
-//   phase B  gate/up + SwiGLU tiles of (active expert, row tile), plus the shared expert's;
-//   -- grid barrier 2 (compute warps only: the producer warp is already streaming phase C's
-//            weight tiles, which do not depend on the activations) --
-//   phase C  down tiles of every active expert for a row tile, the expert rows y kept in shared
-//            memory, then the k-ascending fused combine (+ shared expert) of that row tile.
-// One producer warp issues the bulk copies of every job (router chunk, gate+up tile, down tile)
-// into a ring of slots; four compute warps decode and reduce (the dec_* kernels' row code).
+//   phase B  warp tasks: one (active expert or shared expert, intermediate row) gate+up row
+//            pair, all tokens routed to that expert, SwiGLU;
+//   -- grid barrier 2 --
+//   phase C  warp tasks: one output row over every active expert (and the shared expert),
+//            then the k-ascending fused combine (+ shared expert) of that row.
+// Each compute warp streams the weight rows of its own tasks through a private ring of bulk
+// copies, phase C's rows included as soon as there is room (they do not depend on the
+// activations), so the weights of the whole layer are in flight while phase B computes.  Per
+// row the arithmetic and its order are those of the separate dec_* kernels.
 // Every wait is bounded: an mbarrier wait gives up after 2 s, a grid barrier after 1 s; a block
 // that gives up raises a status bit (0x200 copy, 0x1000 grid barrier), stops, and waits for its
 // own copies in flight before it exits.
@@ -329,6 +548,7 @@ constexpr int kFdMaxAssign = 64;
 constexpr int kFdCompute = 16;            // compute warps (the producer warp is warp 16)
 constexpr int kFdThreads = 32 * (kFdCompute + 1);
 constexpr int kFdMaxSlots = 4;
+constexpr int kFdMaxStg = 8;              // per-warp weight-row ring stages
 constexpr uint64_t kFdGridWaitNs = 1000000000ull;
 
 __device__ __forceinline__ void fd_compute_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kFdCompute) : "memory"); }
@@ -372,11 +592,13 @@ template <int CG, int CU, int CD, int NS>
 __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArgs a) {
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ uint64_t full[kFdMaxSlots], empty[kFdMaxSlots];
+    __shared__ uint64_t s_wfull[kFdCompute][kFdMaxStg];
     // s_cabort: written by compute threads (and thread 0 at the grid barriers) and read by them
     // only after a barrier, so their decisions stay uniform; s_pabort: the producer's own
     __shared__ volatile int s_cabort, s_pabort;
     __shared__ int s_n_act, s_qc;
     __shared__ int s_first[kFdMaxAssign];
+    __shared__ const uint8_t* s_wp[3 * kFdMaxAssign];   // gate, up, down of each active expert
     const int E = a.rp.n_exp, K = a.rp.n_used, H = a.rp.n_in, T = a.T, F = a.F;
     const int NA = T * K;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -384,7 +606,9 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
     const int S = a.n_slots;
     const bool sh = a.sh_ff > 0;
     uint8_t* ring = dsm;
-    float* xs = reinterpret_cast<float*>(dsm + (size_t)S * a.slot_bytes);      // [xs_cap] token / act rows
+    // the router's slots and (after barrier 1) the compute warps' weight-row rings share the front
+    const size_t ring_bytes = max((size_t)S * a.slot_bytes, (size_t)kFdCompute * a.n_stg * a.stg_bytes);
+    float* xs = reinterpret_cast<float*>(dsm + ring_bytes);                     // [xs_cap] token / act rows
     const int ES = (E + 3) & ~3;                                                // 16-byte aligned rows
     float* V = xs + a.xs_cap;                                                   // [8][ES] selection scratch
     float* gsm = V + kFdMaxTokens * ES;                                         // [8][64]
@@ -393,17 +617,21 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
     int* act_e = reinterpret_cast<int*>(s_wtop + kFdMaxAssign);                  // [64]
     int* act_cnt = act_e + kFdMaxAssign;                                         // [64]
     int* act_asg = act_cnt + kFdMaxAssign;                                       // [64][8]
-    float* ys = reinterpret_cast<float*>(act_asg + kFdMaxAssign * kFdMaxTokens);  // [(64+8)][rt_c]
+    float* ys = reinterpret_cast<float*>(act_asg + kFdMaxAssign * kFdMaxTokens);  // [16][64+8] expert outputs
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) {
             sync::mbar_init(&full[i], 1);
             sync::mbar_init(&empty[i], 1);
         }
+        for (int w = 0; w < kFdCompute; w++)
+            for (int i = 0; i < a.n_stg; i++) sync::mbar_init(&s_wfull[w][i], 1);
         sync::fence_init();
         s_cabort = 0;
         s_pabort = 0;
         s_qc = 0;
     }
+    // token rows in shared memory when they fit (read in phase B; the router reads its own copies)
+    if (warp < kFdCompute && (size_t)T * H <= (size_t)a.xs_cap) fd_stage_rows(xs, a.X, (size_t)T * H, threadIdx.x);
     __syncthreads();
     fd_stamp(a, 0);
     const bool producer = warp == kFdCompute;
@@ -420,7 +648,6 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             s_pabort = 1;
             return nullptr;
         }
-        if (a.stamps && q < 24) a.stamps[(size_t)blockIdx.x * 64 + 8 + q] = sync::global_ns();
         return ring + (size_t)sl * a.slot_bytes;
     };
     // compute threads: job q's slot, nullptr (uniformly) after a failed wait
@@ -431,7 +658,6 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             s_cabort = 1;
         }
         fd_compute_sync();
-        if (a.stamps && ctid == 0 && q < 24) a.stamps[(size_t)blockIdx.x * 64 + 32 + q] = sync::global_ns();
         if (s_cabort) return nullptr;
         return ring + (size_t)sl * a.slot_bytes;
     };
@@ -493,6 +719,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             if (done && warp == 0 && lane < nch) a.logits[(size_t)ct * E + c % E] = acc;
         }
     }
+    if (ctid == 0) s_qc = (int)q;   // router jobs the compute warps consumed
     // ---------------------------------------------------------------- grid barrier 1
     __syncthreads();
     fd_stamp(a, 1);
@@ -561,100 +788,110 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
         s_n_act = n;
     }
     __syncthreads();
+    if (ok && threadIdx.x < 3 * s_n_act) s_wp[threadIdx.x] = a.tab.w[3 * act_e[threadIdx.x / 3] + threadIdx.x % 3];
+    __syncthreads();
     fd_stamp(a, 3);
     const int n_act = ok ? s_n_act : 0;
     // ---------------------------------------------------------------- phases B and C
+    // Warp tasks: phase B = one (expert or shared expert, intermediate row) pair of gate and up
+    // rows, phase C = one output row over every active expert (and the shared expert), combined
+    // in k order right away.  Each compute warp streams the weight rows of its own tasks, in task
+    // order, through a private ring of n_stg stages by bulk copies (lane 0 issues, one mbarrier per
+    // stage); phase C's rows do not depend on the activations, so they are issued as soon as
+    // phase B's leave room, before grid barrier 2.  The ring aliases the router's slots (all of
+    // them consumed before barrier 1).
     const int nb = H / 256, nbd = F / 256, nbds = sh ? a.sh_ff / 256 : 0;
-    const int bg = superblock_bytes(CG, a.q6s), bu = superblock_bytes(CU, a.q6s), bd = superblock_bytes(CD, a.q6s);
-    const uint32_t rbg = (uint32_t)(nb * bg), rbu = (uint32_t)(nb * bu);
-    const uint32_t rbd = (uint32_t)(nbd * bd), rbds = (uint32_t)(nbds * bd);
-    const int rt_b = a.rt_b, rt_c = a.rt_c;
-    const int tiles_f = F / rt_b, tiles_fs = sh ? a.sh_ff / rt_b : 0;
-    const int items_b = ok ? n_act * tiles_f + tiles_fs : 0;
-    const int items_c = ok ? a.n_out / rt_c : 0;
-    const int exp_c = n_act + (sh ? 1 : 0);
-    const int cg_sz = a.c_group;                           // experts per phase-C job
-    // bytes of one expert's down tile in a phase-C slot: data, then its scale table
-    const uint32_t tile_c = (uint32_t)rt_c * (rbd > rbds ? rbd : rbds) +
-                            (uint32_t)rt_c * (nbd > nbds ? nbd : nbds) * scale_groups<CD>() * 8;
-    if (producer) {
-        // B jobs then C jobs, back to back (C's weight tiles do not wait for the activations)
-        if (lane == 0) {
-            bool go = true;
-            for (int j = b; j < items_b && go; j += G) {
-                uint8_t* dst = claim();
-                if (!dst) {
-                    go = false;
-                    break;
-                }
-                const uint8_t *g, *u;
-                if (j < n_act * tiles_f) {
-                    const int e = act_e[j / tiles_f];
-                    const size_t r0 = (size_t)(j % tiles_f) * rt_b;
-                    g = a.tab.w[3 * e] + r0 * rbg;
-                    u = a.tab.w[3 * e + 1] + r0 * rbu;
-                } else {
-                    const size_t r0 = (size_t)(j - n_act * tiles_f) * rt_b;
-                    g = a.sh_g + r0 * rbg;
-                    u = a.sh_u + r0 * rbu;
-                }
-                const int sl = q % S;
-                sync::mbar_expect_tx(&full[sl], (uint32_t)rt_b * (rbg + rbu));
-                sync::bulk_load(dst, g, rt_b * rbg, &full[sl]);
-                sync::bulk_load(dst + rt_b * rbg, u, rt_b * rbu, &full[sl]);
-                q++;
-            }
-            for (int j = b; j < items_c && go; j += G) {
-                for (int x0 = 0; x0 < exp_c; x0 += cg_sz) {
-                    uint8_t* dst = claim();
-                    if (!dst) {
-                        go = false;
-                        break;
-                    }
-                    const int x1 = min(exp_c, x0 + cg_sz);
-                    uint32_t bytes = 0;
-                    for (int x = x0; x < x1; x++) bytes += (uint32_t)rt_c * (x == n_act ? rbds : rbd);
-                    const int sl = q % S;
-                    sync::mbar_expect_tx(&full[sl], bytes);
-                    for (int x = x0; x < x1; x++) {
-                        const bool shx = x == n_act;
-                        const uint32_t rb = shx ? rbds : rbd;
-                        const uint8_t* src = shx ? a.sh_d : a.tab.w[3 * act_e[x] + 2];
-                        sync::bulk_load(dst + (size_t)(x - x0) * tile_c, src + (size_t)j * rt_c * rb, rt_c * rb,
-                                        &full[sl]);
-                    }
-                    q++;
-                }
-            }
+    const int bg = superblock_bytes(CG, a.q6s), bd = superblock_bytes(CD, a.q6s);
+    const uint32_t rbg = (uint32_t)nb * bg, rbd = (uint32_t)nbd * bd, rbds = (uint32_t)nbds * bd;
+    const int tasks_b = ok ? n_act * F + (sh ? a.sh_ff : 0) : 0;
+    const int tasks_c = ok ? a.n_out : 0;
+    const int gw = b * kFdCompute + warp, GW = G * kFdCompute;   // this warp's global index, all warps
+    const int NST = a.n_stg;
+    const int per_c = n_act + (sh ? 1 : 0);   // pieces of a phase C task
+    if (!producer) {
+        uint8_t* wring = ring + (size_t)warp * NST * a.stg_bytes;
+        uint64_t* wfull = s_wfull[warp];
+        // producer cursor (uniform over the warp; lane 0 issues): the next piece's phase, task, part
+        int p_ph = 0, p_task = gw, p_sub = 0;
+        if (p_task >= tasks_b) {
+            p_ph = 1;
+            if (p_task >= tasks_c) p_ph = 2;
         }
-    } else {
-        // token rows in shared memory when they fit (one L2 round trip instead of one per superblock)
-        const bool x_in_smem = (size_t)T * H <= (size_t)a.xs_cap;
-        if (ok && x_in_smem) fd_stage_rows(xs, a.X, (size_t)T * H, ctid);
-        fd_compute_sync();
-        const float* xbase = x_in_smem ? xs : a.X;
-        // rows of a gate/up tile over the compute warps: warp w takes rows [w * rpw, +rpw)
-        const int rpw = (rt_b + kFdCompute - 1) / kFdCompute;
-        const int r0 = warp * rpw;
-        const int my_rows = max(0, min(rpw, rt_b - r0));
-        for (int j = b; j < items_b && ok; j += G) {
-            uint8_t* tile = take();
-            if (!tile) {
-                ok = false;
-                break;
+        uint32_t n_iss = 0, n_con = 0;   // pieces issued / consumed
+        bool wok = ok;
+        // (a stage is only ever read by this warp's generic loads before the copy that rewrites
+        // it, and those loads completed before the __syncwarp of release_pieces)
+        auto issue = [&]() {
+            while (wok && p_ph < 2 && n_iss < n_con + NST) {
+                const uint8_t* src;
+                uint32_t bytes;
+                if (p_ph == 0) {
+                    const bool shx = p_task >= n_act * F;
+                    const int ax = shx ? 0 : p_task / F, row = shx ? p_task - n_act * F : p_task % F;
+                    const uint8_t* base = shx ? (p_sub ? a.sh_u : a.sh_g) : s_wp[3 * ax + p_sub];
+                    src = base + (size_t)row * rbg;
+                    bytes = rbg;
+                    if (++p_sub == 2) {
+                        p_sub = 0;
+                        p_task += GW;
+                        if (p_task >= tasks_b) {
+                            p_ph = 1;
+                            p_task = gw;
+                            if (p_task >= tasks_c) p_ph = 2;
+                        }
+                    }
+                } else {
+                    const bool shx = p_sub == n_act;
+                    src = shx ? a.sh_d + (size_t)p_task * rbds : s_wp[3 * p_sub + 2] + (size_t)p_task * rbd;
+                    bytes = shx ? rbds : rbd;
+                    if (++p_sub == per_c) {
+                        p_sub = 0;
+                        p_task += GW;
+                        if (p_task >= tasks_c) p_ph = 2;
+                    }
+                }
+                const int st = n_iss % NST;
+                if (lane == 0) {
+                    sync::mbar_expect_tx(&wfull[st], bytes);
+                    sync::bulk_load(wring + (size_t)st * a.stg_bytes, src, bytes, &wfull[st]);
+                }
+                n_iss++;
             }
-            const bool shx = j >= n_act * tiles_f;
-            const int ax = shx ? 0 : j / tiles_f;
-            const int tile_r = shx ? j - n_act * tiles_f : j % tiles_f;
+        };
+        // the next piece in shared memory (nullptr after a failed wait)
+        unsigned long long t_acc[4] = {0, 0, 0, 0};   // DRACO_B200_FD_STATS: wait/compute ns, B and C
+        int t_ph = 0;
+        auto take_piece = [&]() -> const uint8_t* {
+            const unsigned long long tw0 = a.stamps ? sync::global_ns() : 0;
+            const int st = n_con % NST;
+            if (!sync::mbar_wait(&wfull[st], (n_con / NST) & 1)) {
+                if (lane == 0) atomicOr(a.status, 0x200);
+                wok = false;
+            }
+            wok = __all_sync(0xffffffffu, wok);
+            if (a.stamps) t_acc[2 * t_ph] += sync::global_ns() - tw0;
+            if (a.stamps && lane == 0 && n_con == 0) a.stamps[(size_t)blockIdx.x * 64 + 8 + warp] = sync::global_ns();
+            return wok ? wring + (size_t)st * a.stg_bytes : nullptr;
+        };
+        auto release_pieces = [&](int n) {
+            __syncwarp();
+            n_con += n;
+            issue();
+        };
+        issue();
+        const bool x_in_smem = (size_t)T * H <= (size_t)a.xs_cap;   // staged at the start
+        const float* xbase = x_in_smem ? xs : a.X;
+        for (int task = gw; wok && task < tasks_b; task += GW) {
+            const bool shx = task >= n_act * F;
+            const int ax = shx ? 0 : task / F;
+            const int row = shx ? task - n_act * F : task % F;
             const int cnt = shx ? T : act_cnt[ax];
-            uint8_t* sg = tile;
-            uint8_t* su = tile + rt_b * rbg;
-            float2* tg = reinterpret_cast<float2*>(tile + rt_b * (rbg + rbu));
-            float2* tu = tg + rt_b * nb * scale_groups<CG>();
-            fd_scales<CG>(sg, rt_b, nb, bg, tg, ctid, 32 * kFdCompute);
-            fd_scales<CU>(su, rt_b, nb, bu, tu, ctid, 32 * kFdCompute);
-            fd_compute_sync();
-            for (int tc = 0; tc < cnt && my_rows > 0; tc += 2) {
+            const uint8_t* grow = take_piece();
+            n_con++;
+            const uint8_t* urow = wok ? take_piece() : nullptr;
+            n_con--;
+            if (!wok) break;
+            for (int tc = 0; tc < cnt; tc += 2) {
                 const int nt = min(2, cnt - tc);
                 const float* xr[2];
                 int slot[2];
@@ -665,43 +902,47 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                     slot[jj] = i;
                     xr[jj] = xbase + (size_t)(shx ? i : i / K) * H;
                 }
-                float ag[4][2], au[4][2];
-                if (nt == 2) rows_dot<CG, CU, true, 2>(sg, tg, su, tu, rbg, rbu, bg, bu, nb, r0, my_rows, xr, lane, ag, au);
-                else rows_dot<CG, CU, true, 1>(sg, tg, su, tu, rbg, rbu, bg, bu, nb, r0, my_rows, xr, lane, ag, au);
+                float acc[2][2];
+                const uint8_t* const gu[2] = {grow, urow};
+                const float* const xx[2][2] = {{xr[0], xr[1]}, {xr[0], xr[1]}};
+                const unsigned long long tc0 = a.stamps ? sync::global_ns() : 0;
+                static_assert(CG == CU, "the fused kernel runs gate and up of one format");
+                if (nt == 2) rows_dot_smem<CG, 2, 2, true>(gu, nb, bg, xx, lane, acc);
+                else rows_dot_smem<CG, 1, 2, true>(gu, nb, bg, xx, lane, acc);
+                if (a.stamps) t_acc[1] += sync::global_ns() - tc0;
+                const float (&ag)[2] = acc[0];
+                const float (&au)[2] = acc[1];
 #pragma unroll
-                for (int r = 0; r < 4; r++) {
-                    if (r < my_rows) {
-#pragma unroll
-                        for (int jj = 0; jj < 2; jj++) {
-                            if (jj < nt) {
-                                const float gv = warp_sum(ag[r][jj]), uv = warp_sum(au[r][jj]);
-                                const int row = tile_r * rt_b + r0 + r;
-                                if (lane == 0) {
-                                    if (shx) a.act_sh[(size_t)slot[jj] * a.sh_ff + row] = silu_mul(gv, uv);
-                                    else a.act[(size_t)slot[jj] * F + row] = silu_mul(gv, uv);
-                                }
-                            }
+                for (int jj = 0; jj < 2; jj++) {
+                    if (jj < nt) {
+                        const float gv = warp_sum(ag[jj]), uv = warp_sum(au[jj]);
+                        if (lane == 0) {
+                            if (shx) a.act_sh[(size_t)slot[jj] * a.sh_ff + row] = silu_mul(gv, uv);
+                            else a.act[(size_t)slot[jj] * F + row] = silu_mul(gv, uv);
                         }
                     }
                 }
             }
-            release();
+            release_pieces(2);
         }
+        if (!wok) s_cabort = 1;
+        if (a.stamps && lane == 0) a.stamps[(size_t)blockIdx.x * 64 + 24 + warp] = sync::global_ns();
         // ------------------------------------------------------------ grid barrier 2
         fd_compute_sync();
         fd_stamp(a, 4);
         if (ctid == 0) {
-            if (!ok || !fd_grid_arrive_wait(a.bar + 1, (unsigned)(G + a.bar_extra))) {
-                if (ok) atomicOr(a.status, 0x1000);
+            if (!ok || s_cabort || !fd_grid_arrive_wait(a.bar + 1, (unsigned)(G + a.bar_extra))) {
+                if (ok && !s_cabort) atomicOr(a.status, 0x1000);
                 s_cabort = 1;
             }
         }
         fd_compute_sync();
         fd_stamp(a, 5);
         ok = !s_cabort;
+        wok = wok && ok;
         // the activation rows of every assignment (and the shared expert's) in shared memory
         const size_t act_n = (size_t)NA * F + (sh ? (size_t)T * a.sh_ff : 0);
-        const bool a_in_smem = items_c > 0 && act_n <= (size_t)a.xs_cap;
+        const bool a_in_smem = act_n <= (size_t)a.xs_cap;
         if (ok && a_in_smem) {
             fd_stage_rows(xs, a.act, (size_t)NA * F, ctid);
             if (sh) fd_stage_rows(xs + (size_t)NA * F, a.act_sh, (size_t)T * a.sh_ff, ctid);
@@ -709,97 +950,101 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
         fd_compute_sync();
         const float* abase = a_in_smem ? xs : a.act;
         const float* sbase = a_in_smem ? xs + (size_t)NA * F : a.act_sh;
-        // row-dot tasks of a down job over the compute warps: task = (tile in the group, rpc rows)
-        const int rpc = rt_c >= 8 ? 2 : 1;
-        const int tasks_per_tile = rt_c / rpc;
-        for (int j = b; j < items_c && ok; j += G) {
-            for (int x0 = 0; x0 < exp_c && ok; x0 += cg_sz) {
-                uint8_t* slotp = take();
-                if (!slotp) {
-                    ok = false;
-                    break;
+        float* yw = ys + (size_t)warp * (kFdMaxAssign + kFdMaxTokens);   // this warp's expert outputs
+        t_ph = 1;
+        for (int r = gw; wok && r < tasks_c; r += GW) {
+            for (int x = 0; x < per_c; x++) {
+                const bool shx = x == n_act;
+                const int cnt = shx ? T : act_cnt[x];
+                const int nbx = shx ? nbds : nbd;
+                if (!shx && x + 1 < n_act && cnt == 1 && act_cnt[x + 1] == 1) {
+                    // two experts with one assignment each: both rows at once
+                    const uint8_t* d0 = take_piece();
+                    n_con++;
+                    const uint8_t* d1 = wok ? take_piece() : nullptr;
+                    n_con--;
+                    if (!wok) break;
+                    const int i0 = act_asg[x * kFdMaxTokens], i1 = act_asg[(x + 1) * kFdMaxTokens];
+                    const uint8_t* const dd[2] = {d0, d1};
+                    const float* const xx[2][2] = {{abase + (size_t)i0 * F, abase + (size_t)i0 * F},
+                                                   {abase + (size_t)i1 * F, abase + (size_t)i1 * F}};
+                    float ad[2][2];
+                    const unsigned long long tc0 = a.stamps ? sync::global_ns() : 0;
+                    if (a_in_smem) rows_dot_smem<CD, 1, 2, false>(dd, nbx, bd, xx, lane, ad);
+                    else rows_dot_smem<CD, 1, 2, false, true>(dd, nbx, bd, xx, lane, ad);
+                    if (a.stamps) t_acc[3] += sync::global_ns() - tc0;
+                    const float v0 = warp_sum(ad[0][0]), v1 = warp_sum(ad[1][0]);
+                    if (lane == 0) {
+                        yw[i0] = v0;
+                        yw[i1] = v1;
+                    }
+                    release_pieces(2);
+                    x++;
+                    continue;
                 }
-                const int x1 = min(exp_c, x0 + cg_sz);
-                for (int x = x0; x < x1; x++) {
-                    const bool shx = x == n_act;
-                    uint8_t* tile = slotp + (size_t)(x - x0) * tile_c;
-                    const int nbx = shx ? nbds : nbd;
-                    const uint32_t rb = shx ? rbds : rbd;
-                    fd_scales<CD>(tile, rt_c, nbx, bd, reinterpret_cast<float2*>(tile + rt_c * rb), ctid,
-                                  32 * kFdCompute);
-                }
-                fd_compute_sync();
-                for (int task = warp; task < (x1 - x0) * tasks_per_tile; task += kFdCompute) {
-                    const int x = x0 + task / tasks_per_tile;
-                    const int c0 = (task % tasks_per_tile) * rpc;
-                    const bool shx = x == n_act;
-                    uint8_t* tile = slotp + (size_t)(x - x0) * tile_c;
-                    const int cnt = shx ? T : act_cnt[x];
-                    const int nbx = shx ? nbds : nbd;
-                    const uint32_t rb = shx ? rbds : rbd;
-                    float2* td = reinterpret_cast<float2*>(tile + rt_c * rb);
-                    for (int tc = 0; tc < cnt; tc += 2) {
-                        const int nt = min(2, cnt - tc);
-                        const float* xr[2];
-                        int slot[2];
+                const uint8_t* drow = take_piece();
+                if (!drow) break;
+                for (int tc = 0; tc < cnt; tc += 2) {
+                    const int nt = min(2, cnt - tc);
+                    const float* xr[1][2];
+                    int slot[2];
 #pragma unroll
-                        for (int jj = 0; jj < 2; jj++) {
-                            const int m = tc + min(jj, nt - 1);
-                            const int i = shx ? m : act_asg[x * kFdMaxTokens + m];
-                            slot[jj] = shx ? NA + i : i;
-                            xr[jj] = shx ? sbase + (size_t)i * a.sh_ff : abase + (size_t)i * F;
-                        }
-                        float ad[4][2], unused[4][2];
-                        if (a_in_smem) {
-                            if (nt == 2)
-                                rows_dot<CD, CD, false, 2>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0, rpc, xr,
-                                                           lane, ad, unused);
-                            else
-                                rows_dot<CD, CD, false, 1>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0, rpc, xr,
-                                                           lane, ad, unused);
-                        } else {
-                            if (nt == 2)
-                                rows_dot<CD, CD, false, 2, true>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0,
-                                                                 rpc, xr, lane, ad, unused);
-                            else
-                                rows_dot<CD, CD, false, 1, true>(tile, td, nullptr, nullptr, rb, 0, bd, 0, nbx, c0,
-                                                                 rpc, xr, lane, ad, unused);
-                        }
+                    for (int jj = 0; jj < 2; jj++) {
+                        const int m = tc + min(jj, nt - 1);
+                        const int i = shx ? m : act_asg[x * kFdMaxTokens + m];
+                        slot[jj] = shx ? NA + i : i;
+                        xr[0][jj] = shx ? sbase + (size_t)i * a.sh_ff : abase + (size_t)i * F;
+                    }
+                    const uint8_t* const dd[1] = {drow};
+                    float ad[1][2];
+                    const unsigned long long tc0 = a.stamps ? sync::global_ns() : 0;
+                    if (a_in_smem) {
+                        if (nt == 2) rows_dot_smem<CD, 2, 1, true>(dd, nbx, bd, xr, lane, ad);
+                        else rows_dot_smem<CD, 1, 1, true>(dd, nbx, bd, xr, lane, ad);
+                    } else {
+                        // rows written by other blocks of this launch: L2 loads
+                        if (nt == 2) rows_dot_smem<CD, 2, 1, true, true>(dd, nbx, bd, xr, lane, ad);
+                        else rows_dot_smem<CD, 1, 1, true, true>(dd, nbx, bd, xr, lane, ad);
+                    }
+                    if (a.stamps) t_acc[3] += sync::global_ns() - tc0;
 #pragma unroll
-                        for (int r = 0; r < 4; r++) {
-                            if (r < rpc) {
-#pragma unroll
-                                for (int jj = 0; jj < 2; jj++) {
-                                    if (jj < nt) {
-                                        const float v = warp_sum(ad[r][jj]);
-                                        if (lane == 0) ys[slot[jj] * rt_c + c0 + r] = v;
-                                    }
-                                }
-                            }
+                    for (int jj = 0; jj < 2; jj++) {
+                        if (jj < nt) {
+                            const float v = warp_sum(ad[0][jj]);
+                            if (lane == 0) yw[slot[jj]] = v;
                         }
                     }
                 }
-                release();
+                release_pieces(1);
             }
-            if (!ok) break;
-            // combine this row tile: k ascending fused multiply-adds, then the shared expert
-            for (int c = ctid; c < T * rt_c; c += 32 * kFdCompute) {
-                const int t = c / rt_c, r = c % rt_c;
+            if (!wok) break;
+            __syncwarp();
+            // combine: k ascending fused multiply-adds, then the shared expert
+            if (lane < T) {
+                const int t = lane;
                 float acc = 0.f;
                 for (int k = 0; k < K; k++) {
                     const int i = t * K + k, e = s_order[i];
-                    if (e >= 0 && e < E) acc = fmaf(s_wtop[i], ys[i * rt_c + r], acc);
+                    if (e >= 0 && e < E) acc = fmaf(s_wtop[i], yw[i], acc);
                 }
-                if (sh) acc = __fadd_rn(acc, ys[(NA + t) * rt_c + r]);
-                a.out[(size_t)t * a.n_out + (size_t)j * rt_c + r] = acc;
+                if (sh) acc = __fadd_rn(acc, yw[NA + t]);
+                a.out[(size_t)t * a.n_out + r] = acc;
             }
-            fd_compute_sync();
+            __syncwarp();
         }
-        if (ctid == 0) s_qc = (int)q;
+        if (a.stamps && lane == 0) {
+            a.stamps[(size_t)blockIdx.x * 64 + 40 + warp] = sync::global_ns();
+            if (warp == 0 || warp == 15)
+                for (int i = 0; i < 4; i++) a.stamps[(size_t)blockIdx.x * 64 + 56 + (warp ? 4 : 0) + i] = t_acc[i];
+        }
+        // copies issued but not consumed (after a failure) land before the warp exits
+        if (lane == 0)
+            for (uint32_t r = n_con; r < n_iss; r++) sync::mbar_wait(&wfull[r % NST], (r / NST) & 1);
+        __syncwarp();
         fd_stamp(a, 6);
     }
     __syncthreads();
-    // copies issued but not consumed (after a failure) land before the block exits
+    // router copies issued but not consumed (after a failure) land before the block exits
     if (producer && lane == 0)
         for (uint32_t r = (uint32_t)s_qc; r < q; r++) sync::mbar_wait(&full[r % S], (r / S) & 1);
 }
@@ -870,64 +1115,60 @@ int launch_fused_decode(FusedDecodeArgs a, int cg, int cu, int cd, cudaStream_t 
     auto ok_code = [](int c) { return c == DRACO_CODE_Q4_K || c == DRACO_CODE_Q6_K; };
     if (!ok_code(cg) || !ok_code(cd)) return 1;
     if (a.q6s != kQ6Padded && (cg == DRACO_CODE_Q6_K || cd == DRACO_CODE_Q6_K)) return 1;
-    int dev = 0, sms = 0, coop = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) ||
-        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) || !coop) {
+    // per device: SM count and cooperative-launch support; per (kernel, shared memory bytes): the
+    // attribute set and the occupancy check passed (queried once, not on every decode call)
+    struct DevInfo {
+        int sms = -1, coop = 0;
+        std::vector<std::pair<const void*, size_t>> ready;   // (kernel, bytes) checked
+        std::vector<std::pair<const void*, size_t>> attr;    // (kernel, largest bytes set)
+    };
+    static DevInfo info[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
         cudaGetLastError();
         return 1;
     }
+    DevInfo& di = info[dev];
+    if (di.sms < 0) {
+        if (cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev) ||
+            cudaDeviceGetAttribute(&di.coop, cudaDevAttrCooperativeLaunch, dev)) {
+            cudaGetLastError();
+            di.sms = -1;
+            return 1;
+        }
+    }
+    const int sms = di.sms;
+    if (!di.coop) return 1;
     const int G = sms;   // one block per SM
-    const int nb = H / 256, nbd = a.F / 256, nbds = a.sh_ff / 256;
-    const size_t rbg = (size_t)nb * superblock_bytes(cg, a.q6s), rbu = (size_t)nb * superblock_bytes(cu, a.q6s);
-    const size_t rbd = (size_t)nbd * superblock_bytes(cd, a.q6s), rbds = (size_t)nbds * superblock_bytes(cd, a.q6s);
-    constexpr size_t kSlotMax = 64 * 1024;
-    auto slot_b = [&](int rt) { return (size_t)rt * (rbg + rbu) + (size_t)rt * nb * (groups_of(cg) + groups_of(cu)) * 8; };
-    auto tile_c = [&](int rt) {
-        return (size_t)rt * std::max(rbd, rbds) + (size_t)rt * std::max(nbd, nbds) * groups_of(cd) * 8;
-    };
-    const int n_act_max = std::min(T * K, E);
-    const int exp_c_max = n_act_max + (a.sh_ff ? 1 : 0);
-    // tile rows: the largest with at least one item per block, else the smallest that fits
-    static const int cand[4] = {16, 12, 8, 4};
-    int rt_b = 0, rt_c = 0;
-    for (int r : cand)
-        if (a.F % r == 0 && a.sh_ff % r == 0 && slot_b(r) <= kSlotMax) {
-            rt_b = r;
-            if (n_act_max * (a.F / r) >= G) break;
-        }
-    for (int r : cand)
-        if (a.n_out % r == 0 && tile_c(r) <= kSlotMax) {
-            rt_c = r;
-            if (a.n_out / r >= G) break;
-        }
-    if (!rt_b || !rt_c) return 1;
-    // experts per down job: as many tiles as a slot holds, split evenly over the jobs
-    const int gmax = std::max(1, (int)(kSlotMax / tile_c(rt_c)));
-    const int njobs = (exp_c_max + gmax - 1) / gmax;
-    const int c_group = (exp_c_max + njobs - 1) / njobs;
-    // router chunk: the longest of 512 / 256 / 128 values whose stage fits a slot
+    // router chunk: the longest of 512 / 256 / 128 values whose ring stage stays within 64 KB
     const int nch_max = (T * E + G - 1) / G;
     if (nch_max > 32) return 1;
     auto stage_a = [&](int kc) { return (size_t)(nch_max + T) * (kc + 4) * 4; };
-    const size_t slot_bc = std::max(slot_b(rt_b), (size_t)c_group * tile_c(rt_c));
     int kc = 128;
     for (int c : {512, 256})
-        if (H % c == 0 && stage_a(c) <= std::max(slot_bc, (size_t)8192)) {
+        if (H % c == 0 && stage_a(c) <= 64u * 1024) {
             kc = c;
             break;
         }
-    size_t slot = std::max(slot_bc, stage_a(kc));
-    slot = (slot + 127) / 128 * 128;
-    // token rows (phase B) / activation rows (phase C) staged in shared memory up to 64 KB
+    const size_t slot = (stage_a(kc) + 127) / 128 * 128;
+    // token rows (phase B) / activation rows (phase C) staged in shared memory up to 32 KB
     const size_t rows_b = (size_t)T * H, rows_c = (size_t)T * K * a.F + (size_t)T * a.sh_ff;
-    const int xs_cap = (int)std::min<size_t>(16384, std::max(rows_b, rows_c));
+    const int xs_cap = (int)std::min<size_t>(8192, std::max(rows_b, rows_c));
     const size_t extra = (size_t)xs_cap * 4 + ((size_t)kFdMaxTokens * ((E + 3) & ~3) + kFdMaxTokens * 64) * 4 +
                          2 * kFdMaxAssign * 4 + (2 * kFdMaxAssign + kFdMaxAssign * kFdMaxTokens) * 4 +
-                         (size_t)(kFdMaxAssign + kFdMaxTokens) * 16 * 4 + 256;
+                         (size_t)(kFdMaxAssign + kFdMaxTokens) * kFdCompute * 4 + 256;
+    // per-warp weight-row ring: stages of the longest row, as many as fit (at least 2: a gate/up
+    // task holds two)
+    const int bg = superblock_bytes(cg, a.q6s), bd = superblock_bytes(cd, a.q6s);
+    const size_t stg = std::max({(size_t)(H / 256) * bg, (size_t)(a.F / 256) * bd, (size_t)(a.sh_ff / 256) * bd});
+    constexpr size_t kSmemMax = 220u * 1024;
+    if (extra + 2 * kFdCompute * stg > kSmemMax) return 1;
+    const int n_stg = (int)std::min<size_t>(kFdMaxStg, (kSmemMax - extra) / (kFdCompute * stg));
     int slots = kFdMaxSlots;
-    while (slots > 2 && slots * slot + extra > 220u * 1024) slots--;
-    const size_t total = slots * slot + extra;
-    if (total > 220u * 1024) return 1;
+    const size_t wring = (size_t)kFdCompute * n_stg * stg;
+    while (slots > 2 && slots * slot > std::max(wring, kSmemMax - extra)) slots--;
+    const size_t total = std::max(slots * slot, wring) + extra;
+    if (total > kSmemMax) return 1;
     const void* kern = nullptr;
     const int ns = E <= 128 ? 4 : E <= 256 ? 8 : 16;
     constexpr int Q4 = DRACO_CODE_Q4_K, Q6 = DRACO_CODE_Q6_K;
@@ -942,21 +1183,31 @@ int launch_fused_decode(FusedDecodeArgs a, int cg, int cu, int cd, cudaStream_t 
     DRACO_FD_PICK(Q6, Q4)
 #undef DRACO_FD_PICK
     if (!kern) return 1;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess) {
-        cudaGetLastError();
-        return 1;
+    // the kernel's dynamic shared memory limit only grows: a smaller request after a larger one
+    // keeps the larger setting, which covers both
+    auto at = std::find_if(di.attr.begin(), di.attr.end(), [&](const auto& p) { return p.first == kern; });
+    if (at == di.attr.end() || at->second < total) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess) {
+            cudaGetLastError();
+            return 1;
+        }
+        if (at == di.attr.end()) di.attr.emplace_back(kern, total);
+        else at->second = total;
     }
-    int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kFdThreads, total) != cudaSuccess || occ < 1) {
-        cudaGetLastError();
-        return 1;
+    const std::pair<const void*, size_t> key(kern, total);
+    if (std::find(di.ready.begin(), di.ready.end(), key) == di.ready.end()) {
+        int occ = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kFdThreads, total) != cudaSuccess || occ < 1) {
+            cudaGetLastError();
+            return 1;
+        }
+        di.ready.push_back(key);
     }
-    a.rt_b = rt_b;
-    a.rt_c = rt_c;
     a.slot_bytes = (int)slot;
     a.n_slots = slots;
+    a.stg_bytes = (int)stg;
+    a.n_stg = n_stg;
     a.kc = kc;
-    a.c_group = c_group;
     a.xs_cap = xs_cap;
     void* args[] = {&a};
     const cudaError_t e = cudaLaunchCooperativeKernel(kern, G, kFdThreads, args, total, s);

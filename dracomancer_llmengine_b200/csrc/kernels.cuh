@@ -93,8 +93,9 @@ struct FusedDecodeArgs {
     int q6s;
     int bar_extra;              // test hook: arrivals awaited beyond the grid (0 in use)
     unsigned long long* stamps; // optional [grid][8] %globaltimer at the phase boundaries (or null)
-    int rt_b, rt_c, slot_bytes, n_slots;   // set by the launcher: tile rows, ring slots
-    int kc, c_group, xs_cap;    // router k-chunk, experts per down job, staged-row floats
+    int slot_bytes, n_slots;    // set by the launcher: router ring slots
+    int stg_bytes, n_stg;       // per-warp weight-row ring: stage bytes, stages
+    int kc, xs_cap;             // router k-chunk, staged-row floats
 };
 // 0 launched; 1 not applicable (the caller runs the separate kernels); -3 launch error
 int launch_fused_decode(FusedDecodeArgs a, int cg, int cu, int cd, cudaStream_t s);

@@ -55,6 +55,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         if ((i & 63) == 0 && global_ns() - t0 > kWaitLimitNs) return false;
     }
 }
+// orders this thread's earlier generic-proxy accesses of shared memory before its later
+// async-proxy ones (a bulk copy into a buffer that was just read)
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // global -> shared bulk copy (both addresses 16-byte aligned, bytes a multiple of 16), completing
 // on bar's transaction count
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -114,11 +114,15 @@ def test_fused_barrier_wait_runs_out_and_reports(dlib, port):
     d = dm.layer_desc(layer, keep)
     out = np.empty((2, layer.hidden), np.float32)
     dlib.draco_b200_test_fused_barrier_extra(1)
+    dm.profile(True)
     try:
         rc = dlib.draco_b200_moe_forward(ct.byref(d), X.ctypes.data, 2, out.ctypes.data, None, None, None)
     finally:
         dlib.draco_b200_test_fused_barrier_extra(0)
-    assert rc == -5, (rc, dm.last_error())
+        prof = dm.profile_read()
+        dm.profile(False)
+    assert prof["fused"][1] >= 1, "the fused kernel did not run"
+    assert rc == -5, (rc, dm.last_error(), prof["fused"])
     assert "0x1000" in dm.last_error()
     good = dm.forward(layer, X)
     o_ref, w_ref = port.route(layer, X)
