@@ -12,7 +12,7 @@
 // one device) race on the array: serialise them.
 //
 // The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
-// that device current and remembers it; make that first call before any stream capture.
+// that device current and remembers it.
 // Nothing here calls cudaMalloc, cudaFree or any other allocating routine.
 #include "../../include/draco_moe_b200.h"
 #include "kernels.cuh"

@@ -258,9 +258,10 @@ int draco_b200_ep_pull_combine(const float* const* src_partial, const int* row_o
  * is a fixed 32 MiB device array inside the library, held by every GPU that loads it until the
  * process exits: calls needing more (T*n_used*(inter+n_out)*4 bytes plus small lists) return -4
  * without running.  All calls share that array and it keeps the last call's contents; calls that
- * overlap on the GPU race on it.  The first call on a device looks up the array's address (make
- * it before any stream capture).  Asynchronous on `stream`.  Returns 0, -1 (shape or
- * arguments), -3 (CUDA error), -4 (exceeds the scratch maximum); messages go to stderr. */
+ * overlap on the GPU race on it.  The first call on a device looks up the array's address.
+ * Asynchronous on `stream`.  Returns 0, -1 (shape or arguments, including a null weight address
+ * or one not aligned for its format: Q4_K 16 bytes, the others 2), -3 (CUDA error), -4 (exceeds
+ * the scratch maximum); messages go to stderr. */
 int draco_b200_moe_tok_noalloc(const float* X, const int* order, const float* wtop,
                                const uint64_t* ep_dev, const int* ec, int T, int n_used, int inter,
                                int n_in, int n_out, int n_exp, float* out, void* stream);

@@ -94,7 +94,8 @@ def logits_ref(X, W):
 # (width % 4 != 0)
 @pytest.mark.parametrize("T,E,H", [(1, 128, 2048), (3, 384, 7168), (4, 60, 516), (5, 128, 2048), (48, 384, 1024),
                                    (300, 128, 512), (600, 128, 2048), (2400, 256, 256), (2400, 256, 260),
-                                   (40, 64, 258)])
+                                   (40, 64, 258), (512, 128, 2048), (64, 384, 7168), (100, 128, 2048),
+                                   (33, 90, 1028)])
 def test_router_logits_exact_order(dlib, T, E, H):
     rng = np.random.default_rng(T + E + H)
     X = rng.standard_normal((T, H), dtype=np.float32)
