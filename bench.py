@@ -106,10 +106,10 @@ def layer_work(layer, order, T, experts=None):
                 gateup_flops=2 * 2 * H * F * assign, assignments=assign)
 
 
-def profiled_traffic(config: str):
-    """DRAM bytes per launch of the gate/up GEMM kernel from the committed ncu summary of this
-    workload (profiles/tc_gemm_<config>.md, line `traffic_bytes_per_launch: N`), else None."""
-    p = os.path.join(ROOT, "profiles", f"tc_gemm_{config}.md")
+def profiled_traffic(config: str, kernel: str = "tc_gemm"):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary of this
+    workload (profiles/<kernel>_<config>.md, line `traffic_bytes_per_launch: N`), else None."""
+    p = os.path.join(ROOT, "profiles", f"{kernel}_{config}.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -517,7 +517,7 @@ def run_workload(name, args, ctx, headline):
             "achieved": gu_tfs if tensor_bound else gu_gbs, "peak": bf16 if tensor_bound else hbm,
             "unit": "TFLOP/s" if tensor_bound else "GB/s",
             "frac": (gu_tfs / bf16) if tensor_bound else (gu_gbs / hbm),
-            "traffic": profiled_traffic(name) if world == 1 else None,
+            "traffic": profiled_traffic(name, "fused_decode" if fused else "tc_gemm") if world == 1 else None,
             "algorithmic_bytes": kbytes, "algorithmic_flops": kflops,
             "peak_source": src + (" (cuBLAS bf16 burst; the kernel runs fp16 operands)" if tensor_bound else
                                   " (copy bandwidth)"),
