@@ -916,8 +916,8 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         static unsigned long long* fd_stamps = nullptr;   // DRACO_B200_FD_STATS=1: phase timestamps
         if (!fd_stamps && env_flag("DRACO_B200_FD_STATS")) {
             // device memory (a managed buffer would migrate to the host and back between calls)
-            cudaMalloc(&fd_stamps, sizeof(unsigned long long) * 64 * 4096);
-            cudaMemset(fd_stamps, 0, sizeof(unsigned long long) * 64 * 4096);
+            cudaMalloc(&fd_stamps, sizeof(unsigned long long) * 128 * 4096);
+            cudaMemset(fd_stamps, 0, sizeof(unsigned long long) * 128 * 4096);
         }
         f.stamps = fd_stamps;
         CK(cudaMemsetAsync(b.fd_ctl, 0, 4 * sizeof(int), s));
@@ -934,24 +934,26 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
             if (fd_stamps) {
                 // per phase: median and max over the blocks of the time since the block started
                 cudaStreamSynchronize(s);
-                std::vector<unsigned long long> hs((size_t)64 * 4096);
+                std::vector<unsigned long long> hs((size_t)128 * 4096);
                 cudaMemcpy(hs.data(), fd_stamps, sizeof(unsigned long long) * hs.size(), cudaMemcpyDeviceToHost);
                 cudaMemset(fd_stamps, 0, sizeof(unsigned long long) * hs.size());
                 const unsigned long long* st = hs.data();
                 int G = 0;
-                while (G < 4096 && st[(size_t)G * 64] != 0) G++;
+                while (G < 4096 && st[(size_t)G * 128] != 0) G++;
                 fprintf(stderr, "[fused decode stats] blocks=%d", G);
                 static const char* nm[7] = {"start", "A", "bar1", "S", "B", "bar2", "C"};
-                for (int i = 1; i < 7; i++) {
+                for (int i : {1, 2, 66, 64, 65, 3, 4, 5, 6}) {
                     std::vector<double> v;
                     for (int g = 0; g < G; g++)
-                        if (st[(size_t)g * 64 + i]) v.push_back((st[(size_t)g * 64 + i] - st[(size_t)g * 64]) * 1e-3);
+                        if (st[(size_t)g * 128 + i]) v.push_back((st[(size_t)g * 128 + i] - st[(size_t)g * 128]) * 1e-3);
                     std::sort(v.begin(), v.end());
-                    if (!v.empty()) fprintf(stderr, " %s=%.1f/%.1fus", nm[i], v[v.size() / 2], v.back());
+                    if (!v.empty())
+                        fprintf(stderr, " %s=%.1f/%.1fus", i < 7 ? nm[i] : i == 66 ? "S:logits" : i == 64 ? "S:select" : "S:list",
+                                v[v.size() / 2], v.back());
                 }
                 for (int blk : {0, G / 2}) {
                     if (blk >= G) continue;
-                    const unsigned long long* sb = st + (size_t)blk * 64;
+                    const unsigned long long* sb = st + (size_t)blk * 128;
                     fprintf(stderr, "\n[block %d per warp: first piece / B done / C done us]", blk);
                     for (int w = 0; w < 16; w++)
                         fprintf(stderr, " %d:%.1f/%.1f/%.1f", w, sb[8 + w] ? (sb[8 + w] - sb[0]) * 1e-3 : -1.0,

@@ -547,9 +547,10 @@ constexpr int kFdMaxTokens = 8;
 constexpr int kFdMaxAssign = 64;
 constexpr int kFdCompute = 16;            // compute warps (the producer warp is warp 16)
 constexpr int kFdThreads = 32 * (kFdCompute + 1);
-constexpr int kFdMaxSlots = 4;
+constexpr int kFdMaxSlots = 16;              // router chunk slots (all chunks at once when they fit)
 constexpr int kFdMaxStg = 8;              // per-warp weight-row ring stages
 constexpr uint64_t kFdGridWaitNs = 1000000000ull;
+constexpr int kFdStampStride = 128;       // DRACO_B200_FD_STATS words per block
 
 __device__ __forceinline__ void fd_compute_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kFdCompute) : "memory"); }
 
@@ -585,7 +586,7 @@ __device__ __forceinline__ void fd_stage_rows(float* dst, const float* src, size
 
 // optional phase timestamps (DRACO_B200_FD_STATS): thread 0 of each block
 __device__ __forceinline__ void fd_stamp(const FusedDecodeArgs& a, int i) {
-    if (a.stamps && threadIdx.x == 0) a.stamps[(size_t)blockIdx.x * 64 + i] = sync::global_ns();
+    if (a.stamps && threadIdx.x == 0) a.stamps[(size_t)blockIdx.x * kFdStampStride + i] = sync::global_ns();
 }
 
 template <int CG, int CU, int CD, int NS>
@@ -673,11 +674,26 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
     const int nch = (a.W && b < C) ? (C - 1 - b) / G + 1 : 0;
     const int KC = a.kc, RS = a.kc + 4;
     const int n_chunks = H / KC;
+    // all k-chunks fit the slots at once: the copy warp issues them all up front and warp 0 alone
+    // walks its chains as each chunk lands (no per-chunk block synchronisation); else the ring
+    const bool all_at_once = n_chunks <= S;
+    auto chain_chunk = [&](const uint8_t* src, float& acc, int ct) {
+        const float4* w4 = reinterpret_cast<const float4*>(src + (size_t)lane * RS * 4);
+        const float4* x4 = reinterpret_cast<const float4*>(src + (size_t)(nch + ct) * RS * 4);
+#pragma unroll 8
+        for (int k = 0; k < KC / 4; k++) {
+            const float4 w = w4[k], x = x4[k];
+            acc = __fadd_rn(acc, __fmul_rn(x.x, w.x));
+            acc = __fadd_rn(acc, __fmul_rn(x.y, w.y));
+            acc = __fadd_rn(acc, __fmul_rn(x.z, w.z));
+            acc = __fadd_rn(acc, __fmul_rn(x.w, w.w));
+        }
+    };
     if (nch > 0) {
         if (producer) {
             if (lane == 0)
                 for (int ch = 0; ch < n_chunks; ch++) {
-                    uint8_t* dst = claim();
+                    uint8_t* dst = all_at_once ? ring + (size_t)ch * a.slot_bytes : claim();
                     if (!dst) break;
                     const int sl = q % S;
                     sync::mbar_expect_tx(&full[sl], (uint32_t)(nch + T) * KC * 4);
@@ -691,6 +707,24 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                                         KC * 4, &full[sl]);
                     q++;
                 }
+        } else if (all_at_once) {
+            if (warp == 0) {
+                float acc = 0.f;
+                const int c = b + G * lane;
+                const int ct = c / E;
+                bool done = true;
+                for (int ch = 0; ch < n_chunks; ch++) {
+                    if (!sync::mbar_wait(&full[ch], 0)) {
+                        if (lane == 0) atomicOr(a.status, 0x200);
+                        s_cabort = 1;
+                        done = false;
+                        break;
+                    }
+                    if (lane < nch) chain_chunk(ring + (size_t)ch * a.slot_bytes, acc, ct);
+                    q++;
+                }
+                if (done && lane < nch) a.logits[(size_t)ct * E + c % E] = acc;
+            }
         } else {
             float acc = 0.f;
             const int c = b + G * lane;
@@ -702,18 +736,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                     done = false;
                     break;
                 }
-                if (warp == 0 && lane < nch) {
-                    const float4* w4 = reinterpret_cast<const float4*>(src + (size_t)lane * RS * 4);
-                    const float4* x4 = reinterpret_cast<const float4*>(src + (size_t)(nch + ct) * RS * 4);
-#pragma unroll 8
-                    for (int k = 0; k < KC / 4; k++) {
-                        const float4 w = w4[k], x = x4[k];
-                        acc = __fadd_rn(acc, __fmul_rn(x.x, w.x));
-                        acc = __fadd_rn(acc, __fmul_rn(x.y, w.y));
-                        acc = __fadd_rn(acc, __fmul_rn(x.z, w.z));
-                        acc = __fadd_rn(acc, __fmul_rn(x.w, w.w));
-                    }
-                }
+                if (warp == 0 && lane < nch) chain_chunk(src, acc, ct);
                 release();
             }
             if (done && warp == 0 && lane < nch) a.logits[(size_t)ct * E + c % E] = acc;
@@ -739,6 +762,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                 float* Vw = V + (size_t)warp * ES;
                 for (int e = lane; e < E; e += 32) Vw[e] = __ldcg(a.logits + (size_t)t * E + e);
                 __syncwarp();
+                if (t == 0) fd_stamp(a, 66);
                 select_token<NS>(a.rp, Vw, s_order + t * K, s_wtop + t * K, a.route_err, Vw, gsm + warp * 64);
                 __syncwarp();
             }
@@ -749,6 +773,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             }
         }
     }
+    fd_stamp(a, 64);
     __syncthreads();
     if (ok && a.W && b == 0)
         for (int i = threadIdx.x; i < NA; i += blockDim.x) {
@@ -788,6 +813,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
         s_n_act = n;
     }
     __syncthreads();
+    fd_stamp(a, 65);
     if (ok && threadIdx.x < 3 * s_n_act) s_wp[threadIdx.x] = a.tab.w[3 * act_e[threadIdx.x / 3] + threadIdx.x % 3];
     __syncthreads();
     fd_stamp(a, 3);
@@ -870,7 +896,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             }
             wok = __all_sync(0xffffffffu, wok);
             if (a.stamps) t_acc[2 * t_ph] += sync::global_ns() - tw0;
-            if (a.stamps && lane == 0 && n_con == 0) a.stamps[(size_t)blockIdx.x * 64 + 8 + warp] = sync::global_ns();
+            if (a.stamps && lane == 0 && n_con == 0) a.stamps[(size_t)blockIdx.x * kFdStampStride + 8 + warp] = sync::global_ns();
             return wok ? wring + (size_t)st * a.stg_bytes : nullptr;
         };
         auto release_pieces = [&](int n) {
@@ -926,7 +952,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             release_pieces(2);
         }
         if (!wok) s_cabort = 1;
-        if (a.stamps && lane == 0) a.stamps[(size_t)blockIdx.x * 64 + 24 + warp] = sync::global_ns();
+        if (a.stamps && lane == 0) a.stamps[(size_t)blockIdx.x * kFdStampStride + 24 + warp] = sync::global_ns();
         // ------------------------------------------------------------ grid barrier 2
         fd_compute_sync();
         fd_stamp(a, 4);
@@ -1033,9 +1059,9 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             __syncwarp();
         }
         if (a.stamps && lane == 0) {
-            a.stamps[(size_t)blockIdx.x * 64 + 40 + warp] = sync::global_ns();
+            a.stamps[(size_t)blockIdx.x * kFdStampStride + 40 + warp] = sync::global_ns();
             if (warp == 0 || warp == 15)
-                for (int i = 0; i < 4; i++) a.stamps[(size_t)blockIdx.x * 64 + 56 + (warp ? 4 : 0) + i] = t_acc[i];
+                for (int i = 0; i < 4; i++) a.stamps[(size_t)blockIdx.x * kFdStampStride + 56 + (warp ? 4 : 0) + i] = t_acc[i];
         }
         // copies issued but not consumed (after a failure) land before the warp exits
         if (lane == 0)
@@ -1164,8 +1190,12 @@ int launch_fused_decode(FusedDecodeArgs a, int cg, int cu, int cd, cudaStream_t 
     constexpr size_t kSmemMax = 220u * 1024;
     if (extra + 2 * kFdCompute * stg > kSmemMax) return 1;
     const int n_stg = (int)std::min<size_t>(kFdMaxStg, (kSmemMax - extra) / (kFdCompute * stg));
-    int slots = kFdMaxSlots;
     const size_t wring = (size_t)kFdCompute * n_stg * stg;
+    // router chunk slots: every chunk of the row at once when they fit next to the weight rings'
+    // share of shared memory (they alias it), else a ring of 4
+    const int n_chunks = H / kc;
+    int slots = 4;
+    if (n_chunks <= kFdMaxSlots && n_chunks * slot <= std::max(wring, kSmemMax - extra)) slots = std::max(4, n_chunks);
     while (slots > 2 && slots * slot > std::max(wring, kSmemMax - extra)) slots--;
     const size_t total = std::max(slots * slot, wring) + extra;
     if (total > kSmemMax) return 1;
