@@ -537,6 +537,8 @@ def run_workload(name, args, ctx, headline):
               "l2": "weights and activations exceed L2 (no flush needed)" if name != "cfg1_decode"
               else "decode weights 25 MB fit in L2; flushed between steps by a 256 MB write then a 256 MB read",
               "parallelism": par, "distinct_experts": work["distinct"], "assignments": work["assignments"]}
+    if args.overrides:
+        config["override"] = dict(args.overrides)
     rec = {"value": value, "unit": "tok/s", "ms_per_step": ms_per_step, "scaling": scaling, "config": config,
            "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": int(T * layer.hidden * 4),
                    "d2h_bytes_per_step": int(T * layer.hidden * 4)},
@@ -568,6 +570,9 @@ def main():
                     help="comma-separated workloads reported under `configs` ('none': headline only)")
     ap.add_argument("--impl", default="draco", choices=["draco", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--override", default="",
+                    help="KEY=VALUE[,KEY=VALUE] changes to the workloads' shape (n_exp, tokens), for profiler "
+                         "captures of a smaller case of the same kernels; the line says so in config.override")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "fixed", "compact"],
                     help="expert-parallel token exchange (N > 1): peer-memory stores/loads with flag barriers, "
                          "or NCCL all-to-all with fixed blocks / exchanged counts")
@@ -578,6 +583,15 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
     from dracomancer_llmengine_b200 import synth
+    overrides = {}
+    for kv in filter(None, args.override.split(",")):
+        k, v = kv.split("=", 1)
+        if k not in ("n_exp", "tokens"):
+            raise SystemExit(f"--override: {k} is not n_exp or tokens")
+        overrides[k] = int(v)
+    for c in synth.CONFIGS.values():
+        c.update(overrides)
+    args.overrides = overrides
     cfgd = synth.CONFIGS[args.config]
     T = cfgd["tokens"]
 
