@@ -106,18 +106,22 @@ def layer_work(layer, order, T, experts=None):
                 gateup_flops=2 * 2 * H * F * assign, assignments=assign)
 
 
-def profiled_traffic(config: str, kernel: str = "tc_gemm"):
+def profiled_traffic(config: str, kernel: str = "tc_gemm", algorithmic_bytes: float = 0.0):
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary of this
-    workload (profiles/<kernel>_<config>.md, line `traffic_bytes_per_launch: N`), else None."""
+    workload (profiles/<kernel>_<config>.md): the line `traffic_bytes_per_launch: N` of a
+    capture at full size, or `traffic_per_algorithmic_byte: r` of a capture on a smaller case of
+    the same kernel, scaled here by this launch's algorithmic bytes; else None."""
     p = os.path.join(ROOT, "profiles", f"{kernel}_{config}.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
-        if line.startswith("traffic_bytes_per_launch:"):
-            try:
+        try:
+            if line.startswith("traffic_bytes_per_launch:"):
                 return int(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
+            if line.startswith("traffic_per_algorithmic_byte:") and algorithmic_bytes:
+                return int(float(line.split(":", 1)[1].strip()) * algorithmic_bytes)
+        except ValueError:
+            return None
     return None
 
 
@@ -517,7 +521,8 @@ def run_workload(name, args, ctx, headline):
             "achieved": gu_tfs if tensor_bound else gu_gbs, "peak": bf16 if tensor_bound else hbm,
             "unit": "TFLOP/s" if tensor_bound else "GB/s",
             "frac": (gu_tfs / bf16) if tensor_bound else (gu_gbs / hbm),
-            "traffic": profiled_traffic(name, "fused_decode" if fused else "tc_gemm") if world == 1 else None,
+            "traffic": (profiled_traffic(name, "fused_decode" if fused else "tc_gemm", kbytes)
+                        if world == 1 and not args.overrides else None),
             "algorithmic_bytes": kbytes, "algorithmic_flops": kflops,
             "peak_source": src + (" (cuBLAS bf16 burst; the kernel runs fp16 operands)" if tensor_bound else
                                   " (copy bandwidth)"),
