@@ -313,7 +313,25 @@ void launch_router_logits(const float* X, const float* W, int T, int E, int H, f
     const bool vec_ok = H % 4 == 0 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0;
     if (vec_ok) {
         if (router_tiles(T, E, 64, 64) >= 148) {   // enough 64 x 64 tiles for every SM: 16 chains a lane
-            launch_router_tile<8, 2, 8, 3>(X, W, T, E, H, logits, s, zero_err);
+            // token rows per warp (8 warps a block): the one that minimises the busiest SM's
+            // work, (blocks on that SM) x (rows per warp); the full 8-row tiles of cfg4 (256 blocks
+            // on 148 SMs) left 40 SMs with one block while the others ran two
+            int best = 8;
+            long best_cost = -1;
+            for (int tpw = 8; tpw >= 5; tpw--) {
+                const long blocks = (long)((T + 8 * tpw - 1) / (8 * tpw)) * ((E + 63) / 64);
+                const long cost = (blocks + 147) / 148 * tpw;
+                if (best_cost < 0 || cost < best_cost) {
+                    best_cost = cost;
+                    best = tpw;
+                }
+            }
+            switch (best) {
+                case 5: launch_router_tile<5, 2, 8, 3>(X, W, T, E, H, logits, s, zero_err); break;
+                case 6: launch_router_tile<6, 2, 8, 3>(X, W, T, E, H, logits, s, zero_err); break;
+                case 7: launch_router_tile<7, 2, 8, 3>(X, W, T, E, H, logits, s, zero_err); break;
+                default: launch_router_tile<8, 2, 8, 3>(X, W, T, E, H, logits, s, zero_err); break;
+            }
             return;
         }
         if (T <= 16) {

@@ -90,12 +90,13 @@ def logits_ref(X, W):
 
 
 # shapes reaching every logits kernel: the small-batch tiles (deep and shallow rings, partial last
-# chunk, batches of 1-5 tokens), the register-tiled kernel for many tiles, the scalar fallback
-# (width % 4 != 0)
+# chunk, batches of 1-5 tokens), the register-tiled kernel for many tiles with 5, 6, 7 and 8 token
+# rows a warp, the scalar fallback (width % 4 != 0)
 @pytest.mark.parametrize("T,E,H", [(1, 128, 2048), (3, 384, 7168), (4, 60, 516), (5, 128, 2048), (48, 384, 1024),
                                    (300, 128, 512), (600, 128, 2048), (2400, 256, 256), (2400, 256, 260),
                                    (40, 64, 258), (512, 128, 2048), (64, 384, 7168), (100, 128, 2048),
-                                   (33, 90, 1028)])
+                                   (33, 90, 1028), (4744, 128, 256), (5928, 128, 260), (7112, 128, 256),
+                                   (4680, 128, 256)])
 def test_router_logits_exact_order(dlib, T, E, H):
     rng = np.random.default_rng(T + E + H)
     X = rng.standard_normal((T, H), dtype=np.float32)
