@@ -1015,7 +1015,8 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         const TcMaps& maps = *(const TcMaps*)a.tab->tc;
         if (rc == 0) {
             PhaseScope ps(kGather, s);
-            tc_gather(call, b.x, xh, rb.ilist, rb.off + a.E, a.K, b.xs_h, s);
+            if (xh) tc_gather(call, b.x, xh, rb.ilist, rb.off + a.E, a.K, b.xs_h, s);
+            else tc_gather_tokens(call, b.x, rb.order, rb.pos_of, T, a.K, a.E, b.xs_h, s);
         }
         if (rc == 0) {
             PhaseScope ps(kGateUp, s);

@@ -540,8 +540,8 @@ __device__ __forceinline__ void rows_dot_smem(const uint8_t* const (&rows)[R], i
 // activations), so the weights of the whole layer are in flight while phase B computes.  Per
 // row the arithmetic and its order are those of the separate dec_* kernels.
 // Every wait is bounded: an mbarrier wait gives up after 2 s, a grid barrier after 1 s; a block
-// that gives up raises a status bit (0x200 copy, 0x1000 grid barrier), stops, and waits for its
-// own copies in flight before it exits.
+// that gives up raises a status bit (0x200 copy, 0x1000 grid barrier, 0x2000 a weight row that is
+// not a whole aligned row), stops, and waits for its own copies in flight before it exits.
 // ------------------------------------------------------------------------------------------
 constexpr int kFdMaxTokens = 8;
 constexpr int kFdMaxAssign = 64;
@@ -838,10 +838,12 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
         uint8_t* wring = ring + (size_t)warp * NST * a.stg_bytes;
         uint64_t* wfull = s_wfull[warp];
         // producer cursor (uniform over the warp; lane 0 issues): the next piece's phase, task, part
+        // (phase C has no pieces when no expert is active and there is no shared expert: every
+        // routing entry of the batch named no expert of the table)
         int p_ph = 0, p_task = gw, p_sub = 0;
         if (p_task >= tasks_b) {
             p_ph = 1;
-            if (p_task >= tasks_c) p_ph = 2;
+            if (p_task >= tasks_c || per_c == 0) p_ph = 2;
         }
         uint32_t n_iss = 0, n_con = 0;   // pieces issued / consumed
         bool wok = ok;
@@ -863,7 +865,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                         if (p_task >= tasks_b) {
                             p_ph = 1;
                             p_task = gw;
-                            if (p_task >= tasks_c) p_ph = 2;
+                            if (p_task >= tasks_c || per_c == 0) p_ph = 2;
                         }
                     }
                 } else {
@@ -875,6 +877,13 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                         p_task += GW;
                         if (p_task >= tasks_c) p_ph = 2;
                     }
+                }
+                // a piece must be a whole, aligned row that fits a stage (status 0x2000 otherwise:
+                // the warp stops instead of copying)
+                if (src == nullptr || bytes == 0 || bytes > (uint32_t)a.stg_bytes || ((uintptr_t)src & 15u)) {
+                    if (lane == 0) atomicOr(a.status, 0x2000);
+                    wok = false;
+                    break;
                 }
                 const int st = n_iss % NST;
                 if (lane == 0) {

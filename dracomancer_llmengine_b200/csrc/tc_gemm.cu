@@ -866,6 +866,30 @@ __global__ void gather_half_kernel(const float* __restrict__ X, const int* __res
     }
 }
 
+// The same rows written token by token: each fp32 token row is read once and its fp16 copy
+// stored to the slots of its valid assignments (pos_of[t*K + k], placed by the dispatch for
+// 0 <= order < E), instead of re-reading the row once per assignment.
+__global__ void gather_tokens_kernel(const float* __restrict__ X, const int* __restrict__ order,
+                                     const int* __restrict__ pos_of, int T, int K, int E, int H,
+                                     __half* __restrict__ Xs) {
+    const int per_row = H / 8;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < (long)T * per_row;
+         i += (long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / per_row), c8 = (int)(i % per_row) * 8;
+        const float4 a = *reinterpret_cast<const float4*>(X + (size_t)t * H + c8);
+        const float4 b = *reinterpret_cast<const float4*>(X + (size_t)t * H + c8 + 4);
+        uint4 o;   // kperm order: positions 1 and 2 of each group of 4 swapped
+        o.x = pack2(a.x, a.z);
+        o.y = pack2(a.y, a.w);
+        o.z = pack2(b.x, b.z);
+        o.w = pack2(b.y, b.w);
+        for (int k = 0; k < K; k++) {
+            const int e = order[(size_t)t * K + k];
+            if (e >= 0 && e < E) *reinterpret_cast<uint4*>(Xs + (size_t)pos_of[(size_t)t * K + k] * H + c8) = o;
+        }
+    }
+}
+
 // the same from token rows that are already fp16
 __global__ void gather_rows16_kernel(const __half* __restrict__ X, const int* __restrict__ ilist,
                                      const int* __restrict__ n_valid, int tok_div, int P, int H,
@@ -1025,6 +1049,12 @@ int tc_prepare(TcCall* call, int cg, int cd, int n_exp, int inter, int n_in, int
 void tc_dense_items(const TcCall& c, int4* items_gu, int* n_gu, int4* items_dn, int* n_dn, cudaStream_t s) {
     tc::dense_items_kernel<<<1, 256, 0, s>>>(c.P, c.nt, tc_tiles_gateup(c.inter), tc_tiles_down(c.n_out), items_gu,
                                              n_gu, items_dn, n_dn);
+}
+
+void tc_gather_tokens(const TcCall& c, const float* X, const int* order, const int* pos_of, int T, int K, int E,
+                      __half* Xs, cudaStream_t s) {
+    if (c.P <= 0 || T <= 0) return;
+    tc::gather_tokens_kernel<<<148 * 8, 256, 0, s>>>(X, order, pos_of, T, K, E, c.n_in, Xs);
 }
 
 void tc_gather(const TcCall& c, const void* X, bool x_half, const int* ilist, const int* n_valid, int tok_div,

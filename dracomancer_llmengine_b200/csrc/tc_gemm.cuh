@@ -41,6 +41,10 @@ int tc_prepare(TcCall* call, int cg, int cd, int n_exp, int inter, int n_in, int
                __half* act_h);
 void tc_gather(const TcCall& call, const void* X, bool x_half, const int* ilist, const int* n_valid, int tok_div,
                __half* Xs, cudaStream_t s);
+// the same for fp32 token rows read once each: row t goes to the slots pos_of[t*K + k] of its
+// assignments with 0 <= order[t*K + k] < E
+void tc_gather_tokens(const TcCall& c, const float* X, const int* order, const int* pos_of, int T, int K, int E,
+                      __half* Xs, cudaStream_t s);
 // item lists of a dense (shared-expert) call: one expert, call.P token rows in order
 void tc_dense_items(const TcCall& call, int4* items_gu, int* n_gu, int4* items_dn, int* n_dn, cudaStream_t s);
 int tc_gateup(const TcCall& call, const TcMaps& maps, const int4* items, const int* n_items, __half* act_h, int* err,

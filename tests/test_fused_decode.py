@@ -94,6 +94,34 @@ def test_fused_given_routing(dlib, port):
     assert rel_l2(got, want) <= REL_L2_TOL
 
 
+@pytest.mark.parametrize("shared", [False, True])
+def test_fused_no_routed_expert(dlib, port, shared):
+    """Every routing entry names no expert (ids -1): no routed expert runs; the output is zero,
+    or the shared expert alone."""
+    kw = dict(LAYERS["cfg1_shape_softmax"])
+    if shared:
+        kw["shared_inter"] = 512
+    layer = synth.make_layer(**kw)
+    X = synth.make_tokens(layer, 3, 12)
+    order = np.full((3, layer.n_used), -1, np.int32)
+    wtop = np.ones((3, layer.n_used), np.float32)
+    keep: list = []
+    d = dm.layer_desc(layer, keep)
+    got = np.full((3, layer.hidden), np.nan, np.float32)
+    dm.profile(True)
+    rc = dlib.draco_b200_experts_forward(ct.byref(d), X.ctypes.data, 3, order.ctypes.data, wtop.ctypes.data, 0, 0,
+                                         got.ctypes.data, 1 if shared else 0, 0, None)
+    prof = dm.profile_read()
+    dm.profile(False)
+    assert rc == 0, dm.last_error()
+    assert prof["fused"][1] >= 1, "the fused kernel did not run"
+    if shared:
+        want = port.layer_forward(layer, X, order, wtop)
+        assert rel_l2(got, want) <= REL_L2_TOL
+    else:
+        assert not np.any(got)
+
+
 def test_fused_ties_lower_index(dlib, port):
     layer = synth.make_layer(hidden=2048, n_exp=64, n_used=8, inter=512, seed=44)
     layer.gate_inp[1::2] = layer.gate_inp[0::2]     # experts 2k and 2k+1 tie everywhere
