@@ -266,12 +266,14 @@ def local_view(layer):
     return dataclasses.replace(layer, n_exp=n, expert0=0)
 
 
-def parity_check(layer, Xs, outs, orders, wtops, sample, world, rank, comm, experts):
+def parity_check(layer, Xs, outs, orders, wtops, sample, world, rank, comm, experts, replicas=False):
     """Routing of every token (all ranks' batches) bit-exact against the C restatement of the
     reference routers; output rows of a seeded sample against the reference's m6_moe_tok (+
     shared expert).  At N > 1 every rank computes the oracle's partial sums of the sampled rows
-    over its own expert slice (the slice it holds on the host) and rank 0 adds them.  Xs, outs,
-    orders, wtops: this rank's arrays.  Returns the record on rank 0."""
+    over its own expert slice (the slice it holds on the host) and rank 0 adds them; with
+    `replicas` (every rank runs the whole layer on its own tokens) rank 0 checks all ranks' rows
+    against the whole layer.  Xs, outs, orders, wtops: this rank's arrays.  Returns the record on
+    rank 0."""
     from oracle.oracle import Port, Ref, ref_available
     port = Port()
     T = Xs.shape[0]
@@ -296,7 +298,7 @@ def parity_check(layer, Xs, outs, orders, wtops, sample, world, rank, comm, expe
     lo, cnt = experts if experts else (0, layer.n_exp)
     o_loc = np.where((o_s >= lo) & (o_s < lo + cnt), o_s - lo, -1).astype(np.int32)
     part = R.moe_tok(local_view(layer) if experts else layer, X_s, o_loc, w_s) if len(X_s) else np.zeros((0, layer.hidden), np.float32)
-    parts = comm.all_gather_object(part) if world > 1 else [part]
+    parts = comm.all_gather_object(part) if world > 1 and not replicas else [part]
     if rank:
         return None
     want = np.sum(np.stack([p.astype(np.float64) for p in parts]), axis=0).astype(np.float32)
@@ -339,15 +341,19 @@ def run_workload(name, args, ctx, headline):
     T_cfg = cfgd["tokens"]
     layout, scaling = "a2a", "weak"
     if world > 1 and not headline:
-        if name in DECODE:
+        if name == "cfg1_decode":
+            # one decode token does not shard: sharding its 8 experts over GPUs only adds an
+            # exchange to a 50 us layer, so every GPU runs the whole layer on its own token
+            layout, scaling = "replicas", "weak"
+        elif name in DECODE:
             layout, scaling = "replicated", "strong"
         else:
             scaling = "strong"
-    T = T_cfg if (world == 1 or headline or layout == "replicated") else T_cfg // world
+    T = T_cfg if (world == 1 or headline or layout in ("replicated", "replicas")) else T_cfg // world
     t_gen = time.perf_counter()
-    experts = (rank * (cfgd["n_exp"] // world), cfgd["n_exp"] // world) if world > 1 else None
+    experts = (rank * (cfgd["n_exp"] // world), cfgd["n_exp"] // world) if world > 1 and layout != "replicas" else None
     layer, Xfull = synth.make_config(name, experts=experts)
-    if world > 1 and headline and rank:
+    if world > 1 and (headline or layout == "replicas") and rank:
         Xh = synth.make_tokens(layer, T, cfgd["seed"] + 1000 * rank, cfgd["zipf"])
     elif world > 1 and scaling == "strong" and layout == "a2a":
         Xh = np.ascontiguousarray(Xfull[rank * T:(rank + 1) * T])
@@ -355,14 +361,14 @@ def run_workload(name, args, ctx, headline):
         Xh = Xfull
     gen_s = time.perf_counter() - t_gen
     keep: list = []
-    desc = dm.layer_desc(layer, keep) if world == 1 else None
+    desc = dm.layer_desc(layer, keep) if (world == 1 or layout == "replicas") else None
     X = torch.from_numpy(Xh).to(dev)
     out = torch.empty((T, layer.hidden), device=dev, dtype=torch.float32)
     order = torch.empty((T, layer.n_used), device=dev, dtype=torch.int32)
     wtop = torch.empty((T, layer.n_used), device=dev, dtype=torch.float32)
     stream = ctx["stream"]
     ep = None
-    if world > 1:
+    if world > 1 and layout != "replicas":
         from dracomancer_llmengine_b200.ep import ExpertParallelMoE
         with torch.cuda.stream(stream):
             ep = ExpertParallelMoE(layer, T, exchange=args.exchange if layout == "a2a" else "fixed",
@@ -472,7 +478,7 @@ def run_workload(name, args, ctx, headline):
     if layer.hidden > 4096:
         sample = min(sample, 64)
     parity = parity_check(layer, Xh, out.cpu().numpy(), my_order.cpu().numpy(), my_wtop.cpu().numpy(),
-                          sample, world, rank, comm, experts)
+                          sample, world, rank, comm, experts, replicas=layout == "replicas")
 
     # ---- e2e: through the public API with pinned host buffers ----
     Xp, Op = ctx["pinned"](T, layer.hidden)
@@ -536,6 +542,8 @@ def run_workload(name, args, ctx, headline):
         par = f"expert parallel x{world}: {layer.n_exp // world} experts/GPU, " + (
             ("peer-memory exchange over NVLink" if args.exchange == "p2p" else f"NCCL all-to-all ({args.exchange})")
             if layout == "a2a" else "replicated tokens, NCCL all-reduce of partial outputs")
+        if layout == "replicas":
+            par = f"{world} replicas: every GPU runs the whole layer on its own tokens (no exchange)"
     config = {"workload": name, "hidden": cfgd["hidden"], "n_exp": cfgd["n_exp"], "top_k": cfgd["n_used"],
               "ffn": cfgd["inter"], "tokens_per_gpu": T, "tokens_per_step": tokens_step,
               "formats": "Q4_K gate/up, Q6_K down", "shared_ffn": cfgd["shared_inter"], "routing": cfgd["scoring"],
