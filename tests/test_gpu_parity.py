@@ -381,10 +381,10 @@ def test_tensor_core_moe_tok(dlib, port, gemm_path, code_gu, code_d, T):
     assert rel_l2(simt, ref) < 1e-5
 
 
-@pytest.mark.parametrize("n_exp,T", [(8, 300), (64, 300)])
+@pytest.mark.parametrize("n_exp,T", [(8, 300), (64, 300), (256, 300)])
 def test_tensor_core_hot_expert_many_tiles(dlib, port, gemm_path, n_exp, T):
     """One expert receives every token and one other half of them: several token tiles
-    (128-token tiles with 8 experts, 64-token tiles with 64: the tile height follows the
+    (128-token tiles with 8 experts, 64-token tiles with 64 and 256: the tile height follows the
     average load per expert)."""
     layer = synth.make_layer(hidden=1024, n_exp=n_exp, n_used=2, inter=512, seed=90)
     X = synth.make_tokens(layer, T, 90)
