@@ -70,15 +70,9 @@ __constant__ uint64_t kExp2Tab[32] = {
     0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
     0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
 
-__device__ __forceinline__ float host_expf(float x) {
-    const uint32_t ux = __float_as_uint(x);
-    const uint32_t abstop = (ux >> 20) & 0x7ff;
-    if (abstop >= 0x42b) {                          // |x| >= 88 (top 12 bits of 88.0f), inf, nan
-        if (ux == 0xff800000u) return 0.0f;         // -inf
-        if (abstop >= 0x7f8) return x + x;          // nan / +inf
-        if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);  // overflow
-        if (x < -0x1.9fe368p6f) return 0.0f;        // underflow
-    }
+// the table-driven part for |x| < 88: 2^(k/32) from `lookup(k & 31)` (the 64-bit table entry)
+template <typename Lookup>
+__device__ __forceinline__ float host_expf_core(float x, Lookup lookup) {
     const double kInvLn2N = 0x1.71547652b82fep+0 * 32.0;
     const double kShift = 0x1.8p+52;
     const double kC0 = 0x1.c6af84b912394p-5 / (32.0 * 32.0 * 32.0);
@@ -90,7 +84,7 @@ __device__ __forceinline__ float host_expf(float x) {
     const uint64_t ki = (uint64_t)__double_as_longlong(kd);
     kd = __dsub_rn(kd, kShift);
     const double r = __fma_rn(kInvLn2N, xd, -kd);
-    uint64_t t = kExp2Tab[ki & 31];
+    uint64_t t = lookup((int)(ki & 31));
     t += ki << 47;
     const double s = __longlong_as_double((long long)t);
     const double zz = __fma_rn(kC0, r, kC1);
@@ -99,6 +93,41 @@ __device__ __forceinline__ float host_expf(float x) {
     y = __fma_rn(zz, r2, y);
     y = __dmul_rn(y, s);
     return __double2float_rn(y);
+}
+// |x| >= 88, inf, nan: sets *res and returns true
+__device__ __forceinline__ bool host_expf_special(float x, float* res) {
+    const uint32_t ux = __float_as_uint(x);
+    const uint32_t abstop = (ux >> 20) & 0x7ff;
+    if (abstop < 0x42b) return false;               // |x| < 88 (top 12 bits of 88.0f)
+    if (ux == 0xff800000u) *res = 0.0f;             // -inf
+    else if (abstop >= 0x7f8) *res = x + x;         // nan / +inf
+    else if (x > 0x1.62e42ep6f) *res = __int_as_float(0x7f800000);   // overflow
+    else if (x < -0x1.9fe368p6f) *res = 0.0f;       // underflow
+    else return false;
+    return true;
+}
+
+__device__ __forceinline__ float host_expf(float x) {
+    float sp;
+    if (host_expf_special(x, &sp)) return sp;
+    return host_expf_core(x, [](int i) { return kExp2Tab[i]; });
+}
+
+// The same for a whole converged warp: lane i holds table entry i (tab_lo, tab_hi: its low and
+// high words, from exp_table_lane()), and each lane fetches its entry by shuffle instead of an
+// indexed constant-memory read, which serialises over the lanes' distinct indices.  Every lane
+// takes the shuffles; the special cases are selected afterwards.
+__device__ __forceinline__ void exp_table_lane(uint32_t& tab_lo, uint32_t& tab_hi) {
+    const uint64_t v = kExp2Tab[threadIdx.x & 31];
+    tab_lo = (uint32_t)v;
+    tab_hi = (uint32_t)(v >> 32);
+}
+__device__ __forceinline__ float host_expf_warp(float x, uint32_t tab_lo, uint32_t tab_hi) {
+    const float y = host_expf_core(x, [&](int i) {
+        return ((uint64_t)__shfl_sync(0xffffffffu, tab_hi, i) << 32) | __shfl_sync(0xffffffffu, tab_lo, i);
+    });
+    float sp;
+    return host_expf_special(x, &sp) ? sp : y;
 }
 
 // g / (1 + e^-g) * u in the reference's operation order (src/m6_layer.c:733-736)

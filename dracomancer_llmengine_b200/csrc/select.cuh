@@ -61,6 +61,8 @@ __device__ __forceinline__ void select_token(const RouterParams& p, const float*
     const int lane = threadIdx.x & 31;
     const int E = p.n_exp, K = p.n_used;
     float S[NS], P[NS];
+    uint32_t tab_lo, tab_hi;   // this lane's entry of the exp table (host_expf_warp)
+    exp_table_lane(tab_lo, tab_hi);
     if (p.scoring == 0) {
         // max-subtracted softmax (src/m6_layer.c:784-789)
         float mx = -1e30f;
@@ -78,7 +80,7 @@ __device__ __forceinline__ void select_token(const RouterParams& p, const float*
 #pragma unroll
         for (int j = 0; j < NS; j++) {
             const int e = lane + 32 * j;
-            P[j] = host_expf(__fsub_rn(S[j], mx));
+            P[j] = host_expf_warp(__fsub_rn(S[j], mx), tab_lo, tab_hi);
             if (e < E) V[e] = P[j];
         }
         __syncwarp();
@@ -104,7 +106,7 @@ __device__ __forceinline__ void select_token(const RouterParams& p, const float*
         for (int j = 0; j < NS; j++) {
             const int e = lane + 32 * j;
             const float l = e < E ? lg[e] : 0.f;
-            P[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, host_expf(-l)));
+            P[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, host_expf_warp(-l, tab_lo, tab_hi)));
             S[j] = __fadd_rn(P[j], p.probs_b && e < E ? p.probs_b[e] : 0.0f);
         }
         if (p.n_group > 1) {
