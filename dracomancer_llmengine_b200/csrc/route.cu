@@ -312,7 +312,7 @@ void launch_router_logits(const float* X, const float* W, int T, int E, int H, f
                           cudaStream_t s, int* zero_err) {
     const bool vec_ok = H % 4 == 0 && ((uintptr_t)X & 15) == 0 && ((uintptr_t)W & 15) == 0;
     if (vec_ok) {
-        if (router_tiles(T, E, 64, 64) >= 148) {   // enough 64 x 64 tiles for every SM: 16 chains a lane
+        if (router_tiles(T, E, 40, 64) >= 148) {   // enough 40..64 x 64 tiles for every SM: 10-16 chains a lane
             // token rows per warp (8 warps a block): the one that minimises the busiest SM's
             // work, (blocks on that SM) x (rows per warp); the full 8-row tiles of cfg4 (256 blocks
             // on 148 SMs) left 40 SMs with one block while the others ran two

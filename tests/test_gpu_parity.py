@@ -96,7 +96,7 @@ def logits_ref(X, W):
                                    (300, 128, 512), (600, 128, 2048), (2400, 256, 256), (2400, 256, 260),
                                    (40, 64, 258), (512, 128, 2048), (64, 384, 7168), (100, 128, 2048),
                                    (33, 90, 1028), (4744, 128, 256), (5928, 128, 260), (7112, 128, 256),
-                                   (4680, 128, 256)])
+                                   (4680, 128, 256), (2048, 256, 256), (1024, 384, 516)])
 def test_router_logits_exact_order(dlib, T, E, H):
     rng = np.random.default_rng(T + E + H)
     X = rng.standard_normal((T, H), dtype=np.float32)
