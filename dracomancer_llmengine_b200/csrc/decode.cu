@@ -850,7 +850,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
         // (a stage is only ever read by this warp's generic loads before the copy that rewrites
         // it, and those loads completed before the __syncwarp of release_pieces)
         auto issue = [&]() {
-            while (wok && p_ph < 2 && n_iss < n_con + NST) {
+            while (wok && p_ph < 2 && n_iss < n_con + a.ahead) {
                 const uint8_t* src;
                 uint32_t bytes;
                 if (p_ph == 0) {
@@ -1246,6 +1246,13 @@ int launch_fused_decode(FusedDecodeArgs a, int cg, int cu, int cd, cudaStream_t 
     a.n_slots = slots;
     a.stg_bytes = (int)stg;
     a.n_stg = n_stg;
+    // rows in flight per warp (DRACO_B200_FD_AHEAD, default all stages); at least 2: a gate/up
+    // task holds two
+    static const int ahead_env = [] {
+        const char* e = getenv("DRACO_B200_FD_AHEAD");
+        return e ? atoi(e) : 0;
+    }();
+    a.ahead = ahead_env >= 2 ? std::min(ahead_env, n_stg) : n_stg;
     a.kc = kc;
     a.xs_cap = xs_cap;
     void* args[] = {&a};

@@ -95,6 +95,7 @@ struct FusedDecodeArgs {
     unsigned long long* stamps; // optional [grid][8] %globaltimer at the phase boundaries (or null)
     int slot_bytes, n_slots;    // set by the launcher: router ring slots
     int stg_bytes, n_stg;       // per-warp weight-row ring: stage bytes, stages
+    int ahead;                  // weight rows a warp keeps in flight (<= n_stg)
     int kc, xs_cap;             // router k-chunk, staged-row floats
 };
 // 0 launched; 1 not applicable (the caller runs the separate kernels); -3 launch error

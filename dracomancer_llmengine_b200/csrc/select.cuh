@@ -51,10 +51,11 @@ __device__ __forceinline__ float pairwise_sum_warp(float v0, float v1, int n) {
 
 // One warp per token.  Lane l holds experts l + 32 j (j < NS) in registers with a bitmask of
 // those still selectable; each of the K rounds takes every lane's best candidate and a 5-step
-// shuffle argmax over (score, expert, prob).  The order of comparisons gives exactly the
-// reference's scan (src/m6_layer.c:860-870): the largest score wins, the lowest expert index
-// among equal scores, and only scores above the -1e30 floor count (NaN never does).  The softmax
-// denominator and the weight sum are taken sequentially in the reference's order.
+// shuffle max over a (score, expert) key, then fetches the winner's probability.  The order of
+// comparisons gives exactly the reference's scan (src/m6_layer.c:860-870): the largest score
+// wins, the lowest expert index among equal scores, and only scores above the -1e30 floor count
+// (NaN never does).  The softmax denominator and the weight sum are taken sequentially in the
+// reference's order.
 template <int NS>
 __device__ __forceinline__ void select_token(const RouterParams& p, const float* __restrict__ lg, int* order_row,
                                              float* wtop_row, int* err, float* V, float* gs) {
@@ -195,17 +196,20 @@ __device__ __forceinline__ void select_token(const RouterParams& p, const float*
                 bp = P[j];
                 bi = lane + 32 * j;
             }
+        // warp argmax as one 64-bit key max: the score in order-preserving bits above the
+        // complemented index, so a larger key is a larger score or, at an equal score, the lower
+        // index (the strict-greater scan's tie rule); no candidate (bi = -1) is key 0, below all.
+        // Scores here are above -1e30, never NaN and never -0, so equal keys are equal scores.
+        const uint32_t ub = __float_as_uint(bv);
+        const uint32_t ord = (ub & 0x80000000u) ? ~ub : (ub | 0x80000000u);
+        unsigned long long key = bi < 0 ? 0ull : ((unsigned long long)ord << 32) | (0xffffffffu - (uint32_t)bi);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
-            if (beats(ov, oi, bv, bi)) {
-                bv = ov;
-                bi = oi;
-                bp = op;
-            }
+            const unsigned long long ok = __shfl_xor_sync(0xffffffffu, key, o);
+            key = ok > key ? ok : key;
         }
+        bi = key ? (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu)) : -1;
+        bp = __shfl_sync(0xffffffffu, bp, bi >= 0 ? (bi & 31) : 0);   // the winner's probability
         if (bi < 0) {
             if (lane == 0) atomicOr(err, 2);
         } else if ((bi & 31) == lane) {
