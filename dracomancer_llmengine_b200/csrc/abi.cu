@@ -954,9 +954,10 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
                 for (int blk : {0, G / 2}) {
                     if (blk >= G) continue;
                     const unsigned long long* sb = st + (size_t)blk * 128;
-                    fprintf(stderr, "\n[block %d per warp: first piece / B done / C done us]", blk);
+                    fprintf(stderr, "\n[block %d per warp: issued / first piece / B done / C done us]", blk);
                     for (int w = 0; w < 16; w++)
-                        fprintf(stderr, " %d:%.1f/%.1f/%.1f", w, sb[8 + w] ? (sb[8 + w] - sb[0]) * 1e-3 : -1.0,
+                        fprintf(stderr, " %d:%.1f/%.1f/%.1f/%.1f", w, sb[68 + w] ? (sb[68 + w] - sb[0]) * 1e-3 : -1.0,
+                                sb[8 + w] ? (sb[8 + w] - sb[0]) * 1e-3 : -1.0,
                                 sb[24 + w] ? (sb[24 + w] - sb[0]) * 1e-3 : -1.0,
                                 sb[40 + w] ? (sb[40 + w] - sb[0]) * 1e-3 : -1.0);
                     fprintf(stderr, "\n[block %d warps 0/15: B wait/compute, C wait/compute us] %.1f/%.1f %.1f/%.1f | %.1f/%.1f %.1f/%.1f",

@@ -520,6 +520,32 @@ __device__ __forceinline__ void rows_dot_smem(const uint8_t* const (&rows)[R], i
     }
 }
 
+// 16-byte asynchronous global -> shared copies of one thread (the load/store unit path, not the
+// tensor-memory-access unit: every lane issues its own share of a row), grouped per piece
+__device__ __forceinline__ void fd_cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void fd_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void fd_cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// wait until at most n of this thread's newest copy groups are still in flight
+__device__ __forceinline__ void fd_cp_wait_n(int n) {
+    switch (n) {
+        case 7: fd_cp_wait<7>(); break;
+        case 6: fd_cp_wait<6>(); break;
+        case 5: fd_cp_wait<5>(); break;
+        case 4: fd_cp_wait<4>(); break;
+        case 3: fd_cp_wait<3>(); break;
+        case 2: fd_cp_wait<2>(); break;
+        case 1: fd_cp_wait<1>(); break;
+        default: fd_cp_wait<0>(); break;
+    }
+}
+
 // ------------------------------------------------------------------------------------------
 // Fused decode layer: the whole MoE layer of a small token batch (T <= 8, T*K <= 64) in ONE
 // cooperative launch of one block per SM:
@@ -535,10 +561,11 @@ __device__ __forceinline__ void rows_dot_smem(const uint8_t* const (&rows)[R], i
 //   -- grid barrier 2 --
 //   phase C  warp tasks: one output row over every active expert (and the shared expert),
 //            then the k-ascending fused combine (+ shared expert) of that row.
-// Each compute warp streams the weight rows of its own tasks through a private ring of bulk
-// copies, phase C's rows included as soon as there is room (they do not depend on the
-// activations), so the weights of the whole layer are in flight while phase B computes.  Per
-// row the arithmetic and its order are those of the separate dec_* kernels.
+// Each compute warp streams the weight rows of its own tasks through a private ring of
+// asynchronous copies (cp.async, every lane its share), phase C's rows included as soon as there
+// is room (they do not depend on the activations), so the weights of the whole layer are in
+// flight while phase B computes.  Per row the arithmetic and its order are those of the
+// separate dec_* kernels.
 // Every wait is bounded: an mbarrier wait gives up after 2 s, a grid barrier after 1 s; a block
 // that gives up raises a status bit (0x200 copy, 0x1000 grid barrier, 0x2000 a weight row that is
 // not a whole aligned row), stops, and waits for its own copies in flight before it exits.
@@ -593,7 +620,6 @@ template <int CG, int CU, int CD, int NS>
 __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArgs a) {
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ uint64_t full[kFdMaxSlots], empty[kFdMaxSlots];
-    __shared__ uint64_t s_wfull[kFdCompute][kFdMaxStg];
     // s_cabort: written by compute threads (and thread 0 at the grid barriers) and read by them
     // only after a barrier, so their decisions stay uniform; s_pabort: the producer's own
     __shared__ volatile int s_cabort, s_pabort;
@@ -624,8 +650,6 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             sync::mbar_init(&full[i], 1);
             sync::mbar_init(&empty[i], 1);
         }
-        for (int w = 0; w < kFdCompute; w++)
-            for (int i = 0; i < a.n_stg; i++) sync::mbar_init(&s_wfull[w][i], 1);
         sync::fence_init();
         s_cabort = 0;
         s_pabort = 0;
@@ -822,10 +846,12 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
     // Warp tasks: phase B = one (expert or shared expert, intermediate row) pair of gate and up
     // rows, phase C = one output row over every active expert (and the shared expert), combined
     // in k order right away.  Each compute warp streams the weight rows of its own tasks, in task
-    // order, through a private ring of n_stg stages by bulk copies (lane 0 issues, one mbarrier per
-    // stage); phase C's rows do not depend on the activations, so they are issued as soon as
-    // phase B's leave room, before grid barrier 2.  The ring aliases the router's slots (all of
-    // them consumed before barrier 1).
+    // order, through a private ring of n_stg stages: every lane copies its 16-byte share of a row
+    // with cp.async, one copy group per row (a single thread issuing bulk copies per row is held to
+    // the copy engine's per-copy rate, ~70 cycles a copy per SM, a ceiling for rows of ~1 KB);
+    // phase C's rows do not depend on the activations, so they are issued as soon as phase B's
+    // leave room, before grid barrier 2.  The ring aliases the router's slots (all of them
+    // consumed before barrier 1).
     const int nb = H / 256, nbd = F / 256, nbds = sh ? a.sh_ff / 256 : 0;
     const int bg = superblock_bytes(CG, a.q6s), bd = superblock_bytes(CD, a.q6s);
     const uint32_t rbg = (uint32_t)nb * bg, rbd = (uint32_t)nbd * bd, rbds = (uint32_t)nbds * bd;
@@ -836,7 +862,6 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
     const int per_c = n_act + (sh ? 1 : 0);   // pieces of a phase C task
     if (!producer) {
         uint8_t* wring = ring + (size_t)warp * NST * a.stg_bytes;
-        uint64_t* wfull = s_wfull[warp];
         // producer cursor (uniform over the warp; lane 0 issues): the next piece's phase, task, part
         // (phase C has no pieces when no expert is active and there is no shared expert: every
         // routing entry of the batch named no expert of the table)
@@ -886,10 +911,9 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                     break;
                 }
                 const int st = n_iss % NST;
-                if (lane == 0) {
-                    sync::mbar_expect_tx(&wfull[st], bytes);
-                    sync::bulk_load(wring + (size_t)st * a.stg_bytes, src, bytes, &wfull[st]);
-                }
+                uint8_t* dst = wring + (size_t)st * a.stg_bytes;
+                for (uint32_t off = 16u * lane; off < bytes; off += 512u) fd_cp16(dst + off, src + off);
+                fd_cp_commit();   // one group per piece on every lane
                 n_iss++;
             }
         };
@@ -899,10 +923,8 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
         auto take_piece = [&]() -> const uint8_t* {
             const unsigned long long tw0 = a.stamps ? sync::global_ns() : 0;
             const int st = n_con % NST;
-            if (!sync::mbar_wait(&wfull[st], (n_con / NST) & 1)) {
-                if (lane == 0) atomicOr(a.status, 0x200);
-                wok = false;
-            }
+            fd_cp_wait_n((int)(n_iss - n_con) - 1);   // this piece's group has landed (own copies)
+            __syncwarp();                             // and the other lanes' shares are visible
             wok = __all_sync(0xffffffffu, wok);
             if (a.stamps) t_acc[2 * t_ph] += sync::global_ns() - tw0;
             if (a.stamps && lane == 0 && n_con == 0) a.stamps[(size_t)blockIdx.x * kFdStampStride + 8 + warp] = sync::global_ns();
@@ -914,6 +936,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
             issue();
         };
         issue();
+        if (a.stamps && lane == 0) a.stamps[(size_t)blockIdx.x * kFdStampStride + 68 + warp] = sync::global_ns();
         const bool x_in_smem = (size_t)T * H <= (size_t)a.xs_cap;   // staged at the start
         const float* xbase = x_in_smem ? xs : a.X;
         for (int task = gw; wok && task < tasks_b; task += GW) {
@@ -1073,8 +1096,7 @@ __global__ void __launch_bounds__(kFdThreads) fused_decode_kernel(FusedDecodeArg
                 for (int i = 0; i < 4; i++) a.stamps[(size_t)blockIdx.x * kFdStampStride + 56 + (warp ? 4 : 0) + i] = t_acc[i];
         }
         // copies issued but not consumed (after a failure) land before the warp exits
-        if (lane == 0)
-            for (uint32_t r = n_con; r < n_iss; r++) sync::mbar_wait(&wfull[r % NST], (r / NST) & 1);
+        fd_cp_wait<0>();
         __syncwarp();
         fd_stamp(a, 6);
     }
