@@ -145,7 +145,12 @@ class ClockSampler:
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.proc = None
-        time.sleep(0.3)
+        # nvidia-smi takes a while to start (driver library initialisation): the timed region
+        # starts only after its first sample is written
+        t0 = time.perf_counter()
+        while self.proc and time.perf_counter() - t0 < 10.0 and os.path.getsize(self.path) == 0:
+            time.sleep(0.02)
+        time.sleep(0.25)
         return self
 
     def __exit__(self, *exc):
@@ -433,10 +438,12 @@ def run_workload(name, args, ctx, headline):
     steps = args.steps
     launches0 = L.draco_b200_launch_count()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk, torch.cuda.stream(stream):
+        # the ranks meet after their samplers have started (which takes each a different time),
+        # so no rank's first step waits in the exchange for a late one
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
         for i in range(steps):
             if flush is not None:
                 flush_l2()

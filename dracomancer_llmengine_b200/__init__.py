@@ -92,6 +92,8 @@ _SIGS = {
     "draco_b200_route": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, _vp], ct.c_int),
     "draco_b200_experts_forward": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, ct.c_int, ct.c_int, _vp,
                                     ct.c_int, ct.c_int, _vp], ct.c_int),
+    "draco_b200_experts_forward_to_ranks": ([ct.POINTER(DracoMoeLayer), _vp, ct.c_int, _vp, _vp, ct.c_int, ct.c_int,
+                                             _vp, ct.c_int, ct.c_int, _vp], ct.c_int),
     "draco_b200_ep_plan": ([_vp, ct.c_int, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _vp, _vp, _vp, _vp], ct.c_int),
     "draco_b200_ep_pack": ([_vp, _vp, _vp, _vp, ct.c_int, _vp, ct.c_int, ct.c_int, ct.c_int, ct.c_int, _vp, _vp,
                             _vp], ct.c_int),

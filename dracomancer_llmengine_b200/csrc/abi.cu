@@ -710,6 +710,8 @@ struct LayerArgs {
     const float* d_gi = nullptr; // router weights (device), null when routing is given
     bool no_routed = false;      // shared expert only
     bool x_half = false;         // b.x holds fp16 rows
+    float* const* out_blk = nullptr;   // output row blocks (device array of pointers), or null
+    int out_block = 0;                 // rows per block
 };
 
 // routing supplied by the caller: rows of ld entries, expert ids minus e_base index the layer's
@@ -720,6 +722,8 @@ struct GivenRoute {
     int ld = 0;
     int e_base = 0;
     bool x_half = false;   // X holds fp16 rows (device memory)
+    float* const* out_blk = nullptr;   // row q of the result goes to out_blk[q / out_block] + (q % out_block) * n_out
+    int out_block = 0;
 };
 
 struct LayerBufs {
@@ -882,7 +886,8 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
     const bool sh_ok = !a.sh || (a.sh->aligned16 && a.sh->cg == a.tab->cg && a.sh->cu == a.tab->cu &&
                                  a.sh->cd == a.tab->cd && a.sh->q6s == a.tab->q6s &&
                                  dec_supported(a.sh->cg, a.sh->cu, a.sh->cd, a.sh_ff, a.n_in, a.n_out, a.sh->q6s));
-    if (!a.no_routed && !xh && !b.use_tc && g_act_mode == 0 && fused_decode_enabled() && T <= 8 && T * a.K <= 64 &&
+    if (!a.no_routed && !xh && !b.use_tc && !a.out_blk && g_act_mode == 0 && fused_decode_enabled() && T <= 8 &&
+        T * a.K <= 64 &&
         a.tab->aligned16 && a.tab->cg == a.tab->cu && sh_ok &&
         dec_supported(a.tab->cg, a.tab->cu, a.tab->cd, a.inter, a.n_in, a.n_out, a.tab->q6s)) {
         FusedDecodeArgs f{};
@@ -1114,10 +1119,10 @@ int run_layer(Ctx* c, const LayerArgs& a, int T, LayerBufs& b, cudaStream_t s) {
         PhaseScope ps(kCombine, s);
         if (b.use_tc && !a.no_routed)
             launch_combine_half(reinterpret_cast<const __half*>(b.y), rb.order, rb.wtop, rb.pos_of, T, a.K, a.E,
-                                a.n_out, a.sh ? b.y_sh : nullptr, b.out, s);
+                                a.n_out, a.sh ? b.y_sh : nullptr, b.out, s, a.out_blk, a.out_block);
         else
             launch_combine(b.y, rb.order, rb.wtop, rb.pos_of, T, a.no_routed ? 0 : a.K, a.E, a.n_out,
-                           a.sh ? b.y_sh : nullptr, b.out, s);
+                           a.sh ? b.y_sh : nullptr, b.out, s, a.out_blk, a.out_block);
         g_launches += 1;
     }
     CK(cudaGetLastError());
@@ -1273,6 +1278,10 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
     a.rp.w_scale = w_scale;
     a.no_routed = gr && !gr->order;
     a.x_half = gr && gr->x_half;
+    if (gr && gr->out_blk) {
+        a.out_blk = gr->out_blk;
+        a.out_block = gr->out_block;
+    }
     if (a.no_routed && !a.sh) {
         set_err("no routed experts and no shared expert: nothing to compute");
         return -1;
@@ -1341,7 +1350,7 @@ int layer_call(const float* x, int T, const uint64_t* ptrs, const int* codes, co
             (uint64_t)a.rp.n_group_used, (uint64_t)a.rp.norm_w, (uint64_t)__float_as_uint_host(a.rp.w_scale),
             (uint64_t)gemm_path(), (uint64_t)g_act_mode, (uint64_t)b.use_tc, (uint64_t)(gr != nullptr),
             (uintptr_t)(gr ? gr->order : nullptr), (uintptr_t)(gr ? gr->wtop : nullptr), (uint64_t)(gr ? gr->ld : 0),
-            (uint64_t)(gr ? gr->e_base : 0), (uint64_t)a.x_half};
+            (uint64_t)(gr ? gr->e_base : 0), (uint64_t)a.x_half, (uintptr_t)a.out_blk, (uint64_t)a.out_block};
         const int rc = captured ? body() : graph_call(c, key, s, body);
         if (!captured) ws_release(c, s);
         return rc;
@@ -1942,6 +1951,33 @@ int draco_b200_experts_forward(const DracoMoeLayer* L, const void* X, int T, con
                       L->scoring, L->n_exp, L->n_used, L->n_group, L->n_group_used, L->norm_w, L->w_scale, L->inter,
                       L->n_in, L->n_out, has_sh ? sh3 : nullptr, shc3, has_sh ? L->sh_ff : 0, out, nullptr, nullptr,
                       (cudaStream_t)stream, &gr);
+}
+
+int draco_b200_experts_forward_to_ranks(const DracoMoeLayer* L, const void* X, int T, const int* order,
+                                        const float* wtop, int ld, int first_expert, float* const* out_blocks,
+                                        int block, int x_fp16, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!order || !wtop || !out_blocks || !X || ld < L->n_used || first_expert < 0 || block < 1 || L->n_out % 4 ||
+        L->n_used > 64) {
+        set_err("draco_b200_experts_forward_to_ranks: need order, wtop, out_blocks, ld >= n_used, first_expert >= 0, "
+                "block >= 1, n_out %% 4 == 0, n_used <= 64");
+        return -1;
+    }
+    if (!dev_kind(X) || !dev_kind(order) || !dev_kind(wtop) || !dev_kind(out_blocks)) {
+        set_err("draco_b200_experts_forward_to_ranks: device pointers only");
+        return -1;
+    }
+    GivenRoute gr;
+    gr.order = order;
+    gr.wtop = wtop;
+    gr.ld = ld;
+    gr.e_base = first_expert;
+    gr.x_half = x_fp16 != 0;
+    gr.out_blk = out_blocks;
+    gr.out_block = block;
+    return layer_call(static_cast<const float*>(X), T, L->exp_ptrs, L->exp_codes, L->gate_inp, L->probs_b,
+                      L->scoring, L->n_exp, L->n_used, L->n_group, L->n_group_used, L->norm_w, L->w_scale, L->inter,
+                      L->n_in, L->n_out, nullptr, nullptr, 0, nullptr, nullptr, nullptr, (cudaStream_t)stream, &gr);
 }
 
 int draco_b200_route(const DracoMoeLayer* L, const float* X, int T, int* order, float* wtop, void* stream) {

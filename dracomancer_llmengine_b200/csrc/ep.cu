@@ -41,28 +41,30 @@ __device__ __forceinline__ unsigned token_mask(const int* order, int t, int K, i
 // One block.  Thread i owns tokens [i*chunk, (i+1)*chunk); rows are rank-major and, within a
 // rank, in token order.  counts[r] = rows for rank r; row_of[t*G + r] = row or -1;
 // src_tok[row] = t.  block == 0: rank r's rows follow rank r-1's (compact); block > 0: rank r's
-// rows start at r*block (fixed-size blocks, block >= T).
+// rows start at r*block (fixed-size blocks, block >= T).  MAXG >= G bounds the per-thread rank
+// counters (registers).
+template <int MAXG>
 __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int* __restrict__ order, int T, int K, int E,
                                                                int G, int block, int* __restrict__ counts,
                                                                int* __restrict__ row_of, int* __restrict__ src_tok) {
-    __shared__ int warp_tot[kEpMaxRanks][kPlanThreads / 32];
-    __shared__ int rank_base[kEpMaxRanks + 1];
+    __shared__ int warp_tot[MAXG][kPlanThreads / 32];
+    __shared__ int rank_base[MAXG + 1];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int e_loc = E / G;
     const int chunk = (T + kPlanThreads - 1) / kPlanThreads;
     const int t0 = min(T, tid * chunk), t1 = min(T, t0 + chunk);
-    int c[kEpMaxRanks];
+    int c[MAXG];
 #pragma unroll
-    for (int r = 0; r < kEpMaxRanks; r++) c[r] = 0;
+    for (int r = 0; r < MAXG; r++) c[r] = 0;
     for (int t = t0; t < t1; t++) {
         const unsigned m = token_mask(order, t, K, E, e_loc);
 #pragma unroll
-        for (int r = 0; r < kEpMaxRanks; r++) c[r] += (m >> r) & 1u;
+        for (int r = 0; r < MAXG; r++) c[r] += (m >> r) & 1u;
     }
     // exclusive prefix over threads, per rank
-    int ex[kEpMaxRanks];
+    int ex[MAXG];
 #pragma unroll
-    for (int r = 0; r < kEpMaxRanks; r++) {
+    for (int r = 0; r < MAXG; r++) {
         const int inc = warp_incl(c[r]);
         ex[r] = inc - c[r];
         if (lane == 31) warp_tot[r][warp] = inc;
@@ -86,13 +88,13 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int* __rest
         }
     }
     __syncthreads();
-    int pos[kEpMaxRanks];
+    int pos[MAXG];
 #pragma unroll
-    for (int r = 0; r < kEpMaxRanks; r++) pos[r] = r < G ? rank_base[r] + warp_tot[r][warp] + ex[r] : 0;
+    for (int r = 0; r < MAXG; r++) pos[r] = r < G ? rank_base[r] + warp_tot[r][warp] + ex[r] : 0;
     for (int t = t0; t < t1; t++) {
         const unsigned m = token_mask(order, t, K, E, e_loc);
 #pragma unroll
-        for (int r = 0; r < kEpMaxRanks; r++) {
+        for (int r = 0; r < MAXG; r++) {
             if (r >= G) break;
             int row = -1;
             if ((m >> r) & 1u) {
@@ -139,29 +141,38 @@ __global__ void ep_pack_kernel(const float* __restrict__ X, const int* __restric
     }
 }
 
-// out[t] = (sum over ranks r ascending of back[row_of[t][r]]) + shared[t]
+// Home-side combine: out[t] = sum over r ascending of back[row_of[t][r]] (+ shared[t]), one
+// thread per 4 outputs, all of a thread's (at most MAXG) loads issued before the first add.
+template <int MAXG>
 __global__ void ep_combine_kernel(const float* __restrict__ back, const int* __restrict__ row_of, int T, int G,
                                   int H, const float* __restrict__ shared, float* __restrict__ out) {
     const int H4 = H / 4;
     const size_t n = (size_t)T * H4;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int t = (int)(i / H4), c = (int)(i % H4);
+        float4 v[MAXG];
+        bool has[MAXG];
+#pragma unroll
+        for (int r = 0; r < MAXG; r++) {
+            const int row = r < G ? __ldg(row_of + (size_t)t * G + r) : -1;
+            has[r] = row >= 0;
+            if (has[r]) v[r] = reinterpret_cast<const float4*>(back + (size_t)row * H)[c];
+        }
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 0; r < G; r++) {
-            const int row = row_of[(size_t)t * G + r];
-            if (row < 0) continue;
-            const float4 v = reinterpret_cast<const float4*>(back + (size_t)row * H)[c];
-            acc.x = __fadd_rn(acc.x, v.x);
-            acc.y = __fadd_rn(acc.y, v.y);
-            acc.z = __fadd_rn(acc.z, v.z);
-            acc.w = __fadd_rn(acc.w, v.w);
+#pragma unroll
+        for (int r = 0; r < MAXG; r++) {
+            if (!has[r]) continue;
+            acc.x = __fadd_rn(acc.x, v[r].x);
+            acc.y = __fadd_rn(acc.y, v[r].y);
+            acc.z = __fadd_rn(acc.z, v[r].z);
+            acc.w = __fadd_rn(acc.w, v[r].w);
         }
         if (shared) {
-            const float4 v = reinterpret_cast<const float4*>(shared + (size_t)t * H)[c];
-            acc.x = __fadd_rn(acc.x, v.x);
-            acc.y = __fadd_rn(acc.y, v.y);
-            acc.z = __fadd_rn(acc.z, v.z);
-            acc.w = __fadd_rn(acc.w, v.w);
+            const float4 u = __ldg(reinterpret_cast<const float4*>(shared + (size_t)t * H) + c);
+            acc.x = __fadd_rn(acc.x, u.x);
+            acc.y = __fadd_rn(acc.y, u.y);
+            acc.z = __fadd_rn(acc.z, u.z);
+            acc.w = __fadd_rn(acc.w, u.w);
         }
         reinterpret_cast<float4*>(out + (size_t)t * H)[c] = acc;
     }
@@ -275,7 +286,9 @@ __global__ void ep_barrier_kernel(unsigned* const* peer_flags, unsigned* my_flag
 }
 
 // Combine by loads from the owners' partial buffers: out[t] = sum over r ascending of
-// partial_r[rank*block + j_r(t)] (+ shared[t]), j_r(t) = row_of[t][r] - r*block.
+// partial_r[rank*block + j_r(t)] (+ shared[t]), j_r(t) = row_of[t][r] - r*block.  One thread per
+// 4 outputs; all of a thread's (at most MAXG) loads are issued before the first add.
+template <int MAXG>
 __global__ void ep_pull_combine_kernel(const float* const* src_partial, const int* __restrict__ row_of, int T,
                                        int G, int rank, int block, int H, const float* __restrict__ shared,
                                        float* __restrict__ out) {
@@ -283,23 +296,32 @@ __global__ void ep_pull_combine_kernel(const float* const* src_partial, const in
     const size_t n = (size_t)T * H4;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int t = (int)(i / H4), c = (int)(i % H4);
+        float4 v[MAXG];
+        bool has[MAXG];
+#pragma unroll
+        for (int r = 0; r < MAXG; r++) {
+            const int row = r < G ? __ldg(row_of + (size_t)t * G + r) : -1;
+            has[r] = row >= 0;
+            if (has[r]) {
+                const size_t srow = (size_t)rank * block + (row - r * block);
+                v[r] = reinterpret_cast<const float4*>(src_partial[r] + srow * H)[c];
+            }
+        }
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 0; r < G; r++) {
-            const int row = row_of[(size_t)t * G + r];
-            if (row < 0) continue;
-            const size_t srow = (size_t)rank * block + (row - r * block);
-            const float4 v = reinterpret_cast<const float4*>(src_partial[r] + srow * H)[c];
-            acc.x = __fadd_rn(acc.x, v.x);
-            acc.y = __fadd_rn(acc.y, v.y);
-            acc.z = __fadd_rn(acc.z, v.z);
-            acc.w = __fadd_rn(acc.w, v.w);
+#pragma unroll
+        for (int r = 0; r < MAXG; r++) {
+            if (!has[r]) continue;
+            acc.x = __fadd_rn(acc.x, v[r].x);
+            acc.y = __fadd_rn(acc.y, v[r].y);
+            acc.z = __fadd_rn(acc.z, v[r].z);
+            acc.w = __fadd_rn(acc.w, v[r].w);
         }
         if (shared) {
-            const float4 v = reinterpret_cast<const float4*>(shared + (size_t)t * H)[c];
-            acc.x = __fadd_rn(acc.x, v.x);
-            acc.y = __fadd_rn(acc.y, v.y);
-            acc.z = __fadd_rn(acc.z, v.z);
-            acc.w = __fadd_rn(acc.w, v.w);
+            const float4 u = __ldg(reinterpret_cast<const float4*>(shared + (size_t)t * H) + c);
+            acc.x = __fadd_rn(acc.x, u.x);
+            acc.y = __fadd_rn(acc.y, u.y);
+            acc.z = __fadd_rn(acc.z, u.z);
+            acc.w = __fadd_rn(acc.w, u.w);
         }
         reinterpret_cast<float4*>(out + (size_t)t * H)[c] = acc;
     }
@@ -325,12 +347,27 @@ void launch_ep_pull_combine(const float* const* src_partial, const int* row_of, 
                             int H, const float* shared, float* out, cudaStream_t s) {
     const size_t n = (size_t)T * (H / 4);
     const int blocks = (int)std::max<size_t>(1, std::min<size_t>(148 * 8, (n + 255) / 256));
-    ep_pull_combine_kernel<<<blocks, 256, 0, s>>>(src_partial, row_of, T, G, rank, block, H, shared, out);
+    if (G <= 2)
+        ep_pull_combine_kernel<2><<<blocks, 256, 0, s>>>(src_partial, row_of, T, G, rank, block, H, shared, out);
+    else if (G <= 4)
+        ep_pull_combine_kernel<4><<<blocks, 256, 0, s>>>(src_partial, row_of, T, G, rank, block, H, shared, out);
+    else if (G <= 8)
+        ep_pull_combine_kernel<8><<<blocks, 256, 0, s>>>(src_partial, row_of, T, G, rank, block, H, shared, out);
+    else
+        ep_pull_combine_kernel<kEpMaxRanks><<<blocks, 256, 0, s>>>(src_partial, row_of, T, G, rank, block, H, shared,
+                                                                  out);
 }
 
 void launch_ep_plan(const int* order, int T, int K, int E, int G, int block, int* counts, int* row_of,
                     int* src_tok, cudaStream_t s) {
-    ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(order, T, K, E, G, block, counts, row_of, src_tok);
+    if (G <= 2)
+        ep_plan_kernel<2><<<1, kPlanThreads, 0, s>>>(order, T, K, E, G, block, counts, row_of, src_tok);
+    else if (G <= 4)
+        ep_plan_kernel<4><<<1, kPlanThreads, 0, s>>>(order, T, K, E, G, block, counts, row_of, src_tok);
+    else if (G <= 8)
+        ep_plan_kernel<8><<<1, kPlanThreads, 0, s>>>(order, T, K, E, G, block, counts, row_of, src_tok);
+    else
+        ep_plan_kernel<kEpMaxRanks><<<1, kPlanThreads, 0, s>>>(order, T, K, E, G, block, counts, row_of, src_tok);
 }
 
 void launch_ep_pack(const float* X, const int* order, const float* wtop, const int* counts, int G, const int* src_tok,
@@ -343,7 +380,14 @@ void launch_ep_combine(const float* back, const int* row_of, int T, int G, int H
                        cudaStream_t s) {
     const size_t n = (size_t)T * (H / 4);
     const int blocks = (int)std::max<size_t>(1, std::min<size_t>(148 * 8, (n + 255) / 256));
-    ep_combine_kernel<<<blocks, 256, 0, s>>>(back, row_of, T, G, H, shared, out);
+    if (G <= 2)
+        ep_combine_kernel<2><<<blocks, 256, 0, s>>>(back, row_of, T, G, H, shared, out);
+    else if (G <= 4)
+        ep_combine_kernel<4><<<blocks, 256, 0, s>>>(back, row_of, T, G, H, shared, out);
+    else if (G <= 8)
+        ep_combine_kernel<8><<<blocks, 256, 0, s>>>(back, row_of, T, G, H, shared, out);
+    else
+        ep_combine_kernel<kEpMaxRanks><<<blocks, 256, 0, s>>>(back, row_of, T, G, H, shared, out);
 }
 
 void launch_route_in(const int* order, const float* wtop, int ld, int e_base, int T, int K, int* o_order,

@@ -445,6 +445,10 @@ __global__ void combine_kernel(const Y* __restrict__ y, const int* __restrict__ 
 // The same sums for n_out % 4 == 0, one block per token row: warp 0 stages the row's valid
 // (weight, y row) pairs in k order in shared memory, then every thread runs the identical fma
 // chain over float4 columns with the y loads of four assignments issued ahead of their fmas.
+// out_blk != nullptr: row t goes to out_blk[t / blk] + (t % blk) * n_out instead (the row blocks
+// of other GPUs' buffers, peer stores), a row without a valid assignment is not written, and
+// every thread fences its stores at system scope before it ends, so a flag barrier that follows
+// publishes them.
 constexpr int kCombineMaxK = 64;
 constexpr int kCombineThreads = 128;
 __device__ __forceinline__ void fma4(float4& a, float w, const float4& v) {
@@ -457,7 +461,7 @@ template <typename Y>
 __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(
     const Y* __restrict__ y, const int* __restrict__ order, const float* __restrict__ wtop,
     const int* __restrict__ pos_of, int K, int E, int n_out, int cpb, const float* __restrict__ shared,
-    float* __restrict__ out) {
+    float* __restrict__ out, float* const* __restrict__ out_blk, int blk) {
     __shared__ float sw[kCombineMaxK];
     __shared__ const Y* sy[kCombineMaxK];
     __shared__ int sn;
@@ -492,8 +496,10 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(
     }
     __syncthreads();
     const int n = sn;
+    if (out_blk && n == 0) return;   // a padding row: nothing of this slice to send
     const float4* sh = shared ? reinterpret_cast<const float4*>(shared + (size_t)t * n_out) : nullptr;
-    float4* o = reinterpret_cast<float4*>(out + (size_t)t * n_out);
+    float4* o = reinterpret_cast<float4*>(out_blk ? out_blk[t / blk] + (size_t)(t % blk) * n_out
+                                                  : out + (size_t)t * n_out);
     for (int c = c0 + threadIdx.x; c < c1; c += kCombineThreads) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         int j = 0;
@@ -515,6 +521,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_rows_kernel(
         }
         o[c] = acc;
     }
+    if (out_blk) __threadfence_system();
 }
 
 __global__ void half_to_float_kernel(const __half* __restrict__ x, float* __restrict__ y, size_t n) {
@@ -534,17 +541,19 @@ void launch_set_pair(int* d, int a, int b, cudaStream_t s) { set_pair_kernel<<<1
 
 template <typename Y>
 static void combine_typed(const Y* y, const int* order, const float* wtop, const int* pos_of, int T, int K, int E,
-                          int n_out, const float* shared, float* out, cudaStream_t s) {
+                          int n_out, const float* shared, float* out, float* const* out_blk, int blk,
+                          cudaStream_t s) {
     const bool vec = n_out % 4 == 0 && K <= kCombineMaxK && !((uintptr_t)y & 15) && !((uintptr_t)out & 15) &&
                      !((uintptr_t)shared & 15);
-    if (vec) {
+    if (vec || out_blk) {   // row blocks: the caller checked n_out % 4 == 0, K <= kCombineMaxK
         // few rows: each row split over blocks of one float4 column a thread, so small batches
         // still spread over the SMs
         const int n4 = n_out / 4;
         const int cpb = T >= 148 ? n4 : kCombineThreads;
         dim3 grid(T, (n4 + cpb - 1) / cpb);
         if (T > 0)
-            combine_rows_kernel<<<grid, kCombineThreads, 0, s>>>(y, order, wtop, pos_of, K, E, n_out, cpb, shared, out);
+            combine_rows_kernel<<<grid, kCombineThreads, 0, s>>>(y, order, wtop, pos_of, K, E, n_out, cpb, shared, out,
+                                                                 out_blk, blk);
         return;
     }
     dim3 grid((n_out + 255) / 256, T);
@@ -552,12 +561,12 @@ static void combine_typed(const Y* y, const int* order, const float* wtop, const
 }
 
 void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T, int K, int E,
-                    int n_out, const float* shared, float* out, cudaStream_t s) {
-    combine_typed(y, order, wtop, pos_of, T, K, E, n_out, shared, out, s);
+                    int n_out, const float* shared, float* out, cudaStream_t s, float* const* out_blk, int blk) {
+    combine_typed(y, order, wtop, pos_of, T, K, E, n_out, shared, out, out_blk, blk, s);
 }
 void launch_combine_half(const __half* y, const int* order, const float* wtop, const int* pos_of, int T, int K, int E,
-                         int n_out, const float* shared, float* out, cudaStream_t s) {
-    combine_typed(y, order, wtop, pos_of, T, K, E, n_out, shared, out, s);
+                         int n_out, const float* shared, float* out, cudaStream_t s, float* const* out_blk, int blk) {
+    combine_typed(y, order, wtop, pos_of, T, K, E, n_out, shared, out, out_blk, blk, s);
 }
 
 // ------------------------------------------------------------------------------------------

@@ -132,13 +132,17 @@ void launch_down_code(const ExpertTable& tab, int cd, const int* active, const i
                       int n_active_max, const int* off, const float* act, int inter, int n_out, float* y,
                       cudaStream_t s, int q6s);
 // out[t][r] = sum_k w[t,k] * y[pos_of[t*K+k]][r] (k ascending, fused multiply-add),
-// then + shared[t][r] when shared != nullptr
+// then + shared[t][r] when shared != nullptr.  out_blk != nullptr (n_out % 4 == 0, K <= 64):
+// row t goes to out_blk[t / blk] + (t % blk) * n_out, rows without a valid assignment are not
+// written, and the stores are fenced at system scope (peer buffers)
 void launch_combine(const float* y, const int* order, const float* wtop, const int* pos_of, int T,
-                    int K, int E, int n_out, const float* shared, float* out, cudaStream_t s);
+                    int K, int E, int n_out, const float* shared, float* out, cudaStream_t s,
+                    float* const* out_blk = nullptr, int blk = 0);
 void launch_half_to_float(const __half* x, float* y, size_t n, cudaStream_t s);
 // the same with fp16 expert output rows (the tensor-core path)
 void launch_combine_half(const __half* y, const int* order, const float* wtop, const int* pos_of, int T,
-                         int K, int E, int n_out, const float* shared, float* out, cudaStream_t s);
+                         int K, int E, int n_out, const float* shared, float* out, cudaStream_t s,
+                         float* const* out_blk = nullptr, int blk = 0);
 // rows y[r] = dot(W row r, x) for r in [o0, o1), any supported code, one vector
 void launch_gemv_rows(int code, const uint8_t* W, const float* x, int n_in, int o0, int o1, float* y,
                       cudaStream_t s, int q6s);

@@ -16,8 +16,10 @@ Two layouts:
   ``exchange="p2p"`` needs no collective at all: every rank maps the other ranks' receive and
   partial buffers (CUDA IPC), the pack kernel stores the token rows straight into the owners'
   receive buffers over NVLink, a flag barrier kernel (bounded wait) publishes them, the owners
-  compute, a second barrier, and the home's combine kernel loads the partial rows from the
-  owners' memory.
+  compute and (``results="push"``, the default) their combine kernel stores each result row
+  straight into its home's partial buffer, a second barrier, and the home adds its partial rows
+  from its own memory; with ``results="pull"`` the owners keep their results and the home's
+  combine kernel loads them from the owners' memory.
 * ``"replicated"`` (decode; every rank holds the same tokens).  Each rank routes all tokens,
   runs its own experts on them (rank 0 adds the shared expert) and an all-reduce sums the
   partial outputs.
@@ -83,6 +85,7 @@ class PeerBuffers:
     def __init__(self, G, rank, B, H, K, device, x_half=True):
         import torch
         self.L, self.G, self.rank, self.device = lib(), G, rank, device
+        self.B, self.H = B, H
         self.x_half = bool(x_half) and H % 8 == 0
         xb = 2 if self.x_half else 4
         sizes = {"x": G * B * H * xb, "meta": G * B * 2 * K * 4, "partial": G * B * H * 4, "ctl": self.CTL}
@@ -106,6 +109,9 @@ class PeerBuffers:
             return torch.tensor([ptrs[r][name] + off for r in range(self.G)], dtype=torch.int64, device=self.device)
         self.dst_x, self.dst_meta = arr("x"), arr("meta")
         self.src_partial, self.peer_flags = arr("partial"), arr("ctl")
+        # where this rank, as an owner, stores the results of the rows home h sent: row block
+        # `rank` of h's partial buffer
+        self.dst_partial = arr("partial", self.rank * self.B * self.H * 4)
 
     def open_peers(self, all_handles):
         """Map the other ranks' buffers from their handles (one process per GPU)."""
@@ -193,6 +199,14 @@ class DeviceOps:
         rows are {K ids, K weight bits} in meta [R, 2K]."""
         self._experts(x, R, meta.data_ptr(), meta.data_ptr() + 4 * K, 2 * K, False, out)
 
+    def experts_to_homes(self, R, K, block, pb: "PeerBuffers"):
+        """The received rows' results stored straight into the homes' partial buffers."""
+        x16 = 1 if pb.x_half else 0
+        _check(self.L.draco_b200_experts_forward_to_ranks(ct.byref(self.local), pb.x.data_ptr(), R, pb.meta.data_ptr(),
+                                                          pb.meta.data_ptr() + 4 * K, 2 * K, self.first,
+                                                          pb.dst_partial.data_ptr(), block, x16, self._s()),
+               "draco_b200_experts_forward_to_ranks")
+
     def combine(self, back, row_of, T, G, H, sh, out):
         _check(self.L.draco_b200_ep_combine(back.data_ptr(), row_of.data_ptr(), T, G, H,
                                             sh.data_ptr() if sh is not None else None, out.data_ptr(), self._s()),
@@ -245,9 +259,10 @@ class ExpertParallelMoE:
     ranks must agree on it for the fixed exchange)."""
 
     def __init__(self, layer, max_tokens: int, comm=None, ops=None, layout: str = "a2a",
-                 exchange: str = "fixed", device=None):
-        if layout not in LAYOUTS or exchange not in EXCHANGES:
-            raise ValueError(f"layout in {LAYOUTS}, exchange in {EXCHANGES}")
+                 exchange: str = "fixed", device=None, results: str = "push"):
+        if layout not in LAYOUTS or exchange not in EXCHANGES or results not in ("push", "pull"):
+            raise ValueError(f"layout in {LAYOUTS}, exchange in {EXCHANGES}, results in ('push', 'pull')")
+        self.results = results
         self.comm = comm if comm is not None else TorchGroup()
         self.G, self.rank = self.comm.world, self.comm.rank
         if layer.n_exp % self.G:
@@ -351,6 +366,11 @@ class ExpertParallelMoE:
             o.shared(x, T, sh)
         o.push(x, b["order"], b["wtop"], b["counts"], G, self.rank, b["src_tok"], B, K, H, pb)
         o.barrier(G, self.rank, pb)                 # every rank's rows have landed
+        if self.results == "push":
+            o.experts_to_homes(G * B, K, B, pb)     # results stored into the homes' partial rows
+            o.barrier(G, self.rank, pb)             # every owner's results have landed
+            o.combine(pb.partial, b["row_of"], T, G, H, sh, out)
+            return out
         o.experts_meta(pb.x, G * B, pb.meta, K, pb.partial)
         o.barrier(G, self.rank, pb)                 # every owner's partial rows are final
         o.pull_combine(b["row_of"], T, G, self.rank, B, H, sh, out, pb)
@@ -425,11 +445,17 @@ def emulate_p2p(ranks: list, xs: list) -> list:
         o.push(x, b["order"], b["wtop"], b["counts"], G, r.rank, b["src_tok"], r.B, r.K, r.H, r.peer)
         sts.append((T, sh))
     for r in ranks:
-        r.ops.experts_meta(r.peer.x, G * r.B, r.peer.meta, r.K, r.peer.partial)
+        if r.results == "push":
+            r.ops.experts_to_homes(G * r.B, r.K, r.B, r.peer)
+        else:
+            r.ops.experts_meta(r.peer.x, G * r.B, r.peer.meta, r.K, r.peer.partial)
     outs = []
     for r, (T, sh) in zip(ranks, sts):
         out = r._bufs["out"][:T]
-        r.ops.pull_combine(r._bufs["row_of"], T, G, r.rank, r.B, r.H, sh, out, r.peer)
+        if r.results == "push":
+            r.ops.combine(r.peer.partial, r._bufs["row_of"], T, G, r.H, sh, out)
+        else:
+            r.ops.pull_combine(r._bufs["row_of"], T, G, r.rank, r.B, r.H, sh, out, r.peer)
         outs.append(out)
     return outs
 

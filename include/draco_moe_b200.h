@@ -203,6 +203,20 @@ int draco_b200_experts_forward(const DracoMoeLayer* L, const void* X, int T, con
                                const float* wtop, int ld, int first_expert, float* out,
                                int with_shared, int x_fp16, void* stream);
 
+/* The routed part of draco_b200_experts_forward for an expert-parallel owner whose results go
+ * straight to the ranks that sent the rows: row q of the result (the weighted sum, k ascending,
+ * of row q's experts in [first_expert, first_expert + n_exp)) is stored to
+ * out_blocks[q / block] + (q % block) * n_out, out_blocks being a device array of row-block
+ * addresses (other GPUs' buffers mapped into this process, or this GPU's own).  Rows without an
+ * expert in the slice are not written.  The stores are fenced at system scope before the call's
+ * last kernel ends, so a flag barrier enqueued after it publishes them.  Device pointers only
+ * (asynchronous on stream when given); needs n_out % 4 == 0 and n_used <= 64; no shared expert.  Replaces nothing in the
+ * reference (single-process there); per rank it is src/m6_moe_tok.c:44-161 on the rank's slice. */
+int draco_b200_experts_forward_to_ranks(const DracoMoeLayer* L, const void* X, int T,
+                                        const int* order, const float* wtop, int ld,
+                                        int first_expert, float* const* out_blocks, int block,
+                                        int x_fp16, void* stream);
+
 /* Expert-parallel token exchange over n_ranks ranks that split n_exp experts contiguously
  * (rank r owns [r*n_exp/n_ranks, (r+1)*n_exp/n_ranks)).  Device pointers, 16-byte aligned,
  * asynchronous on stream.

@@ -196,23 +196,27 @@ def test_ep_emulated_on_one_gpu(port, name, G, exchange, T):
 @pytest.mark.parametrize("name", list(LAYERS))
 @pytest.mark.parametrize("G,T", [(2, 40), (4, 150), (8, 96), (4, 0)])
 def test_ep_p2p_emulated_matches_fixed_exchange(port, name, G, T):
-    """Peer-memory dispatch/combine (push and pull kernels) on G ranks sharing one GPU: the same
-    rows reach the owners as with the fixed-block all-to-all, so the outputs are identical.
-    T = 0: every other rank has no tokens."""
+    """Peer-memory dispatch/combine on G ranks sharing one GPU, with the owners storing their
+    results into the homes' buffers (push) or the homes loading them (pull): the same rows reach
+    the owners as with the fixed-block all-to-all, so the outputs are identical.  T = 0: every
+    other rank has no tokens."""
     layer = synth.make_layer(**LAYERS[name])
     Ts = [T - (i % 3) for i in range(G)] if T else [(23 if i % 2 else 0) for i in range(G)]
     xs = [torch.from_numpy(synth.make_tokens(layer, t, 400 + i, False)).cuda() for i, t in enumerate(Ts)]
     dev = torch.device("cuda")
     res = {}
-    for exchange in ("fixed", "p2p"):
+    for exchange, results in (("fixed", "push"), ("p2p", "push"), ("p2p", "pull")):
         ranks = [ExpertParallelMoE(layer, max(Ts), comm=types.SimpleNamespace(world=G, rank=r),
-                                   ops=DeviceOps(layer, r, G, dev), exchange=exchange) for r in range(G)]
+                                   ops=DeviceOps(layer, r, G, dev), exchange=exchange, results=results)
+                 for r in range(G)]
         outs = emulate(ranks, xs)
         torch.cuda.synchronize()
-        res[exchange] = np.concatenate([o.cpu().numpy() for o in outs])
+        res[exchange if exchange == "fixed" else results] = np.concatenate([o.cpu().numpy() for o in outs])
         for r in ranks:
             r.close()
-    assert np.array_equal(res["p2p"].view(np.uint32), res["fixed"].view(np.uint32))
+    assert np.array_equal(res["push"].view(np.uint32), res["fixed"].view(np.uint32))
+    assert np.array_equal(res["pull"].view(np.uint32), res["fixed"].view(np.uint32))
+    res["p2p"] = res["push"]
     X = np.concatenate([x.cpu().numpy() for x in xs])
     assert rel(res["p2p"], port.layer_forward(layer, X)) < REL_L2_TOL
 
@@ -296,8 +300,9 @@ def _nccl_worker(rank, world, port_no, name, out_dir):
         res = {}
         stream = torch.cuda.Stream(dev)
         with torch.cuda.stream(stream):
-            for exchange in ("fixed", "compact", "p2p"):
-                ep = ExpertParallelMoE(layer, max(Ts), exchange=exchange, device=dev)
+            for exchange in ("fixed", "compact", "p2p", "p2p_pull"):
+                ep = ExpertParallelMoE(layer, max(Ts), exchange=exchange.split("_")[0], device=dev,
+                                       results="pull" if exchange.endswith("pull") else "push")
                 x = torch.from_numpy(xs[rank]).to(dev)
                 res[exchange] = ep.forward(x).cpu().numpy()
                 res[exchange + "_again"] = ep.forward(x).cpu().numpy()
@@ -325,7 +330,7 @@ def test_ep_nccl(port, tmp_path, name):
     X = np.concatenate(xs)
     ref = port.layer_forward(layer, X)
     r = [np.load(os.path.join(tmp_path, f"rank{i}.npz")) for i in range(world)]
-    for exchange in ("fixed", "compact", "p2p"):
+    for exchange in ("fixed", "compact", "p2p", "p2p_pull"):
         got = np.concatenate([r[i][exchange] for i in range(world)])
         assert rel(got, ref) < REL_L2_TOL, exchange
         again = np.concatenate([r[i][exchange + "_again"] for i in range(world)])
@@ -333,5 +338,6 @@ def test_ep_nccl(port, tmp_path, name):
     for i in range(world):
         assert np.array_equal(r[i]["fixed"], r[i]["compact"])
         assert np.array_equal(r[i]["fixed"], r[i]["p2p"])
+        assert np.array_equal(r[i]["fixed"], r[i]["p2p_pull"])
         assert np.array_equal(r[i]["replicated"], r[0]["replicated"])
     assert rel(r[0]["replicated"], ref) < REL_L2_TOL
