@@ -305,122 +305,13 @@ int tile_rows(int rows, uint32_t row_bytes_) {
     return rows % rt ? 0 : rt;
 }
 
-// ------------------------------------------------------------------------------------------
-// Lane-direct superblock decode: the words one lane needs of one superblock loaded straight from
-// global memory (no staging, no scale table), decoded to the same 8 values as decode8 with the
-// same arithmetic (superblock_scales' expressions), so sums match the staged kernels bit for bit.
-// Q4_K: header (16 B, the same for all lanes) + the lane's qs word; Q6_K (224-byte layout): the
-// lane's ql and qh words + the 16 scales and d (the same for all lanes).
-// ------------------------------------------------------------------------------------------
-template <int CODE>
-struct LaneSB;
-template <>
-struct LaneSB<DRACO_CODE_Q4_K> {
-    uint4 hd;
-    uint32_t qs;
-};
-template <>
-struct LaneSB<DRACO_CODE_Q6_K> {
-    uint32_t ql, qh;
-    uint4 sc;
-    uint32_t d;
-};
-
-template <int CODE>
-__device__ __forceinline__ LaneSB<CODE> lane_load(const uint8_t* __restrict__ blk, int lane) {
-    LaneSB<CODE> r;
-    if constexpr (CODE == DRACO_CODE_Q4_K) {
-        r.hd = __ldg(reinterpret_cast<const uint4*>(blk));
-        r.qs = __ldg(reinterpret_cast<const uint32_t*>(blk + 16 + 4 * lane));
-    } else {
-        const int h = lane >> 4, i = lane & 15;
-        r.ql = __ldg(reinterpret_cast<const uint32_t*>(blk + 64 * h + 4 * i));
-        r.qh = __ldg(reinterpret_cast<const uint32_t*>(blk + 128 + 32 * h + 4 * (i & 7)));
-        r.sc = __ldg(reinterpret_cast<const uint4*>(blk + 192));
-        r.d = __ldg(reinterpret_cast<const uint32_t*>(blk + 208));
-    }
-    return r;
-}
-__device__ __forceinline__ int byte_of(const uint4& v, int idx) {   // signed byte idx (0..15)
-    const uint32_t w = (idx >> 2) == 0 ? v.x : (idx >> 2) == 1 ? v.y : (idx >> 2) == 2 ? v.z : v.w;
-    return (int)(int8_t)(w >> (8 * (idx & 3)));
-}
-
-template <int CODE>
-__device__ __forceinline__ void lane_decode(const LaneSB<CODE>& s, int lane, float w[8]) {
-    if constexpr (CODE == DRACO_CODE_Q4_K) {
-        const float d = h2f((uint16_t)(s.hd.x & 0xffff)), dmin = h2f((uint16_t)(s.hd.x >> 16));
-        const int g = lane >> 3;
-        int sc0, m0, sc1, m1;
-        q4k_scale_min(s.hd.y, s.hd.z, s.hd.w, 2 * g, sc0, m0);
-        q4k_scale_min(s.hd.y, s.hd.z, s.hd.w, 2 * g + 1, sc1, m1);
-        const float ds0 = d * (float)sc0, dm0 = dmin * (float)m0;
-        const float ds1 = d * (float)sc1, dm1 = dmin * (float)m1;
-        const float2 t0 = make_float2(64.f * ds0, -(128.f * ds0 + dm0));
-        const float2 t1 = make_float2(64.f * ds1, -(128.f * ds1 + dm1));
-        const uint32_t lo = s.qs & 0x0F0F0F0Fu, hi = (s.qs >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            w[k] = fmaf(code_float(lo, k), t0.x, t0.y);
-            w[4 + k] = fmaf(code_float(hi, k), t1.x, t1.y);
-        }
-    } else {
-        const int h = lane >> 4, i = lane & 15;
-        const float d = h2f((uint16_t)(s.d & 0xffff));
-        const float dsl = d * (float)byte_of(s.sc, 8 * h + (i >> 2));
-        const float dsh = d * (float)byte_of(s.sc, 8 * h + 4 + (i >> 2));
-        const float2 sl = make_float2(64.f * dsl, -160.f * dsl), sh = make_float2(64.f * dsh, -160.f * dsh);
-        const int s0 = 2 * (i >> 3);
-        const uint32_t q_lo = (s.ql & 0x0F0F0F0Fu) | (((s.qh >> s0) & 0x03030303u) << 4);
-        const uint32_t q_hi = ((s.ql >> 4) & 0x0F0F0F0Fu) | (((s.qh >> (s0 + 4)) & 0x03030303u) << 4);
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            w[k] = fmaf(code_float(q_lo, k), sl.x, sl.y);
-            w[4 + k] = fmaf(code_float(q_hi, k), sh.x, sh.y);
-        }
-    }
-}
-
-// dot products of one weight row (nb superblocks of bb bytes, global memory) with nt <= 2 token
-// rows x (shared or global memory): lane partials in superblock order, then the warp sum (the
-// order of rows_dot); loads run four superblocks ahead
-template <int CODE, int NT>
-__device__ __forceinline__ void row_dot_direct(const uint8_t* __restrict__ row, int nb, int bb,
-                                               const float* const (&xr)[2], int lane, float (&acc)[2]) {
-#pragma unroll
-    for (int j = 0; j < 2; j++) acc[j] = 0.f;
-    constexpr int kAhead = 4;
-    LaneSB<CODE> buf[kAhead];
-#pragma unroll
-    for (int u = 0; u < kAhead; u++)
-        if (u < nb) buf[u] = lane_load<CODE>(row + (size_t)u * bb, lane);
-    for (int sb0 = 0; sb0 < nb; sb0 += kAhead) {
-#pragma unroll
-        for (int u = 0; u < kAhead; u++) {
-            const int sb = sb0 + u;
-            if (sb < nb) {
-                float w[8];
-                lane_decode<CODE>(buf[u], lane, w);
-                if (sb + kAhead < nb) buf[u] = lane_load<CODE>(row + (size_t)(sb + kAhead) * bb, lane);
-#pragma unroll
-                for (int j = 0; j < NT; j++) {
-                    float xv[8];
-                    load_x8<CODE>(xr[j], sb, lane, xv);
-#pragma unroll
-                    for (int k = 0; k < 8; k++) acc[j] = fmaf(w[k], xv[k], acc[j]);
-                }
-            }
-        }
-    }
-}
-
 // One staged weight row (nb superblocks of bb bytes, shared memory) with nt <= 2 token rows, the
 // superblock scales computed cooperatively: for a group of superblocks (4 of Q4_K, 2 of Q6_K)
 // every lane works out ONE (64 d sc, offset) pair -- lane L: Q4_K superblock L / 8, sub-block
 // L % 8; Q6_K superblock L / 16, scale L % 16 -- and the lanes that decode with it fetch it by
 // shuffle, instead of each lane unpacking its own scales for every superblock.  The pairs, the
-// decoded weights and the sums are those of lane_decode / decode8 (same expressions, same
-// order), so the results equal the other decode paths bit for bit.
+// decoded weights and the sums are those of decode8 (same expressions, same order), so the
+// results equal the other decode paths bit for bit.
 template <int CODE>
 __device__ __forceinline__ float2 coop_scale(const uint8_t* row, int nb, int bb, int sb0, int lane) {
     if constexpr (CODE == DRACO_CODE_Q4_K) {
